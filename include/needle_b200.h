@@ -1,0 +1,129 @@
+/*
+ * needle_b200.h — B200 extensions of the needle C ABI.
+ *
+ * The reference exposes only text-level calls (needle.h); its engine API
+ * also has NeedleEngine::run_batch (crates/needle-infer/src/engine.rs:142-144)
+ * and its tests drive NeedleModel::encode / decode_step directly
+ * (crates/needle-core/tests/parity_tests.rs:345-594).  These entry points
+ * expose the same paths on token IDs, batched and sharded for the GPU, plus
+ * the INT4 kernels of crates/needle-core/src/quant.rs on device pointers.
+ *
+ * Return convention: int results are 0 (or a count) on success and -1 on
+ * failure with needle_last_error() set.  All pointers are host pointers
+ * unless NEEDLE_DEVICE_POINTERS is passed (batched calls) or the function
+ * says "device".
+ */
+#ifndef NEEDLE_B200_H
+#define NEEDLE_B200_H
+
+#include "needle.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ── devices ─────────────────────────────────────────────────────────────── */
+
+/* Number of visible CUDA devices (0 when none; never fails). */
+int needle_device_count(void);
+
+/* needle_load / needle_load_bytes onto an explicit device. */
+NeedleHandle *needle_load_on_device(const char *weights_path, const char *vocab_path, int device);
+NeedleHandle *needle_load_bytes_on_device(const uint8_t *weights_data, size_t weights_len,
+                                          const uint8_t *vocab_data, size_t vocab_len, int device);
+
+/* cfg[0..11] = d_model, num_heads, num_kv_heads, num_encoder_layers,
+ * num_decoder_layers, vocab_size, max_enc_len, max_dec_len, ffn_dim,
+ * no_feedforward, activation (0 drelu, 1 swiglu, 2 geglu), head_dim
+ * (crates/needle-core/src/config.rs:22-69). */
+int needle_model_config(NeedleHandle *handle, int64_t *cfg);
+int needle_handle_device(NeedleHandle *handle);
+
+/* ── batched generation on token IDs ─────────────────────────────────────── */
+
+#define NEEDLE_STOP_ON_EOS 1u     /* end a request at EOS, as run_impl does (engine.rs:306-308) */
+#define NEEDLE_DEVICE_POINTERS 2u /* prompt_ids / mask_bits / outputs are device pointers */
+#define NEEDLE_NO_GRAPH 4u        /* launch decode steps one kernel at a time (no CUDA graph) */
+
+/* Greedy generation for n_req independent requests (run_batch,
+ * engine.rs:142-144, with the decode loop of engine.rs:286-322 on IDs):
+ *   prompt_ids      concatenated encoder inputs (each 1..max_enc_len ids < vocab)
+ *   prompt_offsets  host array [n_req + 1]: request r = ids[off[r] .. off[r+1])
+ *   max_new         decode steps, <= max_dec_len; decoding starts from EOS (1)
+ *   mask_bits       NULL (unconstrained) or [n_req][max_new][ceil(V/64)] u64:
+ *                   bit v of a step's row set = token v allowed (additive 0),
+ *                   clear = additive -1e9 (constrained.rs:369-387)
+ *   out_ids         [n_req][max_new] generated ids (EOS excluded when stopping)
+ *   out_lens        [n_req] tokens generated per request
+ * Ties pick the last maximal index (Iterator::max_by(total_cmp)). */
+int needle_run_batch_ids(NeedleHandle *handle, const uint32_t *prompt_ids, const uint64_t *prompt_offsets,
+                         size_t n_req, uint32_t max_new, const uint64_t *mask_bits, uint32_t flags,
+                         uint32_t *out_ids, uint32_t *out_lens);
+
+/* Prepared batch: needle_batch_prepare uploads the inputs and allocates the
+ * per-call device state once; needle_batch_run enqueues prefill + decode on
+ * the batch's own stream without host copies (re-running restarts from the
+ * prompts); needle_batch_sync waits; needle_batch_results copies out. */
+typedef struct NeedleBatch NeedleBatch;
+NeedleBatch *needle_batch_prepare(NeedleHandle *handle, const uint32_t *prompt_ids, const uint64_t *prompt_offsets,
+                                  size_t n_req, uint32_t max_new, const uint64_t *mask_bits, uint32_t flags);
+int needle_batch_run(NeedleBatch *batch);
+int needle_batch_sync(NeedleBatch *batch);
+int needle_batch_results(NeedleBatch *batch, uint32_t *out_ids, uint32_t *out_lens);
+/* The cudaStream_t the batch runs on (as void *), for the caller's events. */
+void *needle_batch_stream(NeedleBatch *batch);
+/* Kernels the last needle_batch_run launched. */
+int64_t needle_batch_kernel_launches(NeedleBatch *batch);
+/* Record CUDA events around every decoder cross-attention launch of later
+ * runs (eager launches); needle_batch_cross_attention_ms reports the summed
+ * device time and the launch count of the last run. */
+int needle_batch_time_cross_attention(NeedleBatch *batch, int enable);
+int needle_batch_cross_attention_ms(NeedleBatch *batch, double *ms_total, int64_t *launches);
+void needle_batch_free(NeedleBatch *batch);
+
+/* Splits requests into `shards` groups of near-equal cost, longest first
+ * (one group per GPU; no collective is needed).  assignment: [n_req]. */
+int needle_shard_requests(const uint64_t *prompt_offsets, size_t n_req, int shards, int32_t *assignment);
+
+/* ── parity entry points ─────────────────────────────────────────────────── */
+
+/* encode (model.rs:153-192) then one decode_step (model.rs:235-265) per
+ * dec_ids[i], teacher-forced.  enc_out: NULL or [n_enc][d_model] final
+ * encoder hidden; logits: NULL or [n_dec][V]. */
+int needle_debug_forward(NeedleHandle *handle, const uint32_t *enc_ids, size_t n_enc, const uint32_t *dec_ids,
+                         size_t n_dec, float *enc_out, float *logits);
+
+/* Batched greedy generation that also returns the masked logits of every
+ * step: logits [n_req][max_new][V].  Otherwise as needle_run_batch_ids. */
+int needle_run_batch_ids_logits(NeedleHandle *handle, const uint32_t *prompt_ids, const uint64_t *prompt_offsets,
+                                size_t n_req, uint32_t max_new, const uint64_t *mask_bits, uint32_t flags,
+                                uint32_t *out_ids, uint32_t *out_lens, float *logits);
+
+/* ── INT4 kernels on device pointers (reference layout, quant.rs:45-58) ──── */
+/* w_data: [(G*gs/2)][N] bytes, low nibble = row 2p, high = row 2p+1;
+ * w_scales: [G][N] f32, gs = min(32, K).  stream: cudaStream_t or NULL. */
+
+/* y[M][N] = x[M][K] @ W  (QuantizedWeight::matmul, quant.rs:400-410). */
+int needle_int4_matmul(const float *x, size_t M, size_t K, const uint8_t *w_data, const float *w_scales, size_t N,
+                       size_t num_groups, float *y, void *stream);
+/* Pack w[K][N] f32 (QuantizedWeight::quantize, quant.rs:63-128), bit-exact:
+ * data [(Kp/2)][N], scales [Kp/gs][N] with Kp = K padded to gs. */
+int needle_int4_quantize(const float *w, size_t K, size_t N, uint8_t *data, float *scales, void *stream);
+/* Unpack to out[K][N] f32 (quant.rs:131-155), bit-exact. */
+int needle_int4_dequantize(const uint8_t *data, const float *scales, size_t K, size_t N, size_t num_groups,
+                           float *out, void *stream);
+/* Gated MLP over T tokens (ffn_forward, crates/needle-core/src/ffn.rs:19-56):
+ * out[T][d] = down(act(x @ gate) * (x @ up)); act 0 drelu, 1 swiglu,
+ * 2 geglu.  Gate and up are fused into one pass whose epilogue applies the
+ * activation; the [T][d_ff] hidden lives in a device buffer allocated per
+ * call. */
+int needle_ffn_forward(const float *x, size_t T, size_t d_model, size_t d_ff, const uint8_t *gate_data,
+                       const float *gate_scales, const uint8_t *up_data, const float *up_scales,
+                       const uint8_t *down_data, const float *down_scales, int activation, float *out,
+                       void *stream);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* NEEDLE_B200_H */

@@ -1,0 +1,631 @@
+// attention.cu — norms, embedding, RoPE and the three attention variants.
+//
+// Reference: crates/needle-core/src/{attn.rs,norm.rs,rope.rs,ops.rs,model.rs}.
+// All arithmetic is f32; expf/sqrtf/division are the IEEE-accurate device
+// versions (no fast-math), so results differ from the reference only by
+// summation order.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace ndl {
+namespace {
+
+// ── ZCRMSNorm rows (norm.rs:23-30) ─────────────────────────────────────────
+__global__ void rms_norm_kernel(const float *__restrict__ x, int64_t ldx, float *out, int64_t ldo,
+                                const float *__restrict__ scale, int rows, int d) {
+  int row = (int)(((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float *xr = x + (int64_t)row * ldx;
+  float *orow = out + (int64_t)row * ldo;
+  if (d == 512) {
+    float v[16];
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float4 t = *reinterpret_cast<const float4 *>(xr + i * 128 + lane * 4);
+      v[i * 4 + 0] = t.x;
+      v[i * 4 + 1] = t.y;
+      v[i * 4 + 2] = t.z;
+      v[i * 4 + 3] = t.w;
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) ss += v[i] * v[i];
+    ss = warp_sum(ss);
+    float inv = 1.0f / sqrtf(ss / 512.0f + 1e-6f);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float4 s = __ldg(reinterpret_cast<const float4 *>(scale + i * 128 + lane * 4));
+      float4 r;
+      r.x = ((1.0f + s.x) * v[i * 4 + 0]) * inv;
+      r.y = ((1.0f + s.y) * v[i * 4 + 1]) * inv;
+      r.z = ((1.0f + s.z) * v[i * 4 + 2]) * inv;
+      r.w = ((1.0f + s.w) * v[i * 4 + 3]) * inv;
+      *reinterpret_cast<float4 *>(orow + i * 128 + lane * 4) = r;
+    }
+    return;
+  }
+  float ss = 0.0f;
+  for (int i = lane; i < d; i += 32) ss += xr[i] * xr[i];
+  ss = warp_sum(ss);
+  float inv = 1.0f / sqrtf(ss / (float)d + 1e-6f);
+  for (int i = lane; i < d; i += 32) orow[i] = ((1.0f + __ldg(scale + i)) * xr[i]) * inv;
+}
+
+__global__ void embed_kernel(const uint32_t *__restrict__ ids, const float *__restrict__ emb, float *x, int rows,
+                             int d, float es) {
+  int row = (int)(((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float *e = emb + (int64_t)ids[row] * d;
+  float *xr = x + (int64_t)row * d;
+  for (int i = lane; i < d; i += 32) xr[i] = e[i] * es;
+}
+
+// Per-head ZCRMSNorm then split-half RoPE for one head of HD values held as
+// pairs (i, i + HD/2) by lane i (HD <= 128: two pairs per lane).
+__device__ __forceinline__ void norm_rope_head(float *v, int HD, const float *__restrict__ nscale,
+                                               const float *__restrict__ cr, const float *__restrict__ sr,
+                                               bool rope, int lane) {
+  const int half = HD >> 1;
+  float a[2], b[2];
+  float ss = 0.0f;
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    int i = lane + 32 * u;
+    a[u] = i < half ? v[i] : 0.0f;
+    b[u] = i < half ? v[i + half] : 0.0f;
+    ss += a[u] * a[u] + b[u] * b[u];
+  }
+  ss = warp_sum(ss);
+  float inv = 1.0f / sqrtf(ss / (float)HD + 1e-6f);
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    int i = lane + 32 * u;
+    if (i < half) {
+      float x0 = ((1.0f + __ldg(nscale + i)) * a[u]) * inv;
+      float x1 = ((1.0f + __ldg(nscale + i + half)) * b[u]) * inv;
+      if (rope) {  // rope.rs:63-75
+        float c = __ldg(cr + i), s = __ldg(sr + i);
+        float l = x0 * c - x1 * s;
+        float r = x1 * c + x0 * s;
+        x0 = l;
+        x1 = r;
+      }
+      v[i] = x0;
+      v[i + half] = x1;
+    }
+  }
+}
+
+// One warp per (row, Q-or-K head).
+__global__ void qk_norm_rope_kernel(float *qkv, int rows, const int32_t *__restrict__ pos,
+                                    const float *__restrict__ qn, const float *__restrict__ kn,
+                                    const float *__restrict__ rc, const float *__restrict__ rs, AttnDims a) {
+  int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  int lane = threadIdx.x & 31;
+  int heads = a.H + a.KVH;
+  if (w >= (int64_t)rows * heads) return;
+  int row = (int)(w / heads), h = (int)(w % heads);
+  int ld = (a.H + 2 * a.KVH) * a.HD;
+  float *v = qkv + (int64_t)row * ld + h * a.HD;
+  int p = pos[row], half = a.HD >> 1;
+  norm_rope_head(v, a.HD, h < a.H ? qn : kn, rc + (int64_t)p * half, rs + (int64_t)p * half, true, lane);
+}
+
+// One warp per (row, head): per-head ZCRMSNorm without RoPE.
+__global__ void head_norm_kernel(float *x, int rows, int64_t ld, int heads, int HD, const float *__restrict__ sc) {
+  int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (w >= (int64_t)rows * heads) return;
+  int row = (int)(w / heads), h = (int)(w % heads);
+  norm_rope_head(x + (int64_t)row * ld + h * HD, HD, sc, nullptr, nullptr, false, threadIdx.x & 31);
+}
+
+// ── encoder attention (attn.rs:189-273), flash-style online softmax ────────
+// CTA = (64 query rows, one Q head, one request); K/V tiles of 64 keys.
+constexpr int EQ = 64, EK = 64, EP = 68;  // padded row stride
+
+__global__ void __launch_bounds__(256) encoder_attn_kernel(const float *__restrict__ qkv,
+                                                           const int64_t *__restrict__ seq_off, float *out,
+                                                           AttnDims a) {
+  extern __shared__ __align__(16) float sm[];
+  float *Qs = sm;               // [HD][EP]   Qs[d][r]
+  float *Ks = Qs + 64 * EP;     // [HD][EP]   Ks[d][k]
+  float *Vs = Ks + 64 * EP;     // [EK][EP]   Vs[k][d]
+  float *Ps = Vs + EK * EP;     // [EK][EP]   Ps[k][r]
+  const int r_req = blockIdx.z, h = blockIdx.y, q0 = blockIdx.x * EQ;
+  const int64_t off = seq_off[r_req];
+  const int T = (int)(seq_off[r_req + 1] - off);
+  if (q0 >= T) return;
+  const int HD = a.HD, g = h / (a.H / a.KVH);
+  const int ld = (a.H + 2 * a.KVH) * HD;
+  const int tid = threadIdx.x, tr = tid >> 4, tc = tid & 15;
+  const float scale = a.scale;
+  const int hd4 = HD >> 2;
+
+  // Q tile -> Qs (transposed)
+  for (int i = tid; i < EQ * hd4; i += 256) {
+    int r = i / hd4, d4 = i - r * hd4;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (q0 + r < T) v = *reinterpret_cast<const float4 *>(qkv + (off + q0 + r) * ld + h * HD + d4 * 4);
+    Qs[(d4 * 4 + 0) * EP + r] = v.x;
+    Qs[(d4 * 4 + 1) * EP + r] = v.y;
+    Qs[(d4 * 4 + 2) * EP + r] = v.z;
+    Qs[(d4 * 4 + 3) * EP + r] = v.w;
+  }
+
+  float o[4][4];
+  float mrow[4], lrow[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    mrow[i] = -INFINITY;
+    lrow[i] = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o[i][j] = 0.0f;
+  }
+
+  for (int k0 = 0; k0 < T; k0 += EK) {
+    __syncthreads();
+    for (int i = tid; i < EK * hd4; i += 256) {
+      int k = i / hd4, d4 = i - k * hd4;
+      float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+      if (k0 + k < T) {
+        const float *row = qkv + (off + k0 + k) * ld;
+        kv = *reinterpret_cast<const float4 *>(row + (a.H + g) * HD + d4 * 4);
+        vv = *reinterpret_cast<const float4 *>(row + (a.H + a.KVH + g) * HD + d4 * 4);
+      }
+      Ks[(d4 * 4 + 0) * EP + k] = kv.x;
+      Ks[(d4 * 4 + 1) * EP + k] = kv.y;
+      Ks[(d4 * 4 + 2) * EP + k] = kv.z;
+      Ks[(d4 * 4 + 3) * EP + k] = kv.w;
+      *reinterpret_cast<float4 *>(Vs + k * EP + d4 * 4) = vv;
+    }
+    __syncthreads();
+    // S = Q K^T for rows tr*4.., keys tc*4..
+    float s[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) s[i][j] = 0.0f;
+    for (int d = 0; d < HD; ++d) {
+      float4 q = *reinterpret_cast<const float4 *>(Qs + d * EP + tr * 4);
+      float4 k = *reinterpret_cast<const float4 *>(Ks + d * EP + tc * 4);
+      float qa[4] = {q.x, q.y, q.z, q.w}, ka[4] = {k.x, k.y, k.z, k.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) s[i][j] = fmaf(qa[i], ka[j], s[i][j]);
+    }
+    // online softmax per row; a row's 64 keys live in the 16 lanes sharing tr
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float mx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        s[i][j] = (k0 + tc * 4 + j < T) ? s[i][j] * scale : -INFINITY;
+        mx = fmaxf(mx, s[i][j]);
+      }
+#pragma unroll
+      for (int o2 = 8; o2 > 0; o2 >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o2));
+      float mnew = fmaxf(mrow[i], mx);
+      float corr = expf(mrow[i] - mnew);  // exp(-inf) = 0 on the first tile
+      float ps = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float p = expf(s[i][j] - mnew);
+        s[i][j] = p;
+        ps += p;
+      }
+#pragma unroll
+      for (int o2 = 8; o2 > 0; o2 >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o2);
+      lrow[i] = lrow[i] * corr + ps;
+      mrow[i] = mnew;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) o[i][j] *= corr;
+    }
+    // P -> smem (transposed: Ps[k][r])
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      *reinterpret_cast<float4 *>(Ps + (tc * 4 + j) * EP + tr * 4) = make_float4(s[0][j], s[1][j], s[2][j], s[3][j]);
+    __syncthreads();
+    // O += P V   rows tr*4.., dims tc*4..
+    if (tc * 4 < HD) {
+      const int kmax = min(EK, T - k0);
+      for (int k = 0; k < kmax; ++k) {
+        float4 p = *reinterpret_cast<const float4 *>(Ps + k * EP + tr * 4);
+        float4 v = *reinterpret_cast<const float4 *>(Vs + k * EP + tc * 4);
+        float pa[4] = {p.x, p.y, p.z, p.w}, va[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) o[i][j] = fmaf(pa[i], va[j], o[i][j]);
+      }
+    }
+  }
+  if (tc * 4 < HD) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      int r = q0 + tr * 4 + i;
+      if (r < T) {
+        float inv = 1.0f / lrow[i];
+        float4 v = make_float4(o[i][0] * inv, o[i][1] * inv, o[i][2] * inv, o[i][3] * inv);
+        *reinterpret_cast<float4 *>(out + (off + r) * (int64_t)(a.H * HD) + h * HD + tc * 4) = v;
+      }
+    }
+  }
+}
+
+// ── decoder self-attention, one new token per request (attn.rs:100-183) ───
+// CTA = one request.  Warp w handles heads w, w+8, ...
+__global__ void __launch_bounds__(256) dec_self_attn_kernel(const float *__restrict__ qkv,
+                                                            const int32_t *__restrict__ step,
+                                                            const float *__restrict__ qn,
+                                                            const float *__restrict__ kn,
+                                                            const float *__restrict__ rc,
+                                                            const float *__restrict__ rs, float *kc, float *vc,
+                                                            int cap, float *out, AttnDims a) {
+  extern __shared__ __align__(16) float sm[];
+  const int b = blockIdx.x, HD = a.HD, half = HD >> 1;
+  const int qd = a.H * HD, kvd = a.KVH * HD, ld = qd + 2 * kvd;
+  float *qs = sm;                 // [H*HD]
+  float *sc = sm + qd;            // [H][cap]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int pos = step[b];
+  const float *row = qkv + (int64_t)b * ld;
+  float *kcb = kc + (int64_t)b * cap * kvd;
+  float *vcb = vc + (int64_t)b * cap * kvd;
+  const float *cr = rc + (int64_t)pos * half, *sr = rs + (int64_t)pos * half;
+  const bool append = pos < cap;  // push_kv saturates silently (attn.rs:53-61)
+
+  for (int h = warp; h < a.H + a.KVH; h += 8) {
+    float v[128];
+    const float *src = row + h * HD;  // q heads then k heads are contiguous
+    for (int i = lane; i < half; i += 32) {
+      v[i] = src[i];
+      v[i + half] = src[i + half];
+    }
+    norm_rope_head(v, HD, h < a.H ? qn : kn, cr, sr, true, lane);
+    if (h < a.H) {
+      for (int i = lane; i < half; i += 32) {
+        qs[h * HD + i] = v[i];
+        qs[h * HD + i + half] = v[i + half];
+      }
+    } else if (append) {
+      int g = h - a.H;
+      float *kd = kcb + (int64_t)pos * kvd + g * HD;
+      float *vd = vcb + (int64_t)pos * kvd + g * HD;
+      const float *vs = row + qd + kvd + g * HD;
+      for (int i = lane; i < half; i += 32) {
+        kd[i] = v[i];
+        kd[i + half] = v[i + half];
+        vd[i] = vs[i];
+        vd[i + half] = vs[i + half];
+      }
+    }
+  }
+  __syncthreads();
+  const int ctx = append ? pos + 1 : cap;
+  const int rep = a.H / a.KVH;
+  const float scale = a.scale;
+  for (int h = warp; h < a.H; h += 8) {
+    const int g = h / rep;
+    float *s = sc + h * cap;
+    float mx = -INFINITY;
+    for (int t = lane; t < ctx; t += 32) {
+      const float *k = kcb + (int64_t)t * kvd + g * HD;
+      float acc = 0.0f;
+      for (int d = 0; d < HD; ++d) acc = fmaf(qs[h * HD + d], k[d], acc);
+      acc *= scale;
+      s[t] = acc;
+      mx = fmaxf(mx, acc);
+    }
+    mx = warp_max(mx);
+    float sum = 0.0f;
+    for (int t = lane; t < ctx; t += 32) {
+      float p = expf(s[t] - mx);
+      s[t] = p;
+      sum += p;
+    }
+    sum = warp_sum(sum);
+    float inv = 1.0f / sum;
+    __syncwarp();
+    for (int d = lane; d < HD; d += 32) {
+      float acc = 0.0f;
+      for (int t = 0; t < ctx; ++t) acc = fmaf(s[t] * inv, vcb[(int64_t)t * kvd + g * HD + d], acc);
+      out[(int64_t)b * qd + h * HD + d] = acc;
+    }
+  }
+}
+
+// ── decoder cross-attention (attn.rs:281-337) ──────────────────────────────
+// CTA = (request, KV head).  The dominant HBM reader of batched decode: each
+// CTA streams its request's encoder K then V rows (HD f32 each) exactly once.
+// Specialised for HD == 64: a half-warp reads one 256-byte row with float4s.
+template <int REP>
+__global__ void __launch_bounds__(256) cross_attn_kernel(const float *__restrict__ q, const float *__restrict__ qn,
+                                                         const float *__restrict__ kplane,
+                                                         const float *__restrict__ vplane,
+                                                         const int64_t *__restrict__ seq_off, float *out,
+                                                         AttnDims a) {
+  constexpr int HD = 64;
+  extern __shared__ __align__(16) float sm[];
+  const int b = blockIdx.y, g = blockIdx.x;
+  const int64_t off = seq_off[b];
+  const int T = (int)(seq_off[b + 1] - off);
+  const int kvd = a.KVH * HD, qd = a.H * HD;
+  float *qs = sm;               // [REP][64]
+  float *red = sm + REP * HD;   // [16][REP][64] PV partials, also reductions
+  float *sc = red + 16 * REP * HD;  // [REP][T]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int hw = tid >> 4, hl = tid & 15;  // half-warp index (0..15), lane in half
+
+  // q heads of this group + q_norm (attn.rs:296-300)
+  if (warp < REP) {
+    int h = g * REP + warp;
+    float v[128];
+    const float *src = q + (int64_t)b * qd + h * HD;
+    v[lane] = src[lane];
+    v[lane + 32] = src[lane + 32];
+    norm_rope_head(v, HD, qn, nullptr, nullptr, false, lane);
+    qs[warp * HD + lane] = v[lane];
+    qs[warp * HD + lane + 32] = v[lane + 32];
+  }
+  __syncthreads();
+  float qr[REP][4];
+#pragma unroll
+  for (int j = 0; j < REP; ++j) {
+    float4 t = *reinterpret_cast<const float4 *>(qs + j * HD + hl * 4);
+    qr[j][0] = t.x;
+    qr[j][1] = t.y;
+    qr[j][2] = t.z;
+    qr[j][3] = t.w;
+  }
+  const float scale = a.scale;
+  const float *kb = kplane + off * kvd + g * HD + hl * 4;
+  // scores: in each 64-token block, half-warp hw handles tokens hw + 16u
+  // (u = 0..3, four rows in flight).  The loop bound is uniform over the
+  // block so both halves of a warp always reach the shuffles together.
+  for (int base = 0; base < T; base += 64) {
+    const int t0 = base + hw;
+    float4 kv[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      int t = t0 + u * 16;
+      kv[u] = t < T ? __ldg(reinterpret_cast<const float4 *>(kb + (int64_t)t * kvd)) : make_float4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      int t = t0 + u * 16;
+#pragma unroll
+      for (int j = 0; j < REP; ++j) {
+        float d = qr[j][0] * kv[u].x + qr[j][1] * kv[u].y + qr[j][2] * kv[u].z + qr[j][3] * kv[u].w;
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+        if (hl == 0 && t < T) sc[j * T + t] = d * scale;
+      }
+    }
+  }
+  __syncthreads();
+  // softmax per head (ops.rs:5-36): block max and sum
+  float *stat = red;  // reuse: [REP][8] maxes then sums
+  float mx[REP], inv[REP];
+#pragma unroll
+  for (int j = 0; j < REP; ++j) {
+    float m = -INFINITY;
+    for (int t = tid; t < T; t += 256) m = fmaxf(m, sc[j * T + t]);
+    m = warp_max(m);
+    if (lane == 0) stat[j * 8 + warp] = m;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < REP; ++j) {
+    float m = stat[j * 8];
+    for (int w = 1; w < 8; ++w) m = fmaxf(m, stat[j * 8 + w]);
+    mx[j] = m;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < REP; ++j) {
+    float s = 0.0f;
+    for (int t = tid; t < T; t += 256) {
+      float p = expf(sc[j * T + t] - mx[j]);
+      sc[j * T + t] = p;
+      s += p;
+    }
+    s = warp_sum(s);
+    if (lane == 0) stat[j * 8 + warp] = s;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < REP; ++j) {
+    float s = 0.0f;
+    for (int w = 0; w < 8; ++w) s += stat[j * 8 + w];
+    inv[j] = 1.0f / s;
+  }
+  __syncthreads();
+  // O = P V: half-warp hw accumulates tokens hw, hw+16, ... for dims hl*4..
+  float acc[REP][4];
+#pragma unroll
+  for (int j = 0; j < REP; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[j][e] = 0.0f;
+  const float *vb = vplane + off * kvd + g * HD + hl * 4;
+  for (int base = 0; base < T; base += 64) {
+    const int t0 = base + hw;
+    float4 vv[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      int t = t0 + u * 16;
+      vv[u] = t < T ? __ldg(reinterpret_cast<const float4 *>(vb + (int64_t)t * kvd)) : make_float4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      int t = t0 + u * 16;
+      if (t < T) {
+#pragma unroll
+        for (int j = 0; j < REP; ++j) {
+          float p = sc[j * T + t] * inv[j];
+          acc[j][0] = fmaf(p, vv[u].x, acc[j][0]);
+          acc[j][1] = fmaf(p, vv[u].y, acc[j][1]);
+          acc[j][2] = fmaf(p, vv[u].z, acc[j][2]);
+          acc[j][3] = fmaf(p, vv[u].w, acc[j][3]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < REP; ++j)
+    *reinterpret_cast<float4 *>(red + (hw * REP + j) * HD + hl * 4) =
+        make_float4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]);
+  __syncthreads();
+  for (int i = tid; i < REP * HD; i += 256) {
+    int j = i / HD, d = i - j * HD;
+    float s = 0.0f;
+    for (int w = 0; w < 16; ++w) s += red[(w * REP + j) * HD + d];
+    out[(int64_t)b * qd + (g * REP + j) * HD + d] = s;
+  }
+}
+
+// Generic cross-attention for head dims other than 64 (small test models).
+__global__ void cross_attn_generic_kernel(const float *__restrict__ q, const float *__restrict__ qn,
+                                          const float *__restrict__ kplane, const float *__restrict__ vplane,
+                                          const int64_t *__restrict__ seq_off, float *out, AttnDims a) {
+  extern __shared__ __align__(16) float sm[];
+  const int b = blockIdx.x, HD = a.HD;
+  const int64_t off = seq_off[b];
+  const int T = (int)(seq_off[b + 1] - off);
+  const int kvd = a.KVH * HD, qd = a.H * HD, rep = a.H / a.KVH;
+  float *qs = sm;         // [H*HD]
+  float *sc = sm + qd;    // [H][T]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int h = warp; h < a.H; h += blockDim.x / 32) {
+    float v[128];
+    for (int i = lane; i < HD / 2; i += 32) {
+      v[i] = q[(int64_t)b * qd + h * HD + i];
+      v[i + HD / 2] = q[(int64_t)b * qd + h * HD + i + HD / 2];
+    }
+    norm_rope_head(v, HD, qn, nullptr, nullptr, false, lane);
+    for (int i = lane; i < HD / 2; i += 32) {
+      qs[h * HD + i] = v[i];
+      qs[h * HD + i + HD / 2] = v[i + HD / 2];
+    }
+  }
+  __syncthreads();
+  const float scale = a.scale;
+  for (int h = warp; h < a.H; h += blockDim.x / 32) {
+    int g = h / rep;
+    float *s = sc + h * T;
+    float mx = -INFINITY;
+    for (int t = lane; t < T; t += 32) {
+      const float *k = kplane + (off + t) * kvd + g * HD;
+      float acc = 0.0f;
+      for (int d = 0; d < HD; ++d) acc = fmaf(qs[h * HD + d], k[d], acc);
+      s[t] = acc * scale;
+      mx = fmaxf(mx, s[t]);
+    }
+    mx = warp_max(mx);
+    float sum = 0.0f;
+    for (int t = lane; t < T; t += 32) {
+      float p = expf(s[t] - mx);
+      s[t] = p;
+      sum += p;
+    }
+    sum = warp_sum(sum);
+    __syncwarp();
+    float inv = 1.0f / sum;
+    for (int d = lane; d < HD; d += 32) {
+      float acc = 0.0f;
+      for (int t = 0; t < T; ++t) acc = fmaf(s[t] * inv, vplane[(off + t) * kvd + g * HD + d], acc);
+      out[(int64_t)b * qd + h * HD + d] = acc;
+    }
+  }
+}
+
+}  // namespace
+
+cudaError_t init_attention_kernels() {
+  cudaError_t e = cudaSuccess;
+  auto set = [&](const void *f) {
+    cudaError_t r = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
+    if (r != cudaSuccess) e = r;
+  };
+  set((const void *)encoder_attn_kernel);
+  set((const void *)dec_self_attn_kernel);
+  set((const void *)cross_attn_kernel<2>);
+  set((const void *)cross_attn_generic_kernel);
+  return e;
+}
+
+cudaError_t rms_norm_rows(const float *x, int64_t ldx, float *out, int64_t ldo, const float *scale, int rows,
+                          int d, cudaStream_t st) {
+  if (rows <= 0) return cudaSuccess;
+  if (d == 512 && ((ldx | ldo) & 3)) return cudaErrorInvalidValue;
+  int64_t threads = (int64_t)rows * 32;
+  rms_norm_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(x, ldx, out, ldo, scale, rows, d);
+  return cudaGetLastError();
+}
+
+cudaError_t head_norm_rows(float *x, int rows, int64_t ld, int heads, int HD, const float *scale, cudaStream_t st) {
+  if (rows <= 0 || heads <= 0) return cudaSuccess;
+  if (HD > 128 || (HD & 1)) return cudaErrorInvalidValue;
+  int64_t threads = (int64_t)rows * heads * 32;
+  head_norm_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(x, rows, ld, heads, HD, scale);
+  return cudaGetLastError();
+}
+
+cudaError_t embed_rows(const uint32_t *ids, const float *emb, float *x, int rows, int d, float es,
+                       cudaStream_t st) {
+  if (rows <= 0) return cudaSuccess;
+  int64_t threads = (int64_t)rows * 32;
+  embed_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(ids, emb, x, rows, d, es);
+  return cudaGetLastError();
+}
+
+cudaError_t qk_norm_rope_rows(float *qkv, int rows, const int32_t *pos, const float *q_norm, const float *k_norm,
+                              const float *rope_cos, const float *rope_sin, AttnDims a, cudaStream_t st) {
+  if (rows <= 0) return cudaSuccess;
+  if (a.HD > 128 || (a.HD & 1)) return cudaErrorInvalidValue;
+  int64_t threads = (int64_t)rows * (a.H + a.KVH) * 32;
+  qk_norm_rope_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(qkv, rows, pos, q_norm, k_norm, rope_cos,
+                                                                           rope_sin, a);
+  return cudaGetLastError();
+}
+
+cudaError_t encoder_attention(const float *qkv, const int64_t *seq_off, int n_req, int max_len, float *out,
+                              AttnDims a, cudaStream_t st) {
+  if (n_req <= 0 || max_len <= 0) return cudaSuccess;
+  if (a.HD > 64 || (a.HD & 3)) return cudaErrorInvalidValue;
+  size_t sm = (size_t)4 * 64 * EP * sizeof(float);
+  dim3 grid((max_len + EQ - 1) / EQ, a.H, n_req);
+  encoder_attn_kernel<<<grid, 256, sm, st>>>(qkv, seq_off, out, a);
+  return cudaGetLastError();
+}
+
+cudaError_t decoder_self_attention(const float *qkv, const int32_t *step, const float *q_norm,
+                                   const float *k_norm, const float *rope_cos, const float *rope_sin, float *kc,
+                                   float *vc, int cap, int B, float *out, AttnDims a, cudaStream_t st) {
+  if (B <= 0) return cudaSuccess;
+  if (a.HD > 128 || (a.HD & 1) || cap <= 0) return cudaErrorInvalidValue;
+  size_t sm = ((size_t)a.H * a.HD + (size_t)a.H * cap) * sizeof(float);
+  if (sm > kMaxDynSmem) return cudaErrorInvalidValue;
+  dec_self_attn_kernel<<<B, 256, sm, st>>>(qkv, step, q_norm, k_norm, rope_cos, rope_sin, kc, vc, cap, out, a);
+  return cudaGetLastError();
+}
+
+cudaError_t decoder_cross_attention(const float *q, const float *q_norm, const float *kplane,
+                                    const float *vplane, const int64_t *seq_off, int B, float *out, AttnDims a,
+                                    cudaStream_t st, int max_len) {
+  if (B <= 0) return cudaSuccess;
+  int rep = a.H / a.KVH;
+  if (a.HD == 64 && rep == 2) {
+    size_t sm = ((size_t)rep * 64 + (size_t)16 * rep * 64 + (size_t)rep * max_len) * sizeof(float);
+    if (sm > kMaxDynSmem) return cudaErrorInvalidValue;
+    cross_attn_kernel<2><<<dim3(a.KVH, B), 256, sm, st>>>(q, q_norm, kplane, vplane, seq_off, out, a);
+    return cudaGetLastError();
+  }
+  if (a.HD > 128 || (a.HD & 1)) return cudaErrorInvalidValue;
+  size_t sm = ((size_t)a.H * a.HD + (size_t)a.H * max_len) * sizeof(float);
+  if (sm > kMaxDynSmem) return cudaErrorInvalidValue;
+  cross_attn_generic_kernel<<<B, 256, sm, st>>>(q, q_norm, kplane, vplane, seq_off, out, a);
+  return cudaGetLastError();
+}
+
+}  // namespace ndl

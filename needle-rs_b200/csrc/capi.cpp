@@ -1,0 +1,460 @@
+// capi.cpp — the extern "C" boundary: needle.h (reference ABI) and
+// needle_b200.h (batched / kernel-level extensions).
+//
+// Mirrors crates/needle-c/src/lib.rs: thread-local last error (:21-33),
+// NULL-tolerant frees (:112-127), NULL handle -> NULL without an error
+// (:81-83), error strings "load error: ..." (:63, :164).
+#include <cuda_runtime.h>
+
+#include <cstdlib>
+#include <cstring>
+#include <fstream>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/needle_b200.h"
+#include "engine.h"
+
+using namespace ndl;
+
+struct NeedleHandle {
+  std::unique_ptr<DevModel> model;
+  std::string vocab_text;
+};
+
+struct NeedleBatch {
+  NeedleHandle *h = nullptr;
+  std::unique_ptr<Batch> batch;
+  BatchSpec spec;
+  std::vector<uint64_t> offsets;
+  bool time_cross = false;
+};
+
+namespace {
+
+thread_local std::string g_err;
+thread_local bool g_has_err = false;
+
+void set_err(const std::string &s) {
+  g_err = s;
+  g_has_err = true;
+}
+void clear_err() {
+  g_err.clear();
+  g_has_err = false;
+}
+
+int default_device() {
+  const char *e = std::getenv("NEEDLE_DEVICE");
+  return e ? std::atoi(e) : 0;
+}
+
+bool read_file(const char *path, std::vector<uint8_t> &out, std::string &err) {
+  std::ifstream f(path, std::ios::binary);
+  if (!f) {
+    err = std::string("No such file or directory (os error 2): ") + path;
+    return false;
+  }
+  out.assign(std::istreambuf_iterator<char>(f), std::istreambuf_iterator<char>());
+  return true;
+}
+
+bool valid_utf8(const uint8_t *s, size_t n) {
+  for (size_t i = 0; i < n;) {
+    unsigned char c = s[i];
+    size_t k = c < 0x80 ? 1 : (c >> 5) == 6 ? 2 : (c >> 4) == 14 ? 3 : (c >> 3) == 30 ? 4 : 0;
+    if (!k || i + k > n) return false;
+    for (size_t j = 1; j < k; ++j)
+      if ((s[i + j] >> 6) != 2) return false;
+    i += k;
+  }
+  return true;
+}
+
+NeedleHandle *load_impl(std::vector<uint8_t> weights, const std::string &vocab_text, int device) {
+  std::string err;
+  auto model = load_model(std::move(weights), device, err);
+  if (!model) {
+    set_err("load error: " + err);
+    return nullptr;
+  }
+  auto *h = new NeedleHandle();
+  h->model = std::move(model);
+  h->vocab_text = vocab_text;
+  return h;
+}
+
+NeedleHandle *load_path(const char *wp, const char *vp, int device) {
+  if (!wp || !vp) return nullptr;
+  if (!valid_utf8((const uint8_t *)wp, std::strlen(wp)) || !valid_utf8((const uint8_t *)vp, std::strlen(vp)))
+    return nullptr;
+  clear_err();
+  std::vector<uint8_t> w, v;
+  std::string err;
+  if (!read_file(wp, w, err) || !read_file(vp, v, err)) {
+    set_err("load error: " + err);
+    return nullptr;
+  }
+  return load_impl(std::move(w), std::string(v.begin(), v.end()), device);
+}
+
+NeedleHandle *load_bytes(const uint8_t *wd, size_t wl, const uint8_t *vd, size_t vl, int device) {
+  if (!wd || !vd) {
+    set_err("null pointer passed to needle_load_bytes");
+    return nullptr;
+  }
+  if (!valid_utf8(vd, vl)) {
+    set_err("vocab is not valid UTF-8");
+    return nullptr;
+  }
+  clear_err();
+  return load_impl(std::vector<uint8_t>(wd, wd + wl), std::string((const char *)vd, vl), device);
+}
+
+bool make_spec(NeedleHandle *h, const uint32_t *ids, const uint64_t *off, size_t n_req, uint32_t max_new,
+               const uint64_t *mask, uint32_t flags, BatchSpec &s) {
+  if (!h) return false;
+  if (!ids || !off || n_req == 0 || n_req > (size_t)INT32_MAX) {
+    set_err("invalid batch arguments");
+    return false;
+  }
+  s.ids = ids;
+  s.offsets = off;
+  s.n_req = (int)n_req;
+  s.max_new = (int)max_new;
+  s.mask = mask;
+  uint32_t f = 0;
+  if (flags & NEEDLE_STOP_ON_EOS) f |= BATCH_STOP_ON_EOS;
+  if (flags & NEEDLE_DEVICE_POINTERS) f |= BATCH_DEVICE_INPUTS;
+  if (flags & NEEDLE_NO_GRAPH) f |= BATCH_NO_GRAPH;
+  s.flags = f;
+  return true;
+}
+
+int run_batch(NeedleHandle *h, const uint32_t *ids, const uint64_t *off, size_t n_req, uint32_t max_new,
+              const uint64_t *mask, uint32_t flags, uint32_t *out_ids, uint32_t *out_lens, float *logits) {
+  if (!h) return -1;
+  clear_err();
+  BatchSpec s;
+  if (!make_spec(h, ids, off, n_req, max_new, mask, flags, s)) return -1;
+  s.want_logits = logits != nullptr;
+  Batch b(h->model.get());
+  std::string err;
+  if (!b.prepare(s, err) || !b.run(err) || !b.download(out_ids, out_lens, logits, nullptr, err)) {
+    set_err(err);
+    return -1;
+  }
+  return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+NeedleHandle *needle_load(const char *weights_path, const char *vocab_path) {
+  return load_path(weights_path, vocab_path, default_device());
+}
+
+NeedleHandle *needle_load_bytes(const uint8_t *wd, size_t wl, const uint8_t *vd, size_t vl) {
+  return load_bytes(wd, wl, vd, vl, default_device());
+}
+
+NeedleHandle *needle_load_on_device(const char *weights_path, const char *vocab_path, int device) {
+  return load_path(weights_path, vocab_path, device);
+}
+
+NeedleHandle *needle_load_bytes_on_device(const uint8_t *wd, size_t wl, const uint8_t *vd, size_t vl, int device) {
+  return load_bytes(wd, wl, vd, vl, device);
+}
+
+static char *run_text(NeedleHandle *h, const char *query, const char *tools_json, NeedleStreamCallback cb,
+                      void *ud) {
+  (void)cb;
+  (void)ud;
+  if (!h) return nullptr;
+  if (!query || !tools_json) return nullptr;
+  if (!valid_utf8((const uint8_t *)query, std::strlen(query)) ||
+      !valid_utf8((const uint8_t *)tools_json, std::strlen(tools_json)))
+    return nullptr;
+  clear_err();
+  set_err("needle_run: the text front end is not part of this build; use needle_run_batch_ids");
+  return nullptr;
+}
+
+char *needle_run(NeedleHandle *h, const char *query, const char *tools_json) {
+  return run_text(h, query, tools_json, nullptr, nullptr);
+}
+
+char *needle_run_stream(NeedleHandle *h, const char *query, const char *tools_json, NeedleStreamCallback cb,
+                        void *ud) {
+  return run_text(h, query, tools_json, cb, ud);
+}
+
+size_t needle_contrastive_dim(NeedleHandle *h) {
+  (void)h;
+  return 0;  // random-init / shipped checkpoints without contrastive tensors
+}
+
+bool needle_encode_contrastive(NeedleHandle *h, const char *text, float *out, size_t dim) {
+  (void)text;
+  (void)dim;
+  if (!h || !out) return false;
+  return false;
+}
+
+size_t needle_retrieve_tools(NeedleHandle *h, const char *query, const char **descs, size_t n, size_t k,
+                             size_t *idx, float *scores) {
+  (void)query;
+  (void)descs;
+  (void)idx;
+  (void)scores;
+  if (!h || n == 0 || k == 0) return 0;
+  return 0;
+}
+
+void needle_free_str(char *s) { std::free(s); }
+
+void needle_free(NeedleHandle *h) { delete h; }
+
+const char *needle_last_error(void) { return g_has_err ? g_err.c_str() : nullptr; }
+
+int needle_device_count(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) return 0;
+  return n;
+}
+
+int needle_model_config(NeedleHandle *h, int64_t *cfg) {
+  if (!h || !cfg) return -1;
+  const Config &c = h->model->cfg;
+  int64_t v[12] = {c.d_model,   c.num_heads,   c.num_kv_heads, c.num_layers,     c.num_dec_layers, c.vocab_size,
+                   c.max_enc_len, c.max_dec_len, c.ffn_dim,      c.no_feedforward, c.activation,     c.head_dim()};
+  std::memcpy(cfg, v, sizeof(v));
+  return 0;
+}
+
+int needle_handle_device(NeedleHandle *h) { return h ? h->model->device : -1; }
+
+int needle_run_batch_ids(NeedleHandle *h, const uint32_t *ids, const uint64_t *off, size_t n_req, uint32_t max_new,
+                         const uint64_t *mask, uint32_t flags, uint32_t *out_ids, uint32_t *out_lens) {
+  return run_batch(h, ids, off, n_req, max_new, mask, flags, out_ids, out_lens, nullptr);
+}
+
+int needle_run_batch_ids_logits(NeedleHandle *h, const uint32_t *ids, const uint64_t *off, size_t n_req,
+                                uint32_t max_new, const uint64_t *mask, uint32_t flags, uint32_t *out_ids,
+                                uint32_t *out_lens, float *logits) {
+  return run_batch(h, ids, off, n_req, max_new, mask, flags, out_ids, out_lens, logits);
+}
+
+NeedleBatch *needle_batch_prepare(NeedleHandle *h, const uint32_t *ids, const uint64_t *off, size_t n_req,
+                                  uint32_t max_new, const uint64_t *mask, uint32_t flags) {
+  if (!h) return nullptr;
+  clear_err();
+  auto nb = std::make_unique<NeedleBatch>();
+  nb->h = h;
+  if (!make_spec(h, ids, off, n_req, max_new, mask, flags, nb->spec)) return nullptr;
+  nb->offsets.assign(off, off + n_req + 1);
+  nb->spec.offsets = nb->offsets.data();
+  nb->batch = std::make_unique<Batch>(h->model.get());
+  std::string err;
+  if (!nb->batch->prepare(nb->spec, err)) {
+    set_err(err);
+    return nullptr;
+  }
+  return nb.release();
+}
+
+int needle_batch_run(NeedleBatch *nb) {
+  if (!nb) return -1;
+  clear_err();
+  std::string err;
+  nb->batch->enable_cross_timing(nb->time_cross);
+  if (!nb->batch->run(err)) {
+    set_err(err);
+    return -1;
+  }
+  return 0;
+}
+
+int needle_batch_sync(NeedleBatch *nb) {
+  if (!nb) return -1;
+  cudaError_t e = cudaStreamSynchronize(nb->batch->stream());
+  if (e != cudaSuccess) {
+    set_err(std::string("cudaStreamSynchronize failed: ") + cudaGetErrorString(e));
+    return -1;
+  }
+  return 0;
+}
+
+int needle_batch_results(NeedleBatch *nb, uint32_t *out_ids, uint32_t *out_lens) {
+  if (!nb) return -1;
+  std::string err;
+  if (!nb->batch->download(out_ids, out_lens, nullptr, nullptr, err)) {
+    set_err(err);
+    return -1;
+  }
+  return 0;
+}
+
+void *needle_batch_stream(NeedleBatch *nb) { return nb ? (void *)nb->batch->stream() : nullptr; }
+
+int64_t needle_batch_kernel_launches(NeedleBatch *nb) { return nb ? nb->batch->kernels_launched() : -1; }
+
+int needle_batch_time_cross_attention(NeedleBatch *nb, int enable) {
+  if (!nb) return -1;
+  nb->time_cross = enable != 0;
+  return 0;
+}
+
+int needle_batch_cross_attention_ms(NeedleBatch *nb, double *ms, int64_t *n) {
+  if (!nb) return -1;
+  std::string err;
+  if (!nb->batch->collect_cross_timing(err)) {
+    set_err(err);
+    return -1;
+  }
+  if (ms) *ms = nb->batch->cross_ms();
+  if (n) *n = nb->batch->cross_launches();
+  return 0;
+}
+
+void needle_batch_free(NeedleBatch *nb) { delete nb; }
+
+int needle_shard_requests(const uint64_t *off, size_t n_req, int shards, int32_t *assignment) {
+  if (!off || !assignment || shards <= 0) {
+    set_err("invalid shard arguments");
+    return -1;
+  }
+  shard_requests(off, (int)n_req, shards, assignment);
+  return 0;
+}
+
+int needle_debug_forward(NeedleHandle *h, const uint32_t *enc_ids, size_t n_enc, const uint32_t *dec_ids,
+                         size_t n_dec, float *enc_out, float *logits) {
+  if (!h) return -1;
+  clear_err();
+  if (!enc_ids || n_enc == 0 || (n_dec && !dec_ids)) {
+    set_err("invalid arguments");
+    return -1;
+  }
+  uint64_t off[2] = {0, n_enc};
+  BatchSpec s;
+  s.ids = enc_ids;
+  s.offsets = off;
+  s.n_req = 1;
+  s.max_new = (int)n_dec;
+  s.teacher = dec_ids;
+  s.want_logits = logits != nullptr;
+  s.want_enc_out = enc_out != nullptr;
+  s.flags = BATCH_NO_GRAPH;
+  Batch b(h->model.get());
+  std::string err;
+  for (size_t i = 0; i < n_dec; ++i)
+    if (dec_ids[i] >= (uint32_t)h->model->cfg.vocab_size) {
+      set_err("decoder token id out of range");
+      return -1;
+    }
+  if (!b.prepare(s, err) || !b.run(err) || !b.download(nullptr, nullptr, logits, enc_out, err)) {
+    set_err(err);
+    return -1;
+  }
+  return 0;
+}
+
+static bool dev_check(cudaError_t e) {
+  if (e != cudaSuccess) {
+    set_err(std::string("CUDA error: ") + cudaGetErrorString(e));
+    return false;
+  }
+  return true;
+}
+
+static bool ensure_kernels() {
+  static std::mutex mu;
+  static std::vector<bool> done;
+  int dev = 0;
+  if (!dev_check(cudaGetDevice(&dev))) return false;
+  std::lock_guard<std::mutex> g(mu);
+  if ((int)done.size() <= dev) done.resize(dev + 1, false);
+  if (!done[dev]) {
+    if (!dev_check(init_kernels())) return false;
+    done[dev] = true;
+  }
+  return true;
+}
+
+int needle_int4_matmul(const float *x, size_t M, size_t K, const uint8_t *w, const float *s, size_t N, size_t G,
+                       float *y, void *stream) {
+  clear_err();
+  if (!x || !w || !s || !y || M == 0 || K == 0 || N == 0 || G == 0 || M > INT32_MAX || K > INT32_MAX ||
+      N > INT32_MAX || G > INT32_MAX) {
+    set_err("invalid matmul arguments");
+    return -1;
+  }
+  if (!ensure_kernels()) return -1;
+  Int4Weight W{w, s, (int)K, (int)N, (int)G, (int)(K < 32 ? K : 32)};
+  MatmulOut o;
+  o.y = y;
+  o.ldy = (int64_t)N;
+  return dev_check(int4_matmul(x, (int64_t)K, (int)M, W, o, (cudaStream_t)stream)) ? 0 : -1;
+}
+
+int needle_int4_quantize(const float *w, size_t K, size_t N, uint8_t *data, float *scales, void *stream) {
+  clear_err();
+  if (!w || !data || !scales || K == 0 || N == 0 || K > INT32_MAX || N > INT32_MAX) {
+    set_err("invalid quantize arguments");
+    return -1;
+  }
+  if (!ensure_kernels()) return -1;
+  return dev_check(int4_quantize(w, (int)K, (int)N, data, scales, (cudaStream_t)stream)) ? 0 : -1;
+}
+
+int needle_int4_dequantize(const uint8_t *data, const float *scales, size_t K, size_t N, size_t G, float *out,
+                           void *stream) {
+  clear_err();
+  if (!data || !scales || !out || K == 0 || N == 0 || G == 0 || K > INT32_MAX || N > INT32_MAX) {
+    set_err("invalid dequantize arguments");
+    return -1;
+  }
+  if (!ensure_kernels()) return -1;
+  return dev_check(int4_dequantize(data, scales, (int)K, (int)N, (int)G, out, (cudaStream_t)stream)) ? 0 : -1;
+}
+
+int needle_ffn_forward(const float *x, size_t T, size_t d, size_t ff, const uint8_t *gd, const float *gs,
+                       const uint8_t *ud, const float *us, const uint8_t *dd, const float *ds, int act, float *out,
+                       void *stream) {
+  clear_err();
+  if (!x || !gd || !gs || !ud || !us || !dd || !ds || !out || T == 0 || d == 0 || ff == 0 || act < 0 || act > 2 ||
+      T > INT32_MAX || d > INT32_MAX || ff > INT32_MAX) {
+    set_err("invalid ffn arguments");
+    return -1;
+  }
+  if (!ensure_kernels()) return -1;
+  cudaStream_t st = (cudaStream_t)stream;
+  int gsz = (int)(d < 32 ? d : 32), gsd = (int)(ff < 32 ? ff : 32);
+  int G1 = (int)((d + gsz - 1) / gsz), G2 = (int)((ff + gsd - 1) / gsd);
+  float *hid = nullptr;
+  if (!dev_check(cudaMallocAsync((void **)&hid, T * ff * sizeof(float), st))) return -1;
+  Int4Weight gu{gd, gs, (int)d, (int)(2 * ff), G1, gsz};
+  gu.w2 = ud;
+  gu.s2 = us;
+  MatmulOut a;
+  a.y = hid;
+  a.ldy = (int64_t)ff;
+  a.epi = EPI_ACT;
+  a.act = act;
+  bool ok = dev_check(int4_matmul(x, (int64_t)d, (int)T, gu, a, st));
+  if (ok) {
+    Int4Weight dn{dd, ds, (int)ff, (int)d, G2, gsd};
+    MatmulOut o;
+    o.y = out;
+    o.ldy = (int64_t)d;
+    ok = dev_check(int4_matmul(hid, (int64_t)ff, (int)T, dn, o, st));
+  }
+  cudaFreeAsync(hid, st);
+  return ok ? 0 : -1;
+}
+
+}  // extern "C"

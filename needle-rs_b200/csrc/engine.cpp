@@ -1,0 +1,891 @@
+// engine.cpp — see engine.h.
+#include "engine.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <numeric>
+
+namespace ndl {
+
+#define NDL_CK(call)                                                                 \
+  do {                                                                               \
+    cudaError_t e_ = (call);                                                         \
+    if (e_ != cudaSuccess) {                                                         \
+      err = std::string(#call) + " failed: " + cudaGetErrorString(e_);               \
+      return false;                                                                  \
+    }                                                                                \
+  } while (0)
+
+const char *Config::validate() const {  // config.rs:83-103
+  if (num_heads <= 0) return "num_heads must be > 0";
+  if (num_kv_heads <= 0) return "num_kv_heads must be > 0";
+  if (d_model <= 0) return "d_model must be > 0";
+  if (d_model % num_heads) return "d_model must be divisible by num_heads";
+  if (num_heads % num_kv_heads) return "num_heads must be divisible by num_kv_heads";
+  if (vocab_size <= 0) return "vocab_size must be > 0";
+  return nullptr;
+}
+
+DevModel::~DevModel() {
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(device);
+  if (stream) cudaStreamSynchronize(stream);
+  for (void *p : allocs) cudaFree(p);
+  if (stream) cudaStreamDestroy(stream);
+  cudaSetDevice(prev);
+}
+
+namespace {
+
+struct HostQW {
+  std::vector<uint8_t> data;
+  std::vector<float> scales;
+  int K = 0, N = 0, G = 0, gs = 0;
+};
+
+bool parse_usize(const std::string &s, long long &out) {
+  size_t i = (!s.empty() && s[0] == '+') ? 1 : 0;
+  if (i >= s.size() || s.size() - i > 18) return false;
+  for (size_t j = i; j < s.size(); ++j)
+    if (s[j] < '0' || s[j] > '9') return false;
+  out = std::stoll(s.substr(i));
+  return true;
+}
+
+// engine.rs:578-624
+Config load_config(const SafeTensors &st) {
+  Config d, c;
+  auto uf = [&](const char *k, int fb) {
+    const std::string *v = st.metadata(k);
+    long long x;
+    return (v && parse_usize(*v, x) && x <= (1LL << 30)) ? (int)x : fb;
+  };
+  auto ff = [&](const char *k, float fb) {
+    const std::string *v = st.metadata(k);
+    if (!v || v->empty()) return fb;
+    char *e = nullptr;
+    float x = std::strtof(v->c_str(), &e);
+    return (e && *e == 0) ? x : fb;
+  };
+  auto bf = [&](const char *k, bool fb) {
+    const std::string *v = st.metadata(k);
+    return v ? (*v == "True" || *v == "true" || *v == "1") : fb;
+  };
+  long long me;
+  const std::string *v;
+  if ((v = st.metadata("max_enc_len")) && parse_usize(*v, me) && me <= (1LL << 30))
+    c.max_enc_len = (int)me;
+  else if ((v = st.metadata("max_seq_len")) && parse_usize(*v, me) && me <= (1LL << 30))
+    c.max_enc_len = (int)me;
+  else
+    c.max_enc_len = d.max_enc_len;
+  c.activation = ACT_DRELU;
+  if ((v = st.metadata("activation"))) c.activation = *v == "swiglu" ? ACT_SWIGLU : *v == "geglu" ? ACT_GELU : ACT_DRELU;
+  c.d_model = uf("d_model", d.d_model);
+  c.num_heads = uf("num_heads", d.num_heads);
+  c.num_kv_heads = uf("num_kv_heads", d.num_kv_heads);
+  c.num_layers = uf("num_encoder_layers", d.num_layers);
+  c.num_dec_layers = uf("num_decoder_layers", d.num_dec_layers);
+  c.vocab_size = uf("vocab_size", d.vocab_size);
+  c.max_dec_len = uf("max_dec_len", d.max_dec_len);
+  c.ffn_dim = uf("ffn_dim", d.ffn_dim);
+  c.no_feedforward = bf("no_feedforward", d.no_feedforward);
+  c.rope_theta = ff("rope_theta", d.rope_theta);
+  return c;
+}
+
+struct Loader {
+  const SafeTensors &st;
+  DevModel &m;
+  std::string &err;
+
+  template <class T>
+  bool dalloc(T *&p, size_t n) {
+    void *q = nullptr;
+    NDL_CK(cudaMalloc(&q, std::max<size_t>(n, 1) * sizeof(T)));
+    m.allocs.push_back(q);
+    m.weight_bytes += n * sizeof(T);
+    p = (T *)q;
+    return true;
+  }
+  template <class T>
+  bool upload(T *&p, const T *src, size_t n) {
+    if (!dalloc(p, n)) return false;
+    NDL_CK(cudaMemcpy(p, src, n * sizeof(T), cudaMemcpyHostToDevice));
+    return true;
+  }
+  bool vec(const std::string &name, size_t len, float *&p) {  // engine.rs:784-786
+    std::vector<float> v;
+    if (!st.get_f32(name, v)) v.assign(len, 0.0f);
+    if (v.size() < len) {  // the reference would index past the end
+      err = name + ": expected " + std::to_string(len) + " values, found " + std::to_string(v.size());
+      return false;
+    }
+    v.resize(len);
+    return upload(p, v.data(), len);
+  }
+  bool vec_host(const std::string &name, size_t len, std::vector<float> &v) {
+    if (!st.get_f32(name, v)) v.assign(len, 0.0f);
+    if (v.size() < len) {
+      err = name + ": expected " + std::to_string(len) + " values, found " + std::to_string(v.size());
+      return false;
+    }
+    v.resize(len);
+    return true;
+  }
+  float gate(const std::string &name) {  // engine.rs:788-792, then ops.rs:40-42 sigmoid
+    std::vector<float> v;
+    float g = (st.get_f32(name, v) && !v.empty()) ? v[0] : 0.0f;
+    return 1.0f / (1.0f + std::exp(-g));
+  }
+  bool quantize_dev(const std::vector<float> &w, int K, int N, HostQW &q) {
+    int gs = K < 32 ? K : 32;
+    if (gs <= 0 || (gs & 1)) {
+      err = "in_feat " + std::to_string(K) + " below 32 must be even to pack pairs";
+      return false;
+    }
+    int Kp = K + (gs - K % gs) % gs, G = Kp / gs;
+    q.K = K;
+    q.N = N;
+    q.G = G;
+    q.gs = gs;
+    q.data.assign((size_t)Kp / 2 * N, 0);
+    q.scales.assign((size_t)G * N, 0.0f);
+    float *dw = nullptr, *ds = nullptr;
+    uint8_t *dd = nullptr;
+    NDL_CK(cudaMalloc(&dw, w.size() * sizeof(float) + 16));
+    NDL_CK(cudaMalloc(&dd, q.data.size() + 16));
+    NDL_CK(cudaMalloc(&ds, q.scales.size() * sizeof(float) + 16));
+    bool ok = cudaMemcpy(dw, w.data(), w.size() * sizeof(float), cudaMemcpyHostToDevice) == cudaSuccess &&
+              int4_quantize(dw, K, N, dd, ds, m.stream) == cudaSuccess &&
+              cudaMemcpyAsync(q.data.data(), dd, q.data.size(), cudaMemcpyDeviceToHost, m.stream) == cudaSuccess &&
+              cudaMemcpyAsync(q.scales.data(), ds, q.scales.size() * sizeof(float), cudaMemcpyDeviceToHost,
+                              m.stream) == cudaSuccess &&
+              cudaStreamSynchronize(m.stream) == cudaSuccess;
+    cudaFree(dw);
+    cudaFree(dd);
+    cudaFree(ds);
+    if (!ok) err = "device quantization failed";
+    return ok;
+  }
+  // engine.rs:752-782
+  bool quant(const std::string &name, int K, int N, HostQW &q) {
+    size_t rawlen = 0;
+    const uint8_t *raw = st.get_raw(name, &rawlen);
+    std::vector<float> scales;
+    if (raw && st.get_f32(name + ".scale", scales)) {
+      if (N == 0 || scales.size() % (size_t)N != 0) {
+        std::fprintf(stderr, "Warning: %s.scale length %zu is not divisible by out_feat %d; re-quantizing\n",
+                     name.c_str(), scales.size(), N);
+        std::vector<float> w;
+        if (!st.get_f32(name, w)) w.assign((size_t)K * N, 0.0f);
+        if (w.size() != (size_t)K * N) {
+          err = name + ": cannot re-quantize a tensor of " + std::to_string(w.size()) + " values";
+          return false;
+        }
+        return quantize_dev(w, K, N, q);
+      }
+      q.K = K;
+      q.N = N;
+      q.G = (int)(scales.size() / N);
+      q.gs = K < 32 ? K : 32;
+      if (q.gs & 1) {
+        err = name + ": odd group size";
+        return false;
+      }
+      size_t need = (size_t)q.G * q.gs / 2 * N;
+      if (rawlen < need) {
+        err = name + ": packed data holds " + std::to_string(rawlen) + " bytes, its scales need " +
+              std::to_string(need);
+        return false;
+      }
+      q.data.assign(raw, raw + need);
+      q.scales = std::move(scales);
+      return true;
+    }
+    std::vector<float> w;
+    if (!st.get_f32(name, w)) {
+      std::fprintf(stderr, "Warning: missing tensor %s, using zeros\n", name.c_str());
+      w.assign((size_t)K * N, 0.0f);
+    }
+    if (w.size() != (size_t)K * N) {
+      err = name + ": expected " + std::to_string((size_t)K * N) + " values, found " + std::to_string(w.size());
+      return false;
+    }
+    return quantize_dev(w, K, N, q);
+  }
+  bool put(const HostQW &q, Lin &l) {
+    l.K = q.K;
+    l.N = q.N;
+    l.G = q.G;
+    l.gs = q.gs;
+    return upload(l.w, q.data.data(), q.data.size()) && upload(l.s, q.scales.data(), q.scales.size());
+  }
+};
+
+// Concatenate along N (the reference layout keeps each pair-row contiguous
+// over N, so this is a per-row splice).  Groups are padded to the largest G
+// with zero codes and scales, which contribute exactly 0.
+HostQW concat_cols(const std::vector<const HostQW *> &parts) {
+  HostQW o;
+  o.K = parts[0]->K;
+  o.gs = parts[0]->gs;
+  for (auto *p : parts) {
+    o.N += p->N;
+    o.G = std::max(o.G, p->G);
+  }
+  size_t npairs = (size_t)o.G * o.gs / 2;
+  o.data.assign(npairs * o.N, 0);
+  o.scales.assign((size_t)o.G * o.N, 0.0f);
+  int c = 0;
+  for (auto *p : parts) {
+    size_t pp = (size_t)p->G * p->gs / 2;
+    for (size_t r = 0; r < pp; ++r) std::memcpy(&o.data[r * o.N + c], &p->data[r * p->N], p->N);
+    for (int g = 0; g < p->G; ++g) std::memcpy(&o.scales[(size_t)g * o.N + c], &p->scales[(size_t)g * p->N], p->N * 4);
+    c += p->N;
+  }
+  return o;
+}
+
+// Interleave columns of two same-shape weights: (a_0, b_0, a_1, b_1, ...).
+HostQW interleave_cols(const HostQW &a, const HostQW &b) {
+  HostQW o;
+  o.K = a.K;
+  o.gs = a.gs;
+  o.G = std::max(a.G, b.G);
+  o.N = a.N * 2;
+  size_t npairs = (size_t)o.G * o.gs / 2;
+  o.data.assign(npairs * o.N, 0);
+  o.scales.assign((size_t)o.G * o.N, 0.0f);
+  for (int s = 0; s < 2; ++s) {
+    const HostQW &p = s ? b : a;
+    size_t pp = (size_t)p.G * p.gs / 2;
+    for (size_t r = 0; r < pp; ++r)
+      for (int n = 0; n < p.N; ++n) o.data[r * o.N + 2 * n + s] = p.data[r * p.N + n];
+    for (int g = 0; g < p.G; ++g)
+      for (int n = 0; n < p.N; ++n) o.scales[(size_t)g * o.N + 2 * n + s] = p.scales[(size_t)g * p.N + n];
+  }
+  return o;
+}
+
+}  // namespace
+
+std::unique_ptr<DevModel> load_model(std::vector<uint8_t> raw, int device, std::string &err) {
+  SafeTensors st;
+  if (!st.parse(std::move(raw), err)) return nullptr;
+  Config c = load_config(st);
+  if (const char *e = c.validate()) {
+    err = e;
+    return nullptr;
+  }
+  const int d = c.d_model, H = c.num_heads, KVH = c.num_kv_heads, hd = c.head_dim(), V = c.vocab_size;
+  // Shapes the sm_100a kernels support (the shipped config is d=512, hd=64).
+  if ((d % 4) || (hd % 4) || hd > 64) {
+    err = "unsupported dims for the GPU path: d_model % 4 == 0, head_dim % 4 == 0 and head_dim <= 64 required";
+    return nullptr;
+  }
+  if (std::max(c.max_enc_len, c.max_dec_len) > 8192 || c.ffn_dim <= 0 && !c.no_feedforward) {
+    err = "unsupported max_enc_len / max_dec_len / ffn_dim";
+    return nullptr;
+  }
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+    err = "no CUDA device available";
+    return nullptr;
+  }
+  if (device < 0 || device >= ndev) {
+    err = "device index " + std::to_string(device) + " out of range (" + std::to_string(ndev) + " devices)";
+    return nullptr;
+  }
+  auto m = std::make_unique<DevModel>();
+  m->device = device;
+  m->cfg = c;
+  if (cudaSetDevice(device) != cudaSuccess || init_kernels() != cudaSuccess ||
+      cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess) {
+    err = "CUDA initialisation failed on device " + std::to_string(device);
+    return nullptr;
+  }
+  cudaMemPool_t pool;
+  if (cudaDeviceGetDefaultMemPool(&pool, device) == cudaSuccess) {
+    uint64_t thr = UINT64_MAX;
+    cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &thr);
+  }
+  Loader L{st, *m, err};
+  std::vector<float> emb;
+  if (!st.get_f32("embedding", emb)) {
+    err = "missing embedding tensor";
+    return nullptr;
+  }
+  if (emb.size() != (size_t)V * d) {
+    err = "embedding size mismatch: got " + std::to_string(emb.size()) + ", expected " + std::to_string((size_t)V * d);
+    return nullptr;
+  }
+  m->emb_bf16_exact = st.is_bf16_exact("embedding");
+  if (!L.upload(m->emb, emb.data(), emb.size())) return nullptr;
+
+  auto load_ffn = [&](const std::string &p, Lin &gu, Lin &down, float *&norm, float &gate) {
+    HostQW g, u, dn;
+    if (!L.quant(p + ".ffn.gate_proj", d, c.ffn_dim, g) || !L.quant(p + ".ffn.up_proj", d, c.ffn_dim, u) ||
+        !L.quant(p + ".ffn.down_proj", c.ffn_dim, d, dn))
+      return false;
+    gate = L.gate(p + ".ffn_gate");
+    return L.put(interleave_cols(g, u), gu) && L.put(dn, down) && L.vec(p + ".ffn_norm", d, norm);
+  };
+
+  m->enc.resize(c.num_layers);
+  for (int i = 0; i < c.num_layers; ++i) {  // engine.rs:677-696
+    std::string p = "encoder." + std::to_string(i);
+    EncLayerDev &E = m->enc[i];
+    if (!c.no_feedforward) {
+      E.ffn = true;
+      if (!load_ffn(p, E.gate_up, E.down, E.ffn_norm, E.ffn_gate)) return nullptr;
+    }
+    HostQW wq, wk, wv, wo;
+    std::string a = p + ".self_attn";
+    if (!L.quant(a + ".wq", d, H * hd, wq) || !L.quant(a + ".wk", d, KVH * hd, wk) ||
+        !L.quant(a + ".wv", d, KVH * hd, wv) || !L.quant(a + ".wo", H * hd, d, wo))
+      return nullptr;
+    if (!L.put(concat_cols({&wq, &wk, &wv}), E.qkv) || !L.put(wo, E.o) || !L.vec(a + ".q_norm", hd, E.q_norm) ||
+        !L.vec(a + ".k_norm", hd, E.k_norm) || !L.vec(p + ".norm", d, E.norm))
+      return nullptr;
+    E.gate = L.gate(p + ".self_attn_gate");
+  }
+  m->dec.resize(c.num_dec_layers);
+  std::vector<HostQW> cross_parts(2 * c.num_dec_layers);
+  std::vector<float> knorm_all;
+  for (int i = 0; i < c.num_dec_layers; ++i) {  // engine.rs:698-720
+    std::string p = "decoder." + std::to_string(i);
+    DecLayerDev &D = m->dec[i];
+    if (!c.no_feedforward) {
+      D.ffn = true;
+      if (!load_ffn(p, D.gate_up, D.down, D.ffn_norm, D.ffn_gate)) return nullptr;
+    }
+    HostQW wq, wk, wv, wo, cq, co;
+    std::string a = p + ".self_attn", x = p + ".cross_attn";
+    if (!L.quant(a + ".wq", d, H * hd, wq) || !L.quant(a + ".wk", d, KVH * hd, wk) ||
+        !L.quant(a + ".wv", d, KVH * hd, wv) || !L.quant(a + ".wo", H * hd, d, wo) ||
+        !L.quant(x + ".wq", d, H * hd, cq) || !L.quant(x + ".wk", d, KVH * hd, cross_parts[2 * i]) ||
+        !L.quant(x + ".wv", d, KVH * hd, cross_parts[2 * i + 1]) || !L.quant(x + ".wo", H * hd, d, co))
+      return nullptr;
+    std::vector<float> kn;
+    if (!L.put(concat_cols({&wq, &wk, &wv}), D.sa_qkv) || !L.put(wo, D.sa_o) || !L.put(cq, D.ca_q) ||
+        !L.put(co, D.ca_o) || !L.vec(a + ".q_norm", hd, D.sa_qn) || !L.vec(a + ".k_norm", hd, D.sa_kn) ||
+        !L.vec(x + ".q_norm", hd, D.ca_qn) || !L.vec_host(x + ".k_norm", hd, kn) ||
+        !L.vec(p + ".self_attn_norm", d, D.sa_norm) || !L.vec(p + ".cross_attn_norm", d, D.ca_norm))
+      return nullptr;
+    knorm_all.insert(knorm_all.end(), kn.begin(), kn.end());
+    D.sa_gate = L.gate(p + ".self_attn_gate");
+    D.ca_gate = L.gate(p + ".cross_attn_gate");
+  }
+  if (c.num_dec_layers > 0) {
+    std::vector<const HostQW *> parts;
+    for (auto &q : cross_parts) parts.push_back(&q);
+    if (!L.put(concat_cols(parts), m->cross_kv) || !L.upload(m->cross_knorm, knorm_all.data(), knorm_all.size()))
+      return nullptr;
+  }
+  if (!L.vec("encoder_final_norm", d, m->enc_final_norm) || !L.vec("decoder_final_norm", d, m->dec_final_norm))
+    return nullptr;
+  // RoPE table (rope.rs:20-41, model.rs:52-56), computed on the host with the
+  // reference's formula and uploaded.
+  m->rope_len = std::max(c.max_enc_len, c.max_dec_len);
+  int half = hd / 2;
+  std::vector<float> rc((size_t)m->rope_len * half), rs((size_t)m->rope_len * half);
+  for (int pos = 0; pos < m->rope_len; ++pos)
+    for (int i = 0; i < half; ++i) {
+      float e = 2.0f * (float)i;
+      e = e / (float)hd;
+      float theta = (float)pos / std::pow(c.rope_theta, e);
+      rc[(size_t)pos * half + i] = std::cos(theta);
+      rs[(size_t)pos * half + i] = std::sin(theta);
+    }
+  if (!L.upload(m->rope_cos, rc.data(), rc.size()) || !L.upload(m->rope_sin, rs.data(), rs.size())) return nullptr;
+  m->embed_scale = std::sqrt((float)d);  // model.rs:63
+  m->ad.H = H;
+  m->ad.KVH = KVH;
+  m->ad.HD = hd;
+  m->ad.scale = std::pow((float)hd, -0.5f);  // attn.rs:142
+  return m;
+}
+
+// ── Batch ──────────────────────────────────────────────────────────────────
+Batch::Batch(DevModel *m) : m_(m) {
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(m_->device);
+  if (cudaStreamCreateWithFlags(&st_, cudaStreamNonBlocking) != cudaSuccess) st_ = nullptr;
+  cudaSetDevice(prev);
+}
+
+template <class T>
+T *Batch::alloc(size_t n, std::string &err) {
+  void *p = nullptr;
+  if (!st_) {
+    err = "stream creation failed";
+    return nullptr;
+  }
+  cudaError_t e = cudaMallocAsync(&p, std::max<size_t>(n, 1) * sizeof(T), st_);
+  if (e != cudaSuccess) {
+    err = std::string("device allocation of ") + std::to_string(n * sizeof(T)) + " bytes failed: " +
+          cudaGetErrorString(e);
+    return nullptr;
+  }
+  bufs_.push_back(p);
+  return (T *)p;
+}
+
+Batch::~Batch() {
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(m_->device);
+  if (graph_) cudaGraphExecDestroy(graph_);
+  for (auto &e : cross_events_) {
+    cudaEventDestroy(e.first);
+    cudaEventDestroy(e.second);
+  }
+  if (st_) {
+    for (void *p : bufs_) cudaFreeAsync(p, st_);
+    cudaStreamSynchronize(st_);
+    cudaStreamDestroy(st_);
+  }
+  cudaSetDevice(prev);
+}
+
+bool Batch::prepare(const BatchSpec &spec, std::string &err) {
+  const Config &c = m_->cfg;
+  NDL_CK(cudaSetDevice(m_->device));
+  spec_ = spec;
+  const int B = spec.n_req;
+  if (B <= 0) {
+    err = "empty batch";
+    return false;
+  }
+  if (spec.max_new < 0 || spec.max_new > c.max_dec_len) {
+    // engine.rs:290 bounds generation by max_dec_len.
+    err = "max_new must be in [0, max_dec_len=" + std::to_string(c.max_dec_len) + "]";
+    return false;
+  }
+  if (!spec.offsets || (!spec.ids)) {
+    err = "null prompt pointer";
+    return false;
+  }
+  off_h_.assign(spec.offsets, spec.offsets + B + 1);
+  const uint64_t base = off_h_[0];
+  for (auto &o : off_h_) o -= base;
+  tmax_ = 0;
+  for (int r = 0; r < B; ++r) {
+    if (spec.offsets[r + 1] < spec.offsets[r]) {
+      err = "prompt offsets must be non-decreasing";
+      return false;
+    }
+    int64_t T = (int64_t)(off_h_[r + 1] - off_h_[r]);
+    if (T < 1 || T > c.max_enc_len) {
+      err = "request " + std::to_string(r) + " has " + std::to_string(T) + " prompt tokens; 1.." +
+            std::to_string(c.max_enc_len) + " allowed";
+      return false;
+    }
+    tmax_ = std::max<int>(tmax_, (int)T);
+  }
+  ttot_ = (int64_t)off_h_[B];
+  const bool dev_in = spec.flags & BATCH_DEVICE_INPUTS;
+  const int d = c.d_model, V = c.vocab_size, hd = c.head_dim();
+  const int kvd = c.num_kv_heads * hd, qd = c.num_heads * hd, qkvd = qd + 2 * kvd, L = c.num_dec_layers;
+  W_ = (V + 63) / 64;
+  cap_ = std::max(1, spec.max_new);
+  cudaStream_t st = st_;
+
+  // prompt ids: validated (an out-of-range id would index past the embedding)
+  std::vector<uint32_t> ids_h;
+  if (dev_in) {
+    ids_h.resize(ttot_);
+    NDL_CK(cudaMemcpy(ids_h.data(), spec.ids + base, ttot_ * sizeof(uint32_t), cudaMemcpyDeviceToHost));
+  }
+  const uint32_t *idp = dev_in ? ids_h.data() : spec.ids + base;
+  for (int64_t i = 0; i < ttot_; ++i)
+    if (idp[i] >= (uint32_t)V) {
+      err = "token id " + std::to_string(idp[i]) + " out of range (vocab " + std::to_string(V) + ")";
+      return false;
+    }
+  if (spec.teacher)
+    for (int64_t i = 0; i < (int64_t)B * spec.max_new; ++i)
+      if (spec.teacher[i] >= (uint32_t)V) {
+        err = "teacher token id out of range";
+        return false;
+      }
+  if (dev_in) {
+    ids_ = const_cast<uint32_t *>(spec.ids + base);
+  } else {
+    if (!(ids_ = alloc<uint32_t>(ttot_, err))) return false;
+    NDL_CK(cudaMemcpyAsync(ids_, spec.ids + base, ttot_ * sizeof(uint32_t), cudaMemcpyHostToDevice, st));
+  }
+  std::vector<int64_t> so(off_h_.begin(), off_h_.end());
+  std::vector<int32_t> tp(ttot_);
+  for (int r = 0; r < B; ++r)
+    for (uint64_t t = off_h_[r]; t < off_h_[r + 1]; ++t) tp[t] = (int32_t)(t - off_h_[r]);
+  if (!(seq_off_ = alloc<int64_t>(B + 1, err)) || !(tok_pos_ = alloc<int32_t>(ttot_, err))) return false;
+  NDL_CK(cudaMemcpyAsync(seq_off_, so.data(), so.size() * sizeof(int64_t), cudaMemcpyHostToDevice, st));
+  NDL_CK(cudaMemcpyAsync(tok_pos_, tp.data(), tp.size() * sizeof(int32_t), cudaMemcpyHostToDevice, st));
+  if (spec.mask && spec.max_new > 0) {
+    size_t n = (size_t)B * spec.max_new * W_;
+    if (dev_in) {
+      mask_ = const_cast<uint64_t *>(spec.mask);
+    } else {
+      if (!(mask_ = alloc<uint64_t>(n, err))) return false;
+      NDL_CK(cudaMemcpyAsync(mask_, spec.mask, n * sizeof(uint64_t), cudaMemcpyHostToDevice, st));
+    }
+  }
+  std::vector<uint32_t> first(B, kEosId);  // decoding starts from EOS (engine.rs:287)
+  if (spec.teacher && spec.max_new > 0) {
+    if (!(teacher_ = alloc<uint32_t>((size_t)B * spec.max_new, err))) return false;
+    NDL_CK(cudaMemcpyAsync(teacher_, spec.teacher, (size_t)B * spec.max_new * 4, cudaMemcpyHostToDevice, st));
+    for (int b = 0; b < B; ++b) first[b] = spec.teacher[(size_t)b * spec.max_new];
+  }
+  uint32_t *first_d = alloc<uint32_t>(B, err);
+  if (!first_d) return false;
+  NDL_CK(cudaMemcpyAsync(first_d, first.data(), B * 4, cudaMemcpyHostToDevice, st));
+
+  // prefill chunks bounded by a token budget
+  const int64_t budget = std::max<int64_t>(262144, tmax_);
+  chunks_.clear();
+  chunk_tok_max_ = 0;
+  std::vector<int64_t> rel_all;
+  for (int r = 0; r < B;) {
+    Chunk ch{r, r, (int64_t)off_h_[r], 0, 0, nullptr};
+    while (ch.r1 < B && (ch.ntok + (int64_t)(off_h_[ch.r1 + 1] - off_h_[ch.r1]) <= budget || ch.r1 == r)) {
+      ch.ntok += (int64_t)(off_h_[ch.r1 + 1] - off_h_[ch.r1]);
+      ch.tmax = std::max<int>(ch.tmax, (int)(off_h_[ch.r1 + 1] - off_h_[ch.r1]));
+      ++ch.r1;
+    }
+    chunk_tok_max_ = std::max(chunk_tok_max_, ch.ntok);
+    chunks_.push_back(ch);
+    r = ch.r1;
+  }
+  int64_t nrel = 0;
+  for (auto &ch : chunks_) nrel += ch.r1 - ch.r0 + 1;
+  int64_t *rel = alloc<int64_t>(nrel, err);
+  if (!rel) return false;
+  {
+    std::vector<int64_t> rh;
+    for (auto &ch : chunks_) {
+      ch.rel_off = rel + rh.size();
+      for (int r = ch.r0; r <= ch.r1; ++r) rh.push_back((int64_t)off_h_[r] - ch.tok0);
+    }
+    NDL_CK(cudaMemcpyAsync(rel, rh.data(), rh.size() * sizeof(int64_t), cudaMemcpyHostToDevice, st));
+  }
+  const int64_t ct = chunk_tok_max_;
+  if (!(px_ = alloc<float>(ct * d, err)) || !(pxn_ = alloc<float>(ct * d, err)) ||
+      !(pqkv_ = alloc<float>(ct * qkvd, err)) || !(patt_ = alloc<float>(ct * qd, err)))
+    return false;
+  if (!c.no_feedforward && !(pffn_ = alloc<float>(ct * c.ffn_dim, err))) return false;
+  if (L > 0 && !(kv_planes_ = alloc<float>((size_t)2 * L * ttot_ * kvd, err))) return false;
+  if (spec.want_enc_out && !(enc_out_ = alloc<float>((size_t)ttot_ * d, err))) return false;
+
+  // decoder state
+  if (spec.max_new > 0) {
+    size_t cache = (size_t)L * B * cap_ * kvd;
+    if (!(self_k_ = alloc<float>(cache, err)) || !(self_v_ = alloc<float>(cache, err)) ||
+        !(x_ = alloc<float>((size_t)B * d, err)) || !(xn_ = alloc<float>((size_t)B * d, err)) ||
+        !(h_ = alloc<float>((size_t)B * d, err)) || !(qkv_ = alloc<float>((size_t)B * qkvd, err)) ||
+        !(att_ = alloc<float>((size_t)B * qd, err)) || !(q_ = alloc<float>((size_t)B * qd, err)) ||
+        !(keys_ = alloc<unsigned long long>(B, err)) || !(pos_ = alloc<int32_t>(B, err)) ||
+        !(out_ids_ = alloc<uint32_t>((size_t)B * spec.max_new, err)) || !(lens_ = alloc<uint32_t>(B, err)) ||
+        !(done_ = alloc<uint8_t>(B, err)) || !(n_done_ = alloc<unsigned int>(1, err)))
+      return false;
+    if (!c.no_feedforward && !(ffn_ = alloc<float>((size_t)B * c.ffn_dim, err))) return false;
+    if (spec.want_logits && !(logits_ = alloc<float>((size_t)B * spec.max_new * V, err))) return false;
+  }
+  first_ids_ = first_d;
+  return true;
+}
+
+bool Batch::reset_decoder(std::string &err) {
+  // Fresh decoder state for a (re-)run; inputs and the encoder buffers are
+  // reused as uploaded by prepare().
+  if (spec_.max_new == 0) return true;
+  const int B = spec_.n_req, d = m_->cfg.d_model;
+  cudaStream_t st = st_;
+  NDL_CK(cudaMemsetAsync(keys_, 0, B * sizeof(unsigned long long), st));
+  NDL_CK(cudaMemsetAsync(pos_, 0, B * sizeof(int32_t), st));
+  NDL_CK(cudaMemsetAsync(lens_, 0, B * sizeof(uint32_t), st));
+  NDL_CK(cudaMemsetAsync(done_, 0, B, st));
+  NDL_CK(cudaMemsetAsync(n_done_, 0, sizeof(unsigned int), st));
+  NDL_CK(cudaMemsetAsync(out_ids_, 0, (size_t)B * spec_.max_new * 4, st));
+  NDL_CK(embed_rows(first_ids_, m_->emb, x_, B, d, m_->embed_scale, st));
+  ++launches_;
+  return true;
+}
+
+#define NDL_LK(call)                                                                 \
+  do {                                                                               \
+    cudaError_t e_ = (call);                                                         \
+    ++launches_;                                                                     \
+    if (e_ != cudaSuccess) {                                                         \
+      err = std::string(#call) + " failed: " + cudaGetErrorString(e_);               \
+      return false;                                                                  \
+    }                                                                                \
+  } while (0)
+
+bool Batch::prefill(std::string &err) {
+  const DevModel &m = *m_;
+  const Config &c = m.cfg;
+  const int d = c.d_model, hd = c.head_dim(), qd = c.num_heads * hd, kvd = c.num_kv_heads * hd;
+  const int qkvd = qd + 2 * kvd, L = c.num_dec_layers;
+  cudaStream_t st = st_;
+  for (const Chunk &ch : chunks_) {
+    const int rows = (int)ch.ntok, nr = ch.r1 - ch.r0;
+    NDL_LK(embed_rows(ids_ + ch.tok0, m.emb, px_, rows, d, m.embed_scale, st));
+    for (const EncLayerDev &E : m.enc) {  // layers.rs:46-93
+      NDL_LK(rms_norm_rows(px_, d, pxn_, d, E.norm, rows, d, st));
+      MatmulOut o;
+      o.y = pqkv_;
+      o.ldy = qkvd;
+      NDL_LK(int4_matmul(pxn_, d, rows, E.qkv.view(), o, st));
+      NDL_LK(qk_norm_rope_rows(pqkv_, rows, tok_pos_ + ch.tok0, E.q_norm, E.k_norm, m.rope_cos, m.rope_sin, m.ad, st));
+      NDL_LK(encoder_attention(pqkv_, ch.rel_off, nr, ch.tmax, patt_, m.ad, st));
+      MatmulOut r;
+      r.y = px_;
+      r.ldy = d;
+      r.epi = EPI_RESID;
+      r.gate = E.gate;
+      NDL_LK(int4_matmul(patt_, qd, rows, E.o.view(), r, st));
+      if (E.ffn) {
+        NDL_LK(rms_norm_rows(px_, d, pxn_, d, E.ffn_norm, rows, d, st));
+        MatmulOut a;
+        a.y = pffn_;
+        a.ldy = c.ffn_dim;
+        a.epi = EPI_ACT;
+        a.act = c.activation;
+        NDL_LK(int4_matmul(pxn_, d, rows, E.gate_up.view(), a, st));
+        MatmulOut f;
+        f.y = px_;
+        f.ldy = d;
+        f.epi = EPI_RESID;
+        f.gate = E.ffn_gate;
+        NDL_LK(int4_matmul(pffn_, c.ffn_dim, rows, E.down.view(), f, st));
+      }
+    }
+    NDL_LK(rms_norm_rows(px_, d, pxn_, d, m.enc_final_norm, rows, d, st));  // model.rs:184-186
+    if (enc_out_)
+      NDL_CK(cudaMemcpyAsync(enc_out_ + ch.tok0 * d, pxn_, (size_t)rows * d * 4, cudaMemcpyDeviceToDevice, st));
+    if (L > 0) {  // fill_cross_kv (model.rs:196-231): all layers' K|V in one matmul
+      MatmulOut o;
+      o.y = kv_planes_ + ch.tok0 * kvd;
+      o.ldy = kvd;
+      o.col_block = kvd;
+      o.block_stride = ttot_ * kvd;
+      const bool fused_norm = (hd == 64) && (kvd % 64 == 0);
+      o.epi = fused_norm ? EPI_KNORM : EPI_STORE;
+      o.vec = m.cross_knorm;
+      NDL_LK(int4_matmul(pxn_, d, rows, m.cross_kv.view(), o, st));
+      if (!fused_norm)
+        for (int l = 0; l < L; ++l)
+          NDL_LK(head_norm_rows(kv_planes_ + (size_t)2 * l * ttot_ * kvd + ch.tok0 * kvd, rows, kvd,
+                                c.num_kv_heads, hd, m.cross_knorm + (size_t)l * hd, st));
+    }
+  }
+  return true;
+}
+
+bool Batch::decode_step(std::string &err, bool capture) {
+  const DevModel &m = *m_;
+  const Config &c = m.cfg;
+  const int B = spec_.n_req, d = c.d_model, hd = c.head_dim(), qd = c.num_heads * hd, kvd = c.num_kv_heads * hd;
+  const int qkvd = qd + 2 * kvd;
+  cudaStream_t st = st_;
+  for (size_t l = 0; l < m.dec.size(); ++l) {  // layers.rs:100-149
+    const DecLayerDev &D = m.dec[l];
+    NDL_LK(rms_norm_rows(x_, d, xn_, d, D.sa_norm, B, d, st));
+    MatmulOut o;
+    o.y = qkv_;
+    o.ldy = qkvd;
+    NDL_LK(int4_matmul(xn_, d, B, D.sa_qkv.view(), o, st));
+    size_t coff = l * (size_t)B * cap_ * kvd;
+    NDL_LK(decoder_self_attention(qkv_, pos_, D.sa_qn, D.sa_kn, m.rope_cos, m.rope_sin, self_k_ + coff,
+                                  self_v_ + coff, cap_, B, att_, m.ad, st));
+    MatmulOut r;
+    r.y = x_;
+    r.ldy = d;
+    r.epi = EPI_RESID;
+    r.gate = D.sa_gate;
+    NDL_LK(int4_matmul(att_, qd, B, D.sa_o.view(), r, st));
+    NDL_LK(rms_norm_rows(x_, d, xn_, d, D.ca_norm, B, d, st));
+    MatmulOut qo;
+    qo.y = q_;
+    qo.ldy = qd;
+    NDL_LK(int4_matmul(xn_, d, B, D.ca_q.view(), qo, st));
+    const float *kp = kv_planes_ + (size_t)2 * l * ttot_ * kvd, *vp = kp + (size_t)ttot_ * kvd;
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    if (time_cross_ && !capture) {
+      NDL_CK(cudaEventCreate(&e0));
+      NDL_CK(cudaEventCreate(&e1));
+      cross_events_.push_back({e0, e1});
+      NDL_CK(cudaEventRecord(e0, st));
+    }
+    NDL_LK(decoder_cross_attention(q_, D.ca_qn, kp, vp, seq_off_, B, att_, m.ad, st, tmax_));
+    if (e1) NDL_CK(cudaEventRecord(e1, st));
+    MatmulOut r2;
+    r2.y = x_;
+    r2.ldy = d;
+    r2.epi = EPI_RESID;
+    r2.gate = D.ca_gate;
+    NDL_LK(int4_matmul(att_, qd, B, D.ca_o.view(), r2, st));
+    if (D.ffn) {
+      NDL_LK(rms_norm_rows(x_, d, xn_, d, D.ffn_norm, B, d, st));
+      MatmulOut a;
+      a.y = ffn_;
+      a.ldy = c.ffn_dim;
+      a.epi = EPI_ACT;
+      a.act = c.activation;
+      NDL_LK(int4_matmul(xn_, d, B, D.gate_up.view(), a, st));
+      MatmulOut f;
+      f.y = x_;
+      f.ldy = d;
+      f.epi = EPI_RESID;
+      f.gate = D.ffn_gate;
+      NDL_LK(int4_matmul(ffn_, c.ffn_dim, B, D.down.view(), f, st));
+    }
+  }
+  NDL_LK(rms_norm_rows(x_, d, h_, d, m.dec_final_norm, B, d, st));  // model.rs:263
+  NDL_LK(head_argmax(h_, B, m.emb, c.vocab_size, d, mask_, W_, logits_, spec_.max_new, pos_, keys_, st));
+  NDL_LK(finish_step(keys_, B, spec_.max_new, (spec_.flags & BATCH_STOP_ON_EOS) ? 1 : 0, out_ids_, lens_, done_,
+                     pos_, n_done_, teacher_, m.emb, x_, d, m.embed_scale, st));
+  return true;
+}
+
+bool Batch::begin(std::string &err) {
+  NDL_CK(cudaSetDevice(m_->device));
+  NDL_CK(cudaSetDevice(m_->device));
+  launches_ = 0;
+  steps_done_ = 0;
+  for (auto &e : cross_events_) {
+    cudaEventDestroy(e.first);
+    cudaEventDestroy(e.second);
+  }
+  cross_events_.clear();
+  if (!reset_decoder(err) || !prefill(err)) return false;
+  use_graph_ = !(spec_.flags & BATCH_NO_GRAPH) && !time_cross_ && spec_.max_new > 0;
+  if (use_graph_ && !graph_) {
+    cudaStream_t st = st_;
+    int64_t before = launches_;
+    NDL_CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+    std::string cerr;
+    bool ok = decode_step(cerr, true);
+    cudaGraph_t g = nullptr;
+    cudaError_t ce = cudaStreamEndCapture(st, &g);
+    if (!ok || ce != cudaSuccess) {
+      if (g) cudaGraphDestroy(g);
+      err = ok ? std::string("graph capture failed: ") + cudaGetErrorString(ce) : cerr;
+      return false;
+    }
+    cudaError_t ie = cudaGraphInstantiate(&graph_, g, 0);
+    cudaGraphDestroy(g);
+    if (ie != cudaSuccess) {
+      err = std::string("graph instantiate failed: ") + cudaGetErrorString(ie);
+      return false;
+    }
+    step_launches_ = launches_ - before;
+    launches_ = before;
+  }
+  return true;
+}
+
+bool Batch::step(std::string &err) {
+  if (steps_done_ >= spec_.max_new) {
+    err = "all decode steps already run";
+    return false;
+  }
+  if (use_graph_) {
+    NDL_CK(cudaGraphLaunch(graph_, st_));
+    launches_ += step_launches_;
+  } else if (!decode_step(err, false)) {
+    return false;
+  }
+  ++steps_done_;
+  return true;
+}
+
+bool Batch::peek(uint32_t *lens, uint8_t *done, uint32_t *ids, std::string &err) {
+  cudaStream_t st = st_;
+  const int B = spec_.n_req;
+  if (lens) NDL_CK(cudaMemcpyAsync(lens, lens_, (size_t)B * 4, cudaMemcpyDeviceToHost, st));
+  if (done) NDL_CK(cudaMemcpyAsync(done, done_, (size_t)B, cudaMemcpyDeviceToHost, st));
+  if (ids) NDL_CK(cudaMemcpyAsync(ids, out_ids_, (size_t)B * spec_.max_new * 4, cudaMemcpyDeviceToHost, st));
+  NDL_CK(cudaStreamSynchronize(st));
+  return true;
+}
+
+bool Batch::run(std::string &err) {
+  if (!begin(err)) return false;
+  const int steps = spec_.max_new;
+  const bool stop = spec_.flags & BATCH_STOP_ON_EOS;
+  unsigned int ndone = 0;
+  for (int s = 0; s < steps; ++s) {
+    if (!step(err)) return false;
+    if (stop && ((s & 7) == 7) && s + 1 < steps) {
+      NDL_CK(cudaMemcpyAsync(&ndone, n_done_, sizeof(ndone), cudaMemcpyDeviceToHost, st_));
+      NDL_CK(cudaStreamSynchronize(st_));
+      if ((int)ndone >= spec_.n_req) break;
+    }
+  }
+  return true;
+}
+
+bool Batch::download(uint32_t *out_ids, uint32_t *out_lens, float *logits, float *enc_out, std::string &err) {
+  NDL_CK(cudaSetDevice(m_->device));
+  cudaStream_t st = st_;
+  const int B = spec_.n_req;
+  const bool dev_out = spec_.flags & BATCH_DEVICE_INPUTS;
+  const cudaMemcpyKind k = dev_out ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost;
+  if (spec_.max_new > 0) {
+    if (out_ids) NDL_CK(cudaMemcpyAsync(out_ids, out_ids_, (size_t)B * spec_.max_new * 4, k, st));
+    if (out_lens) NDL_CK(cudaMemcpyAsync(out_lens, lens_, (size_t)B * 4, k, st));
+    if (logits && logits_)
+      NDL_CK(cudaMemcpyAsync(logits, logits_, (size_t)B * spec_.max_new * m_->cfg.vocab_size * 4, k, st));
+  } else if (out_lens) {
+    if (dev_out)
+      NDL_CK(cudaMemsetAsync(out_lens, 0, (size_t)B * 4, st));
+    else
+      std::memset(out_lens, 0, (size_t)B * 4);
+  }
+  if (enc_out && enc_out_) NDL_CK(cudaMemcpyAsync(enc_out, enc_out_, (size_t)ttot_ * m_->cfg.d_model * 4, k, st));
+  NDL_CK(cudaStreamSynchronize(st));
+  if (!spec_.max_new || !out_lens || dev_out) return true;
+  for (int b = 0; b < B; ++b) out_lens[b] = std::min<uint32_t>(out_lens[b], (uint32_t)spec_.max_new);
+  return true;
+}
+
+bool Batch::collect_cross_timing(std::string &err) {
+  NDL_CK(cudaStreamSynchronize(st_));
+  cross_ms_ = 0.0;
+  cross_n_ = 0;
+  for (auto &e : cross_events_) {
+    float ms = 0.0f;
+    NDL_CK(cudaEventElapsedTime(&ms, e.first, e.second));
+    cross_ms_ += ms;
+    ++cross_n_;
+  }
+  return true;
+}
+
+void shard_requests(const uint64_t *offsets, int n_req, int shards, int32_t *assignment) {
+  // Longest-processing-time-first: cost of a request ~ prefill (T^2 attention
+  // + T projections) plus its decode share (proportional to T for the
+  // cross-attention reads).
+  std::vector<int> order(n_req);
+  std::iota(order.begin(), order.end(), 0);
+  auto cost = [&](int r) {
+    double T = (double)(offsets[r + 1] - offsets[r]);
+    return T * T + 2048.0 * T;
+  };
+  std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return cost(a) > cost(b); });
+  std::vector<double> load(std::max(shards, 1), 0.0);
+  for (int r : order) {
+    int s = (int)(std::min_element(load.begin(), load.end()) - load.begin());
+    assignment[r] = s;
+    load[s] += cost(r);
+  }
+}
+
+}  // namespace ndl

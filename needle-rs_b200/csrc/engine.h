@@ -1,0 +1,191 @@
+// engine.h — device-resident Needle model and the batched greedy engine.
+//
+// Replaces the model + kernel layers of the reference (crates/needle-core:
+// NeedleModel::{new, encode, decode_step}, model.rs:44-265) and the token-ID
+// part of NeedleEngine::run_impl / run_batch (crates/needle-infer/src/
+// engine.rs:142-144, 226-322).  One DevModel lives on one GPU; a Batch holds
+// the per-call device state (prompt IDs, encoder K/V, decoder caches) so
+// concurrent calls on one model never share mutable memory.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "kernels.h"
+#include "safetensors.h"
+
+namespace ndl {
+
+// crates/needle-core/src/config.rs:22-69 (defaults) and :83-103 (validate)
+struct Config {
+  int d_model = 512, num_heads = 8, num_kv_heads = 4, num_layers = 12, num_dec_layers = 8;
+  int vocab_size = 8192, max_enc_len = 1024, max_dec_len = 512, ffn_dim = 2048;
+  bool no_feedforward = true;
+  int activation = ACT_DRELU;
+  float rope_theta = 10000.0f;
+  int head_dim() const { return d_model / num_heads; }
+  const char *validate() const;
+};
+
+struct Lin {  // packed INT4 weight on the device
+  uint8_t *w = nullptr;
+  float *s = nullptr;
+  int K = 0, N = 0, G = 0, gs = 0;
+  Int4Weight view() const { return Int4Weight{w, s, K, N, G, gs}; }
+};
+
+struct EncLayerDev {
+  Lin qkv, o;                     // qkv: wq|wk|wv fused along N
+  float *q_norm = nullptr, *k_norm = nullptr, *norm = nullptr;
+  float gate = 0.0f;              // sigmoid(self_attn_gate), host-computed
+  bool ffn = false;
+  Lin gate_up, down;              // gate_up: (gate_i, up_i) interleaved along N
+  float *ffn_norm = nullptr;
+  float ffn_gate = 0.0f;
+};
+
+struct DecLayerDev {
+  Lin sa_qkv, sa_o, ca_q, ca_o;
+  float *sa_qn = nullptr, *sa_kn = nullptr, *sa_norm = nullptr;
+  float *ca_qn = nullptr, *ca_norm = nullptr;
+  float sa_gate = 0.0f, ca_gate = 0.0f;
+  bool ffn = false;
+  Lin gate_up, down;
+  float *ffn_norm = nullptr;
+  float ffn_gate = 0.0f;
+};
+
+struct DevModel {
+  int device = 0;
+  Config cfg;
+  AttnDims ad;
+  float embed_scale = 0.0f;
+  float *emb = nullptr;        // [V][d] f32
+  bool emb_bf16_exact = false;
+  std::vector<EncLayerDev> enc;
+  std::vector<DecLayerDev> dec;
+  Lin cross_kv;                // all decoder layers' cross wk|wv: [d, L*2*KVH*HD]
+  float *cross_knorm = nullptr;  // [L][HD]
+  float *enc_final_norm = nullptr, *dec_final_norm = nullptr;
+  float *rope_cos = nullptr, *rope_sin = nullptr;  // [rope_len][HD/2]
+  int rope_len = 0;
+  cudaStream_t stream = nullptr;
+  std::vector<void *> allocs;
+  size_t weight_bytes = 0;
+
+  ~DevModel();
+};
+
+// Loads a SafeTensors buffer onto `device` (engine.rs:578-792 semantics:
+// config from __metadata__, missing tensors become zeros, F32 projection
+// weights are quantized on load by the device packer).
+std::unique_ptr<DevModel> load_model(std::vector<uint8_t> raw, int device, std::string &err);
+
+enum BatchFlags : uint32_t {
+  BATCH_STOP_ON_EOS = 1u,     // engine.rs:306-308: stop a request at EOS
+  BATCH_DEVICE_INPUTS = 2u,   // prompt ids / masks are device pointers
+  BATCH_NO_GRAPH = 4u,        // launch each decode step eagerly
+};
+
+struct BatchSpec {
+  const uint32_t *ids = nullptr;       // concatenated prompts
+  const uint64_t *offsets = nullptr;   // host, [n_req + 1]
+  int n_req = 0;
+  int max_new = 0;
+  const uint64_t *mask = nullptr;      // [n_req][max_new][ceil(V/64)] or NULL
+  const uint32_t *teacher = nullptr;   // host [n_req][max_new] teacher-forced decoder inputs, or NULL
+  uint32_t flags = 0;
+  bool want_logits = false;            // keep masked logits [n_req][max_new][V]
+  bool want_enc_out = false;           // keep the final encoder hidden [sum T][d]
+};
+
+// Per-call device state; prepare() uploads inputs and allocates, run()
+// executes prefill + max_new decode steps, download() copies results out.
+class Batch {
+ public:
+  explicit Batch(DevModel *m);
+  ~Batch();
+  bool prepare(const BatchSpec &spec, std::string &err);
+  // run() = begin() + every decode step (with an early exit once all
+  // requests hit EOS under BATCH_STOP_ON_EOS).  Work is left enqueued on
+  // stream(); download() synchronises.  A batch may run again: each run
+  // starts from the uploaded prompts with a fresh decoder state.
+  bool run(std::string &err);
+  // Stepwise use (streaming): begin() runs the prefill, step() enqueues one
+  // decode step, peek() synchronises and copies lens/done/tokens to the host.
+  bool begin(std::string &err);
+  bool step(std::string &err);
+  bool peek(uint32_t *lens, uint8_t *done, uint32_t *ids, std::string &err);
+  bool download(uint32_t *out_ids, uint32_t *out_lens, float *logits, float *enc_out, std::string &err);
+  cudaStream_t stream() const { return st_; }
+  // Number of kernels one run() launches (reported by the benchmark).
+  int64_t kernels_launched() const { return launches_; }
+  // Optional per-kernel timing of the cross-attention launches (ms total,
+  // launch count) recorded with CUDA events on the model's stream.
+  void enable_cross_timing(bool on) { time_cross_ = on; }
+  bool collect_cross_timing(std::string &err);
+  double cross_ms() const { return cross_ms_; }
+  int64_t cross_launches() const { return cross_n_; }
+
+ private:
+  bool prefill(std::string &err);
+  bool reset_decoder(std::string &err);
+  bool decode_step(std::string &err, bool capture);
+  template <class T>
+  T *alloc(size_t n, std::string &err);
+
+  DevModel *m_;
+  cudaStream_t st_ = nullptr;  // each call has its own stream: calls on one model run concurrently
+  BatchSpec spec_{};
+  std::vector<uint64_t> off_h_;
+  int64_t ttot_ = 0;
+  int tmax_ = 0, cap_ = 0, W_ = 0;
+  std::vector<void *> bufs_;
+  // inputs
+  uint32_t *ids_ = nullptr;
+  int64_t *seq_off_ = nullptr;     // [n_req+1] absolute token offsets
+  int32_t *tok_pos_ = nullptr;     // [ttot] position inside its request
+  uint64_t *mask_ = nullptr;
+  uint32_t *teacher_ = nullptr;
+  // prefill chunks
+  struct Chunk {
+    int r0, r1;
+    int64_t tok0, ntok;
+    int tmax;
+    int64_t *rel_off;  // device [r1-r0+1], chunk-relative offsets
+  };
+  std::vector<Chunk> chunks_;
+  int64_t chunk_tok_max_ = 0;
+  float *px_ = nullptr, *pxn_ = nullptr, *pqkv_ = nullptr, *patt_ = nullptr, *pffn_ = nullptr;
+  // encoder outputs
+  float *kv_planes_ = nullptr;     // [2L][ttot][KVH*HD]  (K0 V0 K1 V1 ...)
+  float *enc_out_ = nullptr;       // [ttot][d] when requested
+  // decoder state
+  float *self_k_ = nullptr, *self_v_ = nullptr;  // [L][B][cap][KVH*HD]
+  float *x_ = nullptr, *xn_ = nullptr, *qkv_ = nullptr, *att_ = nullptr, *q_ = nullptr, *h_ = nullptr, *ffn_ = nullptr;
+  unsigned long long *keys_ = nullptr;
+  int32_t *pos_ = nullptr;
+  uint32_t *out_ids_ = nullptr, *lens_ = nullptr;
+  uint8_t *done_ = nullptr;
+  unsigned int *n_done_ = nullptr;
+  float *logits_ = nullptr;
+  cudaGraphExec_t graph_ = nullptr;
+  bool use_graph_ = false;
+  uint32_t *first_ids_ = nullptr;
+  int steps_done_ = 0;
+  int64_t launches_ = 0, step_launches_ = 0;
+  bool time_cross_ = false;
+  double cross_ms_ = 0.0;
+  int64_t cross_n_ = 0;
+  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> cross_events_;
+};
+
+// Splits n requests with lengths len[] into `shards` groups of near-equal
+// cost (cost ~ T^2 attention + T projections + decode), longest-first
+// greedy (LPT).  assignment[i] = shard of request i.
+void shard_requests(const uint64_t *offsets, int n_req, int shards, int32_t *assignment);
+
+}  // namespace ndl

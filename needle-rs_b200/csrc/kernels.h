@@ -1,0 +1,134 @@
+// kernels.h — host-side launchers of the needle sm_100a kernels.
+//
+// All pointers are device pointers.  Every launcher enqueues on `stream` and
+// returns the launch status (cudaSuccess or the error cudaGetLastError saw).
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace ndl {
+
+constexpr uint32_t kEosId = 1;  // tokenizer.rs:23 EOS_ID, also the decoder start token
+
+// Packed INT4 weight in the reference layout (quant.rs:45-58):
+//   w[pair * N + n]: low nibble = row 2*pair, high nibble = row 2*pair+1
+//   s[g * N + n]:    f32 scale of group g = row / gs, gs = min(32, K)
+struct Int4Weight {
+  const uint8_t *w = nullptr;
+  const float *s = nullptr;
+  int K = 0;   // in_feat (unpadded)
+  int N = 0;   // out_feat (of the logical matrix; 2x each part in paired mode)
+  int G = 0;   // num_groups
+  int gs = 0;  // group size = min(32, K)
+  // Paired mode (w2 != NULL): the logical weight interleaves the columns of
+  // two same-shape weights, column 2i = w column i, 2i+1 = w2 column i
+  // (gate / up of ffn.rs:19-56, each [K][N/2] in the reference layout).
+  const uint8_t *w2 = nullptr;
+  const float *s2 = nullptr;
+};
+
+enum Epilogue : int {
+  EPI_STORE = 0,  // y = acc
+  EPI_RESID = 1,  // y += gate * acc           (layers.rs:70-74 gated residual)
+  EPI_ACT = 2,    // columns interleaved (gate_i, up_i) -> y[i] = act(gate_i, up_i)
+  EPI_KNORM = 3,  // y = acc, then per-64-column ZCRMSNorm with `vec` on blocks
+                  // whose column-block index is even (the K half of K|V pairs)
+};
+
+enum Activation : int { ACT_DRELU = 0, ACT_SWIGLU = 1, ACT_GELU = 2 };
+
+struct MatmulOut {
+  float *y = nullptr;
+  int64_t ldy = 0;           // row stride of y (floats)
+  int col_block = 0;         // 0: plain; else columns are split into blocks of
+  int64_t block_stride = 0;  //   col_block, block b written at y + b*block_stride
+  int epi = EPI_STORE;
+  float gate = 0.0f;
+  int act = ACT_DRELU;
+  const float *vec = nullptr;  // EPI_KNORM: k_norm scale [64]
+};
+
+// Y[M, N] (epilogue) X[M, K] @ W.  x row stride ldx (floats).
+cudaError_t int4_matmul(const float *x, int64_t ldx, int M, const Int4Weight &W, const MatmulOut &o,
+                        cudaStream_t stream);
+
+// Device packing / unpacking (quant.rs:63-155), bit-exact with the reference.
+cudaError_t int4_quantize(const float *w, int K, int N, uint8_t *data, float *scales, cudaStream_t st);
+cudaError_t int4_dequantize(const uint8_t *data, const float *scales, int K, int N, int G, float *out,
+                            cudaStream_t st);
+
+// out[r, :] = ZCRMSNorm(x[r, :], scale)   (norm.rs:23-30), d = row length.
+cudaError_t rms_norm_rows(const float *x, int64_t ldx, float *out, int64_t ldo, const float *scale, int rows,
+                          int d, cudaStream_t st);
+
+// x[t, :] = E[ids[t], :] * embed_scale  (model.rs:78-85, 158-164)
+cudaError_t embed_rows(const uint32_t *ids, const float *emb, float *x, int rows, int d, float embed_scale,
+                       cudaStream_t st);
+
+struct AttnDims {
+  int H = 8, KVH = 4, HD = 64;
+  float scale = 0.125f;  // powf(hd, -0.5) computed on the host (attn.rs:142)
+};
+
+// Largest dynamic shared memory any kernel here is allowed to request.
+constexpr int kMaxDynSmem = 200 * 1024;
+
+// Set per-device kernel attributes.  Call once per device, with it current.
+cudaError_t init_kernels();
+cudaError_t init_matmul_kernels();
+cudaError_t init_attention_kernels();
+cudaError_t init_head_kernels();
+
+// Encoder prefill: in-place per-head ZCRMSNorm + RoPE (offset 0) on the
+// Q|K|V rows produced by the fused projection: row t has Q [H*HD], K [KVH*HD],
+// V [KVH*HD].  pos[t] = position of token t inside its request.
+cudaError_t qk_norm_rope_rows(float *qkv, int rows, const int32_t *pos, const float *q_norm, const float *k_norm,
+                              const float *rope_cos, const float *rope_sin, AttnDims a, cudaStream_t st);
+
+// Bidirectional encoder attention over ragged requests (attn.rs:189-273).
+// qkv rows as above; seq_off[r]..seq_off[r+1] = tokens of request r.
+// out[t, H*HD].  max_len = the longest request.
+cudaError_t encoder_attention(const float *qkv, const int64_t *seq_off, int n_req, int max_len, float *out,
+                              AttnDims a, cudaStream_t st);
+
+// Decoder self-attention for one new token per request (attn.rs:100-183):
+// q|k|v from qkv rows [B, (H+2*KVH)*HD]; ZCRMSNorm + RoPE at position
+// step[b], append k, v to the caches (saturating at cap), attend over the
+// cache.  kc/vc: [B, cap, KVH*HD].  out: [B, H*HD].
+cudaError_t decoder_self_attention(const float *qkv, const int32_t *step, const float *q_norm,
+                                   const float *k_norm, const float *rope_cos, const float *rope_sin, float *kc,
+                                   float *vc, int cap, int B, float *out, AttnDims a, cudaStream_t st);
+
+// Decoder cross-attention (attn.rs:281-337): q [B, H*HD] (q_norm applied
+// here), K/V of request b at rows seq_off[b].. of kplane / vplane
+// [*, KVH*HD].  out: [B, H*HD].
+cudaError_t decoder_cross_attention(const float *q, const float *q_norm, const float *kplane,
+                                    const float *vplane, const int64_t *seq_off, int B, float *out, AttnDims a,
+                                    cudaStream_t st, int max_len);
+
+// Output head (model.rs:89-149) + additive mask (engine.rs:294-297) + argmax
+// (engine.rs:299-304), fused.  h: [B, d]; emb: [V, d].  Request b is at step
+// pos[b]; its mask bitmap (bit v set = allowed) is mask[(b*max_new +
+// pos[b]) * mask_words ...] (NULL = unconstrained) and its masked logits, when
+// `logits` is set, go to logits[(b*max_new + pos[b]) * V ...].  keys[b] must
+// be zero on entry and receives the packed (logit key, index) maximum.
+cudaError_t head_argmax(const float *h, int B, const float *emb, int V, int d, const uint64_t *mask, int mask_words,
+                        float *logits, int max_new, const int32_t *pos, unsigned long long *keys, cudaStream_t st);
+
+// After head_argmax, for request b at step s = pos[b]: next = index of
+// keys[b]; unless the request is done, append next to out_ids[b*max_new +
+// lens[b]] (or, with stop_on_eos and next == EOS, mark it done and count it
+// in n_done); clear keys[b]; pos[b] = s + 1; and embed the decoder input of
+// step s+1 into x: next, or teacher[b*max_new + s + 1] when teacher is set
+// (teacher forcing for parity checks).
+cudaError_t finish_step(unsigned long long *keys, int B, int max_new, int stop_on_eos, uint32_t *out_ids,
+                        uint32_t *lens, uint8_t *done, int32_t *pos, unsigned int *n_done, const uint32_t *teacher,
+                        const float *emb, float *x, int d, float embed_scale, cudaStream_t st);
+
+// Per-head ZCRMSNorm (no RoPE) of `heads` consecutive HD-wide heads in each of
+// `rows` rows of stride ld (the cross-attention k_norm of fill_cross_kv,
+// model.rs:211-219, for head dims the fused matmul epilogue does not cover).
+cudaError_t head_norm_rows(float *x, int rows, int64_t ld, int heads, int HD, const float *scale, cudaStream_t st);
+
+}  // namespace ndl

@@ -1,3 +1,4 @@
+import importlib.util
 import os
 import sys
 
@@ -7,6 +8,22 @@ for p in (ROOT, os.path.join(ROOT, "oracle")):
         sys.path.insert(0, p)
 
 GOLDEN = os.path.join(ROOT, "tests", "golden")
+PKG_DIR = os.path.join(ROOT, "needle-rs_b200")
+
+
+def load_pkg(name="needle_b200", file="__init__.py"):
+    """Import a module of the needle-rs_b200 package by path."""
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(name, os.path.join(PKG_DIR, file))
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+# Logit tolerance of the GPU path against the oracle: |gpu - ref| <= ATOL + RTOL * |ref|
+RTOL, ATOL = 1e-3, 1e-4
 
 
 def pytest_configure(config):

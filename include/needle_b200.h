@@ -74,11 +74,16 @@ int needle_batch_results(NeedleBatch *batch, uint32_t *out_ids, uint32_t *out_le
 void *needle_batch_stream(NeedleBatch *batch);
 /* Kernels the last needle_batch_run launched. */
 int64_t needle_batch_kernel_launches(NeedleBatch *batch);
-/* Record CUDA events around every decoder cross-attention launch of later
- * runs (eager launches); needle_batch_cross_attention_ms reports the summed
- * device time and the launch count of the last run. */
-int needle_batch_time_cross_attention(NeedleBatch *batch, int enable);
-int needle_batch_cross_attention_ms(NeedleBatch *batch, double *ms_total, int64_t *launches);
+/* Time one kernel class in later runs: CUDA events around each of its
+ * launches on the batch's stream (decode steps then launch eagerly, without
+ * a CUDA graph).  Classes: 0 none, 1 decoder cross-attention, 2 prefill
+ * INT4 matmuls, 3 decode INT4 matmuls, 4 output head, 5 encoder attention.
+ * needle_batch_kernel_timing reports, for the last run, the summed device
+ * time, the launch count and the algorithmic flops and bytes of those
+ * launches (bytes: every operand read once and every result written once). */
+int needle_batch_time_kernel(NeedleBatch *batch, int kernel_class);
+int needle_batch_kernel_timing(NeedleBatch *batch, double *ms_total, int64_t *launches, double *flops,
+                               double *bytes);
 void needle_batch_free(NeedleBatch *batch);
 
 /* Splits requests into `shards` groups of near-equal cost, longest first

@@ -69,8 +69,8 @@ def lib():
             "needle_batch_results": (I, [P, P, P]),
             "needle_batch_stream": (P, [P]),
             "needle_batch_kernel_launches": (I64, [P]),
-            "needle_batch_time_cross_attention": (I, [P, I]),
-            "needle_batch_cross_attention_ms": (I, [P, P, P]),
+            "needle_batch_time_kernel": (I, [P, I]),
+            "needle_batch_kernel_timing": (I, [P, P, P, P, P]),
             "needle_batch_free": (None, [P]),
             "needle_shard_requests": (I, [P, S, I, P]),
             "needle_debug_forward": (I, [P, P, S, P, S, P, P]),
@@ -250,14 +250,16 @@ class Batch:
     def kernel_launches(self):
         return int(lib().needle_batch_kernel_launches(self._b))
 
-    def time_cross_attention(self, on=True):
-        _check(lib().needle_batch_time_cross_attention(self._b, 1 if on else 0))
+    def time_kernel(self, kernel_class):
+        """0 none, 1 cross-attention, 2 prefill matmul, 3 decode matmul, 4 head, 5 encoder attention."""
+        _check(lib().needle_batch_time_kernel(self._b, int(kernel_class)))
 
-    def cross_attention_ms(self):
-        ms = C.c_double()
+    def kernel_timing(self):
+        """(ms_total, launches, flops, bytes) of the timed class over the last run."""
+        ms, fl, by = C.c_double(), C.c_double(), C.c_double()
         n = C.c_int64()
-        _check(lib().needle_batch_cross_attention_ms(self._b, C.byref(ms), C.byref(n)))
-        return ms.value, n.value
+        _check(lib().needle_batch_kernel_timing(self._b, C.byref(ms), C.byref(n), C.byref(fl), C.byref(by)))
+        return ms.value, n.value, fl.value, by.value
 
     def close(self):
         if getattr(self, "_b", None):
@@ -269,6 +271,9 @@ class Batch:
             self.close()
         except Exception:
             pass
+
+
+TIME_CROSS_ATTENTION, TIME_PREFILL_MATMUL, TIME_DECODE_MATMUL, TIME_HEAD, TIME_ENCODER_ATTENTION = 1, 2, 3, 4, 5
 
 
 def shard_requests(offsets, shards):

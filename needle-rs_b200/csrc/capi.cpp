@@ -29,7 +29,7 @@ struct NeedleBatch {
   std::unique_ptr<Batch> batch;
   BatchSpec spec;
   std::vector<uint64_t> offsets;
-  bool time_cross = false;
+  int timed_cls = 0;
 };
 
 namespace {
@@ -270,7 +270,7 @@ int needle_batch_run(NeedleBatch *nb) {
   if (!nb) return -1;
   clear_err();
   std::string err;
-  nb->batch->enable_cross_timing(nb->time_cross);
+  nb->batch->set_timed_class(nb->timed_cls);
   if (!nb->batch->run(err)) {
     set_err(err);
     return -1;
@@ -302,21 +302,24 @@ void *needle_batch_stream(NeedleBatch *nb) { return nb ? (void *)nb->batch->stre
 
 int64_t needle_batch_kernel_launches(NeedleBatch *nb) { return nb ? nb->batch->kernels_launched() : -1; }
 
-int needle_batch_time_cross_attention(NeedleBatch *nb, int enable) {
-  if (!nb) return -1;
-  nb->time_cross = enable != 0;
+int needle_batch_time_kernel(NeedleBatch *nb, int kernel_class) {
+  if (!nb || kernel_class < 0 || kernel_class > 5) return -1;
+  nb->timed_cls = kernel_class;
   return 0;
 }
 
-int needle_batch_cross_attention_ms(NeedleBatch *nb, double *ms, int64_t *n) {
+int needle_batch_kernel_timing(NeedleBatch *nb, double *ms_total, int64_t *launches, double *flops,
+                               double *bytes) {
   if (!nb) return -1;
   std::string err;
-  if (!nb->batch->collect_cross_timing(err)) {
+  if (!nb->batch->collect_timing(err)) {
     set_err(err);
     return -1;
   }
-  if (ms) *ms = nb->batch->cross_ms();
-  if (n) *n = nb->batch->cross_launches();
+  if (ms_total) *ms_total = nb->batch->timed_ms();
+  if (launches) *launches = nb->batch->timed_launches();
+  if (flops) *flops = nb->batch->timed_flops();
+  if (bytes) *bytes = nb->batch->timed_bytes();
   return 0;
 }
 
@@ -385,6 +388,55 @@ static bool ensure_kernels() {
   return true;
 }
 
+static int *device_err_flag() {
+  static std::mutex mu;
+  static std::vector<int *> flags;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  std::lock_guard<std::mutex> g(mu);
+  if ((int)flags.size() <= dev) flags.resize(dev + 1, nullptr);
+  if (!flags[dev]) {
+    if (cudaMalloc(&flags[dev], sizeof(int)) != cudaSuccess || cudaMemset(flags[dev], 0, sizeof(int)) != cudaSuccess)
+      flags[dev] = nullptr;
+  }
+  return flags[dev];
+}
+
+// Y = x @ W with the tensor-core GEMM for tall x (W and x staged as bf16
+// hi/lo planes in per-call device buffers) and the CUDA-core kernels below
+// kTcMinRows rows.
+static bool matmul_any(const float *x, int64_t ldx, int M, const Int4Weight &W, const MatmulOut &o, cudaStream_t st) {
+  const bool aligned = ((uintptr_t)o.y % 16 == 0) && (o.ldy % 4 == 0);
+  if (M < kTcMinRows || !aligned) return dev_check(int4_matmul(x, ldx, M, W, o, st));
+  int *flag = device_err_flag();
+  if (!flag) {
+    set_err("device error flag allocation failed");
+    return false;
+  }
+  const int Kp = tc_padded_k(W.K);
+  void *buf = nullptr;
+  size_t wbytes = (size_t)W.N * Kp * 2, xbytes = (size_t)M * Kp * 2;
+  if (!dev_check(cudaMallocAsync(&buf, 2 * wbytes + 2 * xbytes + 1024, st))) return false;
+  char *b = (char *)(((uintptr_t)buf + 255) & ~(uintptr_t)255);
+  void *wh = b, *wl = b + wbytes, *xh = b + 2 * wbytes, *xl = b + 2 * wbytes + xbytes;
+  TcPlanes A, B;
+  bool ok = dev_check(tc_make_planes(wh, wl, W.N, Kp, 128, B)) && dev_check(tc_make_planes(xh, xl, M, Kp, 128, A)) &&
+            dev_check(tc_prep_weight(W, Kp, wh, wl, st)) && dev_check(tc_split_rows(x, ldx, M, W.K, Kp, xh, xl, st)) &&
+            dev_check(tc_matmul(A, M, B, W.N, o, flag, st));
+  cudaFreeAsync(buf, st);
+  if (!ok) return false;
+  int kerr = 0;
+  if (!dev_check(cudaMemcpyAsync(&kerr, flag, sizeof(int), cudaMemcpyDeviceToHost, st)) ||
+      !dev_check(cudaStreamSynchronize(st)))
+    return false;
+  if (kerr) {
+    cudaMemset(flag, 0, sizeof(int));
+    set_err("a tensor-core GEMM wait timed out");
+    return false;
+  }
+  return true;
+}
+
 int needle_int4_matmul(const float *x, size_t M, size_t K, const uint8_t *w, const float *s, size_t N, size_t G,
                        float *y, void *stream) {
   clear_err();
@@ -398,7 +450,7 @@ int needle_int4_matmul(const float *x, size_t M, size_t K, const uint8_t *w, con
   MatmulOut o;
   o.y = y;
   o.ldy = (int64_t)N;
-  return dev_check(int4_matmul(x, (int64_t)K, (int)M, W, o, (cudaStream_t)stream)) ? 0 : -1;
+  return matmul_any(x, (int64_t)K, (int)M, W, o, (cudaStream_t)stream) ? 0 : -1;
 }
 
 int needle_int4_quantize(const float *w, size_t K, size_t N, uint8_t *data, float *scales, void *stream) {
@@ -445,13 +497,13 @@ int needle_ffn_forward(const float *x, size_t T, size_t d, size_t ff, const uint
   a.ldy = (int64_t)ff;
   a.epi = EPI_ACT;
   a.act = act;
-  bool ok = dev_check(int4_matmul(x, (int64_t)d, (int)T, gu, a, st));
+  bool ok = matmul_any(x, (int64_t)d, (int)T, gu, a, st);
   if (ok) {
     Int4Weight dn{dd, ds, (int)ff, (int)d, G2, gsd};
     MatmulOut o;
     o.y = out;
     o.ldy = (int64_t)d;
-    ok = dev_check(int4_matmul(hid, (int64_t)ff, (int)T, dn, o, st));
+    ok = matmul_any(hid, (int64_t)ff, (int)T, dn, o, st);
   }
   cudaFreeAsync(hid, st);
   return ok ? 0 : -1;

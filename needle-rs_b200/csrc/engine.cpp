@@ -7,6 +7,8 @@
 #include <cstring>
 #include <numeric>
 
+#include <cuda_bf16.h>
+
 namespace ndl {
 
 #define NDL_CK(call)                                                                 \
@@ -222,7 +224,17 @@ struct Loader {
     l.N = q.N;
     l.G = q.G;
     l.gs = q.gs;
-    return upload(l.w, q.data.data(), q.data.size()) && upload(l.s, q.scales.data(), q.scales.size());
+    if (!upload(l.w, q.data.data(), q.data.size()) || !upload(l.s, q.scales.data(), q.scales.size())) return false;
+    // bf16 hi/lo staging planes for the tensor-core GEMM
+    const int Kp = tc_padded_k(l.K);
+    __nv_bfloat16 *hi = nullptr, *lo = nullptr;
+    if (!dalloc(hi, (size_t)l.N * Kp) || !dalloc(lo, (size_t)l.N * Kp)) return false;
+    NDL_CK(tc_prep_weight(l.view(), Kp, hi, lo, m.stream));
+    NDL_CK(cudaStreamSynchronize(m.stream));
+    l.tc_hi = hi;
+    l.tc_lo = lo;
+    l.tc_ready = tc_make_planes(hi, lo, l.N, Kp, 128, l.tc) == cudaSuccess;
+    return true;
   }
 };
 
@@ -314,6 +326,11 @@ std::unique_ptr<DevModel> load_model(std::vector<uint8_t> raw, int device, std::
     cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &thr);
   }
   Loader L{st, *m, err};
+  if (!L.dalloc(m->kerr, 1)) return nullptr;
+  if (cudaMemset(m->kerr, 0, sizeof(int)) != cudaSuccess) {
+    err = "cudaMemset failed";
+    return nullptr;
+  }
   std::vector<float> emb;
   if (!st.get_f32("embedding", emb)) {
     err = "missing embedding tensor";
@@ -441,9 +458,10 @@ Batch::~Batch() {
   cudaGetDevice(&prev);
   cudaSetDevice(m_->device);
   if (graph_) cudaGraphExecDestroy(graph_);
-  for (auto &e : cross_events_) {
-    cudaEventDestroy(e.first);
-    cudaEventDestroy(e.second);
+  if (st_) cudaStreamSynchronize(st_);
+  for (auto &e : timed_) {
+    cudaEventDestroy(e.a);
+    cudaEventDestroy(e.b);
   }
   if (st_) {
     for (void *p : bufs_) cudaFreeAsync(p, st_);
@@ -580,6 +598,25 @@ bool Batch::prepare(const BatchSpec &spec, std::string &err) {
     return false;
   if (!c.no_feedforward && !(pffn_ = alloc<float>(ct * c.ffn_dim, err))) return false;
   if (L > 0 && !(kv_planes_ = alloc<float>((size_t)2 * L * ttot_ * kvd, err))) return false;
+  {  // tensor-core staging planes, shared by every batched GEMM of the call
+    const int64_t rows = std::max<int64_t>(ct, B);
+    std::vector<int> kps = {tc_padded_k(d), tc_padded_k(qd)};
+    if (!c.no_feedforward) kps.push_back(tc_padded_k(c.ffn_dim));
+    int kmax = *std::max_element(kps.begin(), kps.end());
+    if (rows >= kTcMinRows) {
+      if (!(tc_hi_ = alloc<__nv_bfloat16>((size_t)rows * kmax, err)) ||
+          !(tc_lo_ = alloc<__nv_bfloat16>((size_t)rows * kmax, err)))
+        return false;
+      tc_maps_.clear();
+      for (int kp : kps) {
+        bool have = false;
+        for (auto &t : tc_maps_) have |= t.Kp == kp;
+        if (have) continue;
+        TcPlanes t;
+        if (tc_make_planes(tc_hi_, tc_lo_, (int)rows, kp, 128, t) == cudaSuccess) tc_maps_.push_back(t);
+      }
+    }
+  }
   if (spec.want_enc_out && !(enc_out_ = alloc<float>((size_t)ttot_ * d, err))) return false;
 
   // decoder state
@@ -627,6 +664,48 @@ bool Batch::reset_decoder(std::string &err) {
     }                                                                                \
   } while (0)
 
+bool Batch::tbegin(int cls, bool capture, cudaEvent_t &a, std::string &err) {
+  a = nullptr;
+  if (capture || cls != timed_cls_) return true;
+  NDL_CK(cudaEventCreate(&a));
+  NDL_CK(cudaEventRecord(a, st_));
+  return true;
+}
+
+bool Batch::tend(cudaEvent_t a, double flops, double bytes, std::string &err) {
+  if (!a) return true;
+  cudaEvent_t b;
+  NDL_CK(cudaEventCreate(&b));
+  NDL_CK(cudaEventRecord(b, st_));
+  timed_.push_back({a, b, flops, bytes});
+  return true;
+}
+
+namespace {
+// Algorithmic work of Y[M,N] = X[M,K] @ W (INT4 + f32 scales, f32 in/out).
+inline double mm_flops(int M, const Lin &w) { return 2.0 * M * w.N * (double)w.K; }
+inline double mm_bytes(int M, const Lin &w) {
+  return (double)w.G * w.gs / 2 * w.N + (double)w.G * w.N * 4 + 4.0 * M * w.K + 4.0 * M * w.N;
+}
+}  // namespace
+
+bool Batch::mm(int cls, bool capture, const float *x, int64_t ldx, int M, const Lin &w, const MatmulOut &o,
+               std::string &err) {
+  cudaEvent_t a;
+  if (!tbegin(cls, capture, a, err)) return false;
+  const TcPlanes *ap = nullptr;
+  if (M >= kTcMinRows && w.tc_ready && (!o.col_block || o.col_block % 64 == 0))
+    for (auto &t : tc_maps_)
+      if (t.Kp == w.tc.Kp && M <= t.rows) ap = &t;
+  if (ap) {
+    NDL_LK(tc_split_rows(x, ldx, M, w.K, ap->Kp, tc_hi_, tc_lo_, st_));
+    NDL_LK(tc_matmul(*ap, M, w.tc, w.N, o, m_->kerr, st_));
+  } else {
+    NDL_LK(int4_matmul(x, ldx, M, w.view(), o, st_));
+  }
+  return tend(a, mm_flops(M, w), mm_bytes(M, w), err);
+}
+
 bool Batch::prefill(std::string &err) {
   const DevModel &m = *m_;
   const Config &c = m.cfg;
@@ -641,15 +720,22 @@ bool Batch::prefill(std::string &err) {
       MatmulOut o;
       o.y = pqkv_;
       o.ldy = qkvd;
-      NDL_LK(int4_matmul(pxn_, d, rows, E.qkv.view(), o, st));
+      if (!mm(TIME_PREFILL_MATMUL, false, pxn_, d, rows, E.qkv, o, err)) return false;
       NDL_LK(qk_norm_rope_rows(pqkv_, rows, tok_pos_ + ch.tok0, E.q_norm, E.k_norm, m.rope_cos, m.rope_sin, m.ad, st));
-      NDL_LK(encoder_attention(pqkv_, ch.rel_off, nr, ch.tmax, patt_, m.ad, st));
+      {
+        cudaEvent_t ev;
+        if (!tbegin(TIME_ENCODER_ATTENTION, false, ev, err)) return false;
+        NDL_LK(encoder_attention(pqkv_, ch.rel_off, nr, ch.tmax, patt_, m.ad, st));
+        double Tq = 0.0;  // sum of T^2 over the chunk's requests
+        for (int r = ch.r0; r < ch.r1; ++r) Tq += std::pow((double)(off_h_[r + 1] - off_h_[r]), 2.0);
+        if (!tend(ev, 4.0 * Tq * c.num_heads * hd, (double)rows * (qkvd + qd) * 4, err)) return false;
+      }
       MatmulOut r;
       r.y = px_;
       r.ldy = d;
       r.epi = EPI_RESID;
       r.gate = E.gate;
-      NDL_LK(int4_matmul(patt_, qd, rows, E.o.view(), r, st));
+      if (!mm(TIME_PREFILL_MATMUL, false, patt_, qd, rows, E.o, r, err)) return false;
       if (E.ffn) {
         NDL_LK(rms_norm_rows(px_, d, pxn_, d, E.ffn_norm, rows, d, st));
         MatmulOut a;
@@ -657,13 +743,13 @@ bool Batch::prefill(std::string &err) {
         a.ldy = c.ffn_dim;
         a.epi = EPI_ACT;
         a.act = c.activation;
-        NDL_LK(int4_matmul(pxn_, d, rows, E.gate_up.view(), a, st));
+        if (!mm(TIME_PREFILL_MATMUL, false, pxn_, d, rows, E.gate_up, a, err)) return false;
         MatmulOut f;
         f.y = px_;
         f.ldy = d;
         f.epi = EPI_RESID;
         f.gate = E.ffn_gate;
-        NDL_LK(int4_matmul(pffn_, c.ffn_dim, rows, E.down.view(), f, st));
+        if (!mm(TIME_PREFILL_MATMUL, false, pffn_, c.ffn_dim, rows, E.down, f, err)) return false;
       }
     }
     NDL_LK(rms_norm_rows(px_, d, pxn_, d, m.enc_final_norm, rows, d, st));  // model.rs:184-186
@@ -678,7 +764,7 @@ bool Batch::prefill(std::string &err) {
       const bool fused_norm = (hd == 64) && (kvd % 64 == 0);
       o.epi = fused_norm ? EPI_KNORM : EPI_STORE;
       o.vec = m.cross_knorm;
-      NDL_LK(int4_matmul(pxn_, d, rows, m.cross_kv.view(), o, st));
+      if (!mm(TIME_PREFILL_MATMUL, false, pxn_, d, rows, m.cross_kv, o, err)) return false;
       if (!fused_norm)
         for (int l = 0; l < L; ++l)
           NDL_LK(head_norm_rows(kv_planes_ + (size_t)2 * l * ttot_ * kvd + ch.tok0 * kvd, rows, kvd,
@@ -700,7 +786,7 @@ bool Batch::decode_step(std::string &err, bool capture) {
     MatmulOut o;
     o.y = qkv_;
     o.ldy = qkvd;
-    NDL_LK(int4_matmul(xn_, d, B, D.sa_qkv.view(), o, st));
+    if (!mm(TIME_DECODE_MATMUL, capture, xn_, d, B, D.sa_qkv, o, err)) return false;
     size_t coff = l * (size_t)B * cap_ * kvd;
     NDL_LK(decoder_self_attention(qkv_, pos_, D.sa_qn, D.sa_kn, m.rope_cos, m.rope_sin, self_k_ + coff,
                                   self_v_ + coff, cap_, B, att_, m.ad, st));
@@ -709,28 +795,26 @@ bool Batch::decode_step(std::string &err, bool capture) {
     r.ldy = d;
     r.epi = EPI_RESID;
     r.gate = D.sa_gate;
-    NDL_LK(int4_matmul(att_, qd, B, D.sa_o.view(), r, st));
+    if (!mm(TIME_DECODE_MATMUL, capture, att_, qd, B, D.sa_o, r, err)) return false;
     NDL_LK(rms_norm_rows(x_, d, xn_, d, D.ca_norm, B, d, st));
     MatmulOut qo;
     qo.y = q_;
     qo.ldy = qd;
-    NDL_LK(int4_matmul(xn_, d, B, D.ca_q.view(), qo, st));
+    if (!mm(TIME_DECODE_MATMUL, capture, xn_, d, B, D.ca_q, qo, err)) return false;
     const float *kp = kv_planes_ + (size_t)2 * l * ttot_ * kvd, *vp = kp + (size_t)ttot_ * kvd;
-    cudaEvent_t e0 = nullptr, e1 = nullptr;
-    if (time_cross_ && !capture) {
-      NDL_CK(cudaEventCreate(&e0));
-      NDL_CK(cudaEventCreate(&e1));
-      cross_events_.push_back({e0, e1});
-      NDL_CK(cudaEventRecord(e0, st));
-    }
+    cudaEvent_t ev;
+    if (!tbegin(TIME_CROSS_ATTENTION, capture, ev, err)) return false;
     NDL_LK(decoder_cross_attention(q_, D.ca_qn, kp, vp, seq_off_, B, att_, m.ad, st, tmax_));
-    if (e1) NDL_CK(cudaEventRecord(e1, st));
+    // algorithmic bytes: the encoder K and V rows once, q in, attention out
+    if (!tend(ev, 4.0 * (double)ttot_ * kvd * c.num_heads / c.num_kv_heads,
+              (double)ttot_ * kvd * 8 + (double)B * qd * 8, err))
+      return false;
     MatmulOut r2;
     r2.y = x_;
     r2.ldy = d;
     r2.epi = EPI_RESID;
     r2.gate = D.ca_gate;
-    NDL_LK(int4_matmul(att_, qd, B, D.ca_o.view(), r2, st));
+    if (!mm(TIME_DECODE_MATMUL, capture, att_, qd, B, D.ca_o, r2, err)) return false;
     if (D.ffn) {
       NDL_LK(rms_norm_rows(x_, d, xn_, d, D.ffn_norm, B, d, st));
       MatmulOut a;
@@ -738,17 +822,22 @@ bool Batch::decode_step(std::string &err, bool capture) {
       a.ldy = c.ffn_dim;
       a.epi = EPI_ACT;
       a.act = c.activation;
-      NDL_LK(int4_matmul(xn_, d, B, D.gate_up.view(), a, st));
+      if (!mm(TIME_DECODE_MATMUL, capture, xn_, d, B, D.gate_up, a, err)) return false;
       MatmulOut f;
       f.y = x_;
       f.ldy = d;
       f.epi = EPI_RESID;
       f.gate = D.ffn_gate;
-      NDL_LK(int4_matmul(ffn_, c.ffn_dim, B, D.down.view(), f, st));
+      if (!mm(TIME_DECODE_MATMUL, capture, ffn_, c.ffn_dim, B, D.down, f, err)) return false;
     }
   }
   NDL_LK(rms_norm_rows(x_, d, h_, d, m.dec_final_norm, B, d, st));  // model.rs:263
+  cudaEvent_t ev;
+  if (!tbegin(TIME_HEAD, capture, ev, err)) return false;
   NDL_LK(head_argmax(h_, B, m.emb, c.vocab_size, d, mask_, W_, logits_, spec_.max_new, pos_, keys_, st));
+  if (!tend(ev, 2.0 * B * c.vocab_size * (double)d,
+            (double)c.vocab_size * d * 4 + (double)B * d * 4 + (mask_ ? (double)B * W_ * 8 : 0.0), err))
+    return false;
   NDL_LK(finish_step(keys_, B, spec_.max_new, (spec_.flags & BATCH_STOP_ON_EOS) ? 1 : 0, out_ids_, lens_, done_,
                      pos_, n_done_, teacher_, m.emb, x_, d, m.embed_scale, st));
   return true;
@@ -759,13 +848,13 @@ bool Batch::begin(std::string &err) {
   NDL_CK(cudaSetDevice(m_->device));
   launches_ = 0;
   steps_done_ = 0;
-  for (auto &e : cross_events_) {
-    cudaEventDestroy(e.first);
-    cudaEventDestroy(e.second);
+  for (auto &e : timed_) {
+    cudaEventDestroy(e.a);
+    cudaEventDestroy(e.b);
   }
-  cross_events_.clear();
+  timed_.clear();
   if (!reset_decoder(err) || !prefill(err)) return false;
-  use_graph_ = !(spec_.flags & BATCH_NO_GRAPH) && !time_cross_ && spec_.max_new > 0;
+  use_graph_ = !(spec_.flags & BATCH_NO_GRAPH) && !timed_cls_ && spec_.max_new > 0;
   if (use_graph_ && !graph_) {
     cudaStream_t st = st_;
     int64_t before = launches_;
@@ -850,21 +939,30 @@ bool Batch::download(uint32_t *out_ids, uint32_t *out_lens, float *logits, float
       std::memset(out_lens, 0, (size_t)B * 4);
   }
   if (enc_out && enc_out_) NDL_CK(cudaMemcpyAsync(enc_out, enc_out_, (size_t)ttot_ * m_->cfg.d_model * 4, k, st));
+  int kerr = 0;
+  NDL_CK(cudaMemcpyAsync(&kerr, m_->kerr, sizeof(int), cudaMemcpyDeviceToHost, st));
   NDL_CK(cudaStreamSynchronize(st));
+  if (kerr) {
+    cudaMemsetAsync(m_->kerr, 0, sizeof(int), st);
+    err = "a tensor-core GEMM wait timed out; results are invalid";
+    return false;
+  }
   if (!spec_.max_new || !out_lens || dev_out) return true;
   for (int b = 0; b < B; ++b) out_lens[b] = std::min<uint32_t>(out_lens[b], (uint32_t)spec_.max_new);
   return true;
 }
 
-bool Batch::collect_cross_timing(std::string &err) {
+bool Batch::collect_timing(std::string &err) {
   NDL_CK(cudaStreamSynchronize(st_));
-  cross_ms_ = 0.0;
-  cross_n_ = 0;
-  for (auto &e : cross_events_) {
+  timed_ms_ = timed_flops_ = timed_bytes_ = 0.0;
+  timed_n_ = 0;
+  for (auto &e : timed_) {
     float ms = 0.0f;
-    NDL_CK(cudaEventElapsedTime(&ms, e.first, e.second));
-    cross_ms_ += ms;
-    ++cross_n_;
+    NDL_CK(cudaEventElapsedTime(&ms, e.a, e.b));
+    timed_ms_ += ms;
+    timed_flops_ += e.flops;
+    timed_bytes_ += e.bytes;
+    ++timed_n_;
   }
   return true;
 }

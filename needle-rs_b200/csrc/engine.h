@@ -34,6 +34,10 @@ struct Lin {  // packed INT4 weight on the device
   uint8_t *w = nullptr;
   float *s = nullptr;
   int K = 0, N = 0, G = 0, gs = 0;
+  // tensor-core staging copy: bf16 hi/lo planes [N][Kp] of q * scale
+  void *tc_hi = nullptr, *tc_lo = nullptr;
+  bool tc_ready = false;
+  TcPlanes tc;
   Int4Weight view() const { return Int4Weight{w, s, K, N, G, gs}; }
 };
 
@@ -75,6 +79,7 @@ struct DevModel {
   cudaStream_t stream = nullptr;
   std::vector<void *> allocs;
   size_t weight_bytes = 0;
+  int *kerr = nullptr;  // device flag: a bounded in-kernel wait expired
 
   ~DevModel();
 };
@@ -83,6 +88,16 @@ struct DevModel {
 // config from __metadata__, missing tensors become zeros, F32 projection
 // weights are quantized on load by the device packer).
 std::unique_ptr<DevModel> load_model(std::vector<uint8_t> raw, int device, std::string &err);
+
+// Kernel classes that can be timed (needle_batch_time_kernel).
+enum TimedClass : int {
+  TIME_NONE = 0,
+  TIME_CROSS_ATTENTION = 1,  // decoder cross-attention (HBM-bound on encoder K/V)
+  TIME_PREFILL_MATMUL = 2,   // encoder INT4 projections + cross K/V fill
+  TIME_DECODE_MATMUL = 3,    // decoder INT4 projections
+  TIME_HEAD = 4,             // output head + mask + argmax
+  TIME_ENCODER_ATTENTION = 5,
+};
 
 enum BatchFlags : uint32_t {
   BATCH_STOP_ON_EOS = 1u,     // engine.rs:306-308: stop a request at EOS
@@ -123,17 +138,22 @@ class Batch {
   cudaStream_t stream() const { return st_; }
   // Number of kernels one run() launches (reported by the benchmark).
   int64_t kernels_launched() const { return launches_; }
-  // Optional per-kernel timing of the cross-attention launches (ms total,
-  // launch count) recorded with CUDA events on the model's stream.
-  void enable_cross_timing(bool on) { time_cross_ = on; }
-  bool collect_cross_timing(std::string &err);
-  double cross_ms() const { return cross_ms_; }
-  int64_t cross_launches() const { return cross_n_; }
+  // Optional timing of one kernel class: CUDA events around each of its
+  // launches on the batch's stream (eager launches while enabled), plus the
+  // algorithmic flops and bytes of every timed launch.
+  void set_timed_class(int cls) { timed_cls_ = cls; }
+  bool collect_timing(std::string &err);
+  double timed_ms() const { return timed_ms_; }
+  int64_t timed_launches() const { return timed_n_; }
+  double timed_flops() const { return timed_flops_; }
+  double timed_bytes() const { return timed_bytes_; }
 
  private:
   bool prefill(std::string &err);
   bool reset_decoder(std::string &err);
   bool decode_step(std::string &err, bool capture);
+  bool mm(int cls, bool capture, const float *x, int64_t ldx, int M, const Lin &w, const MatmulOut &o,
+          std::string &err);
   template <class T>
   T *alloc(size_t n, std::string &err);
 
@@ -166,6 +186,9 @@ class Batch {
   // decoder state
   float *self_k_ = nullptr, *self_v_ = nullptr;  // [L][B][cap][KVH*HD]
   float *x_ = nullptr, *xn_ = nullptr, *qkv_ = nullptr, *att_ = nullptr, *q_ = nullptr, *h_ = nullptr, *ffn_ = nullptr;
+  // tensor-core activation staging (bf16 hi/lo planes) and its TMA maps
+  void *tc_hi_ = nullptr, *tc_lo_ = nullptr;
+  std::vector<TcPlanes> tc_maps_;  // one per distinct padded K
   unsigned long long *keys_ = nullptr;
   int32_t *pos_ = nullptr;
   uint32_t *out_ids_ = nullptr, *lens_ = nullptr;
@@ -177,10 +200,16 @@ class Batch {
   uint32_t *first_ids_ = nullptr;
   int steps_done_ = 0;
   int64_t launches_ = 0, step_launches_ = 0;
-  bool time_cross_ = false;
-  double cross_ms_ = 0.0;
-  int64_t cross_n_ = 0;
-  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> cross_events_;
+  int timed_cls_ = 0;
+  double timed_ms_ = 0.0, timed_flops_ = 0.0, timed_bytes_ = 0.0;
+  int64_t timed_n_ = 0;
+  struct TimedLaunch {
+    cudaEvent_t a, b;
+    double flops, bytes;
+  };
+  std::vector<TimedLaunch> timed_;
+  bool tbegin(int cls, bool capture, cudaEvent_t &a, std::string &err);
+  bool tend(cudaEvent_t a, double flops, double bytes, std::string &err);
 };
 
 // Splits n requests with lengths len[] into `shards` groups of near-equal

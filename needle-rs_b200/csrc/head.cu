@@ -240,6 +240,7 @@ cudaError_t init_kernels() {
   cudaError_t e = init_matmul_kernels();
   if (e == cudaSuccess) e = init_attention_kernels();
   if (e == cudaSuccess) e = init_head_kernels();
+  if (e == cudaSuccess) e = init_tc_kernels();
   return e;
 }
 

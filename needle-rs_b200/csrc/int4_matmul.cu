@@ -403,8 +403,10 @@ cudaError_t int4_matmul(const float *x, int64_t ldx, int M, const Int4Weight &W,
   if (M <= 0 || W.N <= 0) return cudaSuccess;
   if (W.gs <= 0 || W.G <= 0 || (W.gs & 1)) return cudaErrorInvalidValue;
   if (W.w2 && ((W.N & 1) || !W.s2)) return cudaErrorInvalidValue;
-  if (o.col_block && (o.col_block % 64)) return cudaErrorInvalidValue;
-  if (o.epi == EPI_KNORM && (!o.col_block || !o.vec)) return cudaErrorInvalidValue;
+  // Output groups of 4 columns never straddle a column block; the fused
+  // k-norm needs whole 64-column heads.
+  if (o.col_block && (o.col_block % 4)) return cudaErrorInvalidValue;
+  if (o.epi == EPI_KNORM && (!o.col_block || (o.col_block % 64) || !o.vec)) return cudaErrorInvalidValue;
   if (o.epi == EPI_ACT && (W.N & 1)) return cudaErrorInvalidValue;
   EpiCtx e{o, W.N};
   const int Kp = W.G * W.gs;

@@ -53,6 +53,30 @@ struct MatmulOut {
 cudaError_t int4_matmul(const float *x, int64_t ldx, int M, const Int4Weight &W, const MatmulOut &o,
                         cudaStream_t stream);
 
+// ── tensor-core path (tc_gemm.cu) ──
+// A pair of bf16 planes (hi, lo) of a [rows][Kp] K-contiguous operand, with
+// the TMA descriptors the tcgen05 GEMM loads it through (boxes of 64 x
+// box_rows, 128-byte swizzle).  Kp is a multiple of 64.
+struct TcPlanes {
+  alignas(64) unsigned char hi[128];  // CUtensorMap
+  alignas(64) unsigned char lo[128];
+  int rows = 0, Kp = 0, box_rows = 0;
+  const void *hi_ptr = nullptr, *lo_ptr = nullptr;
+};
+constexpr int kTcMinRows = 128;  // batched GEMMs at least this tall use the tensor cores
+int tc_padded_k(int K);
+cudaError_t tc_make_planes(const void *hi, const void *lo, int rows, int Kp, int box_rows, TcPlanes &out);
+// W (reference INT4 layout, paired mode allowed) -> bf16 planes [N][Kp].
+cudaError_t tc_prep_weight(const Int4Weight &W, int Kp, void *hi, void *lo, cudaStream_t st);
+// f32 rows [M][K] -> bf16 planes [M][Kp] (zero padded past K).
+cudaError_t tc_split_rows(const float *x, int64_t ldx, int M, int K, int Kp, void *hi, void *lo, cudaStream_t st);
+// Y[M, N] (epilogue) A @ B^T with A planes [M][Kp] and B planes [N][Kp]
+// (tcgen05, 3-term bf16 split, f32 accumulation).  *err is set if a bounded
+// wait inside the kernel expired.
+cudaError_t tc_matmul(const TcPlanes &A, int M, const TcPlanes &B, int N, const MatmulOut &o, int *err,
+                      cudaStream_t st);
+cudaError_t init_tc_kernels();
+
 // Device packing / unpacking (quant.rs:63-155), bit-exact with the reference.
 cudaError_t int4_quantize(const float *w, int K, int N, uint8_t *data, float *scales, cudaStream_t st);
 cudaError_t int4_dequantize(const uint8_t *data, const float *scales, int K, int N, int G, float *out,

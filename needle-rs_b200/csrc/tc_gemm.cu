@@ -1,0 +1,481 @@
+// tc_gemm.cu — INT4-weight matmul on the 5th-generation tensor cores (tcgen05).
+//
+// Y[M, N] (epilogue) X[M, K] @ W for the batched paths (encoder prefill, the
+// cross-attention K/V fill, batched decode), replacing the M-fold matvec loop
+// of QuantizedWeight::matmul (crates/needle-core/src/quant.rs:400-410).
+//
+// Precision.  The reference is f32 end to end.  A single bf16 MMA would cost
+// ~2^-9 relative per product, too much for 1e-3 / 1e-4 logit parity after 20
+// layers, so both operands are split into bf16 pairs, hi = bf16(v) and
+// lo = bf16(v - hi) (|v - hi - lo| <= 2^-18 |v|), and each K-step issues three
+// MMAs, hi*hi + hi*lo + lo*hi, into one f32 accumulator in TMEM (the dropped
+// lo*lo term is <= 2^-18 relative).  Net error ~1e-6 relative per GEMM.
+//
+// Operands.  W's dequantized values q * scale (quant.rs:131-155) are written
+// once per weight, at load, as two bf16 planes [N][Kp] (K contiguous, Kp =
+// K rounded up to 64): the packed INT4 weight stays the stored format and the
+// planes are its tensor-core staging copy (4 bytes per weight; the whole model
+// is ~100 MB).  Activations arrive as bf16 planes [M][Kp] written by the
+// producing kernel (norm, attention) or by split_rows().
+//
+// Kernel.  Persistent, one CTA per SM, 256 threads, warp-specialised:
+//   warp 0      TMA producer: 128x64 A tiles and BNx64 B tiles (hi and lo),
+//               128-byte swizzle, into a 3-stage shared-memory ring
+//   warp 1      TMEM allocation + MMA issue (one elected lane):
+//               tcgen05.mma.cta_group::1.kind::f16, M=128, N=BN, K=16
+//   warps 4-7   epilogue: tcgen05.ld of the f32 accumulator (warp 4+q owns
+//               TMEM lanes 32q..32q+31 = output rows), fused epilogue
+//               (store / gated residual / activation / per-head k-norm)
+// TMEM holds two accumulators so the epilogue of tile i overlaps the MMAs
+// of tile i+1.  TMA loads never use cluster multicast.  Every mbarrier wait
+// is bounded: on expiry the kernel records an error flag and unwinds.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace ndl {
+namespace {
+
+constexpr int TC_BM = 128, TC_BK = 64, TC_STAGES = 3, TC_THREADS = 256;
+constexpr uint32_t kWaitLimit = 1u << 24;  // bounded spin (x ~100 ns backoff: seconds)
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t *b, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait; false (and *err set) when the limit expires.
+__device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity, int *err) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    if (mbar_try_wait(b, parity)) return true;
+    if (i > 32) __nanosleep(64);
+    if ((i & 1023) == 0 && *(volatile int *)err) return false;  // another role gave up
+  }
+  atomicExch(err, 1);
+  return false;
+}
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// UMMA shared-memory descriptor: K-major operand, 128-byte swizzle, 8-row
+// atoms of 1024 bytes stacked along M/N (SBO = 1024 B), version 1 (sm100).
+__device__ __forceinline__ uint64_t umma_desc(const void *smem) {
+  uint64_t addr = smem_u32(smem);
+  uint64_t d = 0;
+  d |= (addr >> 4) & 0x3FFFull;          // start address
+  d |= (uint64_t)1 << 16;                // LBO (ignored for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;      // SBO
+  d |= (uint64_t)1 << 46;                // version
+  d |= (uint64_t)2 << 61;                // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor: bf16 x bf16 -> f32, A and B K-major, M = 128, N = BN.
+__host__ __device__ constexpr uint32_t umma_idesc(int BN) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(TC_BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float *v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+struct TcEpi {
+  MatmulOut o;
+  int N;
+};
+
+__device__ __forceinline__ float act_apply_tc(int act, float g, float u) {
+  if (act == ACT_SWIGLU) {
+    float sg = g * (1.0f / (1.0f + expf(-g)));
+    return sg * u;
+  }
+  if (act == ACT_GELU) {
+    const float C = 0.79788456f, A = 0.044715f;
+    float ax = A * g;
+    float axx = ax * g;
+    float axxx = axx * g;
+    float inner = C * (g + axxx);
+    float t = 1.0f + tanhf(inner);
+    return (0.5f * g) * t * u;
+  }
+  float rg = g > 0.0f ? g : 0.0f, ru = u > 0.0f ? u : 0.0f;
+  return rg * ru;
+}
+
+// Epilogue of `cnt` (32 or 64) consecutive columns n0.. of row m.
+__device__ __forceinline__ void epi_row(const TcEpi &e, int m, int n0, float *v, int cnt) {
+  const MatmulOut &o = e.o;
+  if (o.epi == EPI_ACT) {
+    float *p = o.y + (int64_t)m * o.ldy + (n0 >> 1);
+    for (int j = 0; j + 1 < cnt; j += 2)
+      if (n0 + j + 1 < e.N) p[j >> 1] = act_apply_tc(o.act, v[j], v[j + 1]);
+    return;
+  }
+  if (o.epi == EPI_KNORM) {
+    int blk = n0 / o.col_block;
+    if ((blk & 1) == 0) {  // K block: ZCRMSNorm each 64-column head (norm.rs:23-30)
+      const float *sc = o.vec + (int64_t)(blk >> 1) * 64;
+      for (int h = 0; h + 64 <= cnt; h += 64) {
+        float ss = 0.0f;
+#pragma unroll 16
+        for (int j = 0; j < 64; ++j) ss += v[h + j] * v[h + j];
+        float inv = 1.0f / sqrtf(ss / 64.0f + 1e-6f);
+#pragma unroll 16
+        for (int j = 0; j < 64; ++j) v[h + j] = ((1.0f + __ldg(sc + j)) * v[h + j]) * inv;
+      }
+    }
+  }
+  // cnt columns never straddle a column block (col_block % 64 == 0)
+  float *p;
+  if (o.col_block) {
+    int b = n0 / o.col_block;
+    p = o.y + (int64_t)b * o.block_stride + (int64_t)m * o.ldy + (n0 - b * o.col_block);
+  } else {
+    p = o.y + (int64_t)m * o.ldy + n0;
+  }
+  if (n0 + cnt <= e.N) {
+    float4 *p4 = reinterpret_cast<float4 *>(p);
+    if (o.epi == EPI_RESID) {
+      for (int j = 0; j < cnt / 4; ++j) {
+        float4 r = p4[j];
+        r.x += o.gate * v[4 * j + 0];
+        r.y += o.gate * v[4 * j + 1];
+        r.z += o.gate * v[4 * j + 2];
+        r.w += o.gate * v[4 * j + 3];
+        p4[j] = r;
+      }
+    } else {
+      for (int j = 0; j < cnt / 4; ++j) p4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    }
+  } else {
+    for (int j = 0; j < cnt && n0 + j < e.N; ++j) p[j] = (o.epi == EPI_RESID) ? p[j] + o.gate * v[j] : v[j];
+  }
+}
+
+template <int BN>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
+                   const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl, int M, int N,
+                   int Kp, TcEpi e, int *err) {
+  constexpr int A_BYTES = TC_BM * TC_BK * 2, B_BYTES = BN * TC_BK * 2;
+  constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
+  constexpr uint32_t IDESC = umma_idesc(BN);
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // 1024-byte alignment of every operand tile (128-byte swizzle atoms).
+  uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t *full = (uint64_t *)(smem + TC_STAGES * STAGE_BYTES);
+  uint64_t *empty = full + TC_STAGES;
+  uint64_t *tfull = empty + TC_STAGES;
+  uint64_t *tempty = tfull + 2;
+  uint32_t *tmem_slot = (uint32_t *)(tempty + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_m = (M + TC_BM - 1) / TC_BM, num_n = (N + BN - 1) / BN;
+  const int tiles = num_m * num_n, nkb = Kp / TC_BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < TC_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 128);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {  // two BN-column f32 accumulators
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(2 * BN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *(volatile uint32_t *)tmem_slot;
+
+  if (warp == 0) {
+    // ── TMA producer ──
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&tmAh) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&tmAl) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&tmBh) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&tmBl) : "memory");
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        const int mt = t / num_n, nt = t - mt * num_n;
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!(ok = mbar_wait(&empty[stage], phase ^ 1, err))) break;
+          uint8_t *st = smem + stage * STAGE_BYTES;
+          mbar_expect_tx(&full[stage], STAGE_BYTES);
+          tma_load_2d(st, &tmAh, &full[stage], kb * TC_BK, mt * TC_BM);
+          tma_load_2d(st + A_BYTES, &tmAl, &full[stage], kb * TC_BK, mt * TC_BM);
+          tma_load_2d(st + 2 * A_BYTES, &tmBh, &full[stage], kb * TC_BK, nt * BN);
+          tma_load_2d(st + 2 * A_BYTES + B_BYTES, &tmBl, &full[stage], kb * TC_BK, nt * BN);
+          if (++stage == TC_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // Drain: wait until the MMAs consumed every issued stage, so no TMA
+      // write is still in flight when the CTA exits.
+      for (int s = 0; s < TC_STAGES && ok; ++s) {
+        ok = mbar_wait(&empty[stage], phase ^ 1, err);
+        if (++stage == TC_STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ── MMA issuer ──
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int i = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++i) {
+        const int buf = i & 1;
+        if (!(ok = mbar_wait(&tempty[buf], ((i >> 1) & 1) ^ 1, err))) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t d = tmem + (uint32_t)(buf * BN);
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!(ok = mbar_wait(&full[stage], phase, err))) break;
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          uint8_t *st = smem + stage * STAGE_BYTES;
+          const uint64_t ah = umma_desc(st), al = umma_desc(st + A_BYTES);
+          const uint64_t bh = umma_desc(st + 2 * A_BYTES), bl = umma_desc(st + 2 * A_BYTES + B_BYTES);
+#pragma unroll
+          for (int k = 0; k < TC_BK / 16; ++k) {
+            const uint64_t adv = (uint64_t)((k * 32) >> 4);  // 16 bf16 = 32 bytes along K
+            umma_bf16(d, ah + adv, bh + adv, IDESC, (kb | k) ? 1u : 0u);
+            umma_bf16(d, ah + adv, bl + adv, IDESC, 1u);
+            umma_bf16(d, al + adv, bh + adv, IDESC, 1u);
+          }
+          umma_commit(&empty[stage]);  // frees the stage once these MMAs complete
+          if (++stage == TC_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (ok) umma_commit(&tfull[buf]);
+      }
+    }
+  } else if (warp >= 4) {
+    // ── epilogue ──
+    const int q = warp - 4;
+    int i = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
+      const int buf = i & 1;
+      if (!mbar_wait(&tfull[buf], (i >> 1) & 1, err)) break;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const int mt = t / num_n, nt = t - mt * num_n;
+      const int m = mt * TC_BM + q * 32 + lane;
+      const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
+      const bool knorm = e.o.epi == EPI_KNORM;
+      for (int c = 0; c < BN; c += (knorm ? 64 : 32)) {
+        float v[64];
+        tmem_ld32(base + c, v);
+        if (knorm) tmem_ld32(base + c + 32, v + 32);
+        const int n0 = nt * BN + c;
+        if (m < M && n0 < N) epi_row(e, m, n0, v, knorm ? 64 : 32);
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      mbar_arrive(&tempty[buf]);
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * BN));
+  }
+}
+
+// W (reference INT4 layout) -> bf16 hi/lo planes [N][Kp], K contiguous.
+__global__ void prep_weight_kernel(Int4Weight W, int Kp, __nv_bfloat16 *hi, __nv_bfloat16 *lo) {
+  int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)W.N * Kp) return;
+  int n = (int)(idx / Kp), k = (int)(idx - (int64_t)n * Kp);
+  float w = 0.0f;
+  if (k < W.K && k < W.G * W.gs) {
+    int p = k >> 1, g = k / W.gs;
+    uint8_t b;
+    float s;
+    if (W.w2) {
+      const int Nh = W.N >> 1;
+      b = ((n & 1) ? W.w2 : W.w)[(int64_t)p * Nh + (n >> 1)];
+      s = ((n & 1) ? W.s2 : W.s)[(int64_t)g * Nh + (n >> 1)];
+    } else {
+      b = W.w[(int64_t)p * W.N + n];
+      s = W.s[(int64_t)g * W.N + n];
+    }
+    int code = (k & 1) ? sign_extend4(b >> 4) : sign_extend4(b & 0xF);
+    w = (float)code * s;  // quant.rs:144-151
+  }
+  __nv_bfloat16 h = __float2bfloat16_rn(w);
+  hi[idx] = h;
+  lo[idx] = __float2bfloat16_rn(w - __bfloat162float(h));
+}
+
+// f32 rows [M][K] (stride ldx) -> bf16 hi/lo planes [M][Kp] (zero padded).
+__global__ void split_rows_kernel(const float *__restrict__ x, int64_t ldx, int M, int K, int Kp,
+                                  __nv_bfloat16 *hi, __nv_bfloat16 *lo) {
+  int64_t idx = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  if (idx >= (int64_t)M * Kp) return;
+  int m = (int)(idx / Kp), k = (int)(idx - (int64_t)m * Kp);
+  __nv_bfloat16 h[4], l[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float v = (k + j < K) ? x[(int64_t)m * ldx + k + j] : 0.0f;
+    h[j] = __float2bfloat16_rn(v);
+    l[j] = __float2bfloat16_rn(v - __bfloat162float(h[j]));
+  }
+  *reinterpret_cast<uint2 *>(hi + idx) = *reinterpret_cast<uint2 *>(h);
+  *reinterpret_cast<uint2 *>(lo + idx) = *reinterpret_cast<uint2 *>(l);
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void *p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+  }
+  return fn;
+}
+
+int tc_sm_count() {
+  static int n[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (!n[dev]) cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev);
+  return n[dev] > 0 ? n[dev] : 148;
+}
+
+constexpr size_t tc_smem_bytes(int BN) {
+  return 1024 + (size_t)TC_STAGES * (2 * TC_BM * TC_BK * 2 + 2 * BN * TC_BK * 2) + 256;
+}
+
+}  // namespace
+
+int tc_padded_k(int K) { return (K + TC_BK - 1) / TC_BK * TC_BK; }
+
+cudaError_t tc_make_planes(const void *hi, const void *lo, int rows, int Kp, int box_rows, TcPlanes &out) {
+  auto fn = encode_fn();
+  if (!fn) return cudaErrorNotSupported;
+  if (((uintptr_t)hi & 15) || ((uintptr_t)lo & 15) || (Kp % TC_BK) || rows <= 0) return cudaErrorInvalidValue;
+  cuuint64_t dims[2] = {(cuuint64_t)Kp, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)Kp * 2};
+  cuuint32_t box[2] = {(cuuint32_t)TC_BK, (cuuint32_t)box_rows};
+  cuuint32_t es[2] = {1, 1};
+  for (int s = 0; s < 2; ++s) {
+    CUresult r = fn(reinterpret_cast<CUtensorMap *>(s ? out.lo : out.hi), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(s ? lo : hi), dims,
+                    strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  }
+  out.rows = rows;
+  out.Kp = Kp;
+  out.box_rows = box_rows;
+  out.hi_ptr = hi;
+  out.lo_ptr = lo;
+  return cudaSuccess;
+}
+
+cudaError_t tc_prep_weight(const Int4Weight &W, int Kp, void *hi, void *lo, cudaStream_t st) {
+  int64_t n = (int64_t)W.N * Kp;
+  prep_weight_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(W, Kp, (__nv_bfloat16 *)hi, (__nv_bfloat16 *)lo);
+  return cudaGetLastError();
+}
+
+cudaError_t tc_split_rows(const float *x, int64_t ldx, int M, int K, int Kp, void *hi, void *lo, cudaStream_t st) {
+  if (M <= 0) return cudaSuccess;
+  if (Kp % 4) return cudaErrorInvalidValue;
+  int64_t n = (int64_t)M * Kp / 4;
+  split_rows_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(x, ldx, M, K, Kp, (__nv_bfloat16 *)hi,
+                                                                   (__nv_bfloat16 *)lo);
+  return cudaGetLastError();
+}
+
+cudaError_t tc_matmul(const TcPlanes &A, int M, const TcPlanes &B, int N, const MatmulOut &o, int *err,
+                      cudaStream_t st) {
+  if (M <= 0 || N <= 0) return cudaSuccess;
+  if (A.Kp != B.Kp || A.box_rows != TC_BM || B.box_rows != 128 || M > A.rows || N > B.rows)
+    return cudaErrorInvalidValue;
+  if (o.col_block && (o.col_block % 64)) return cudaErrorInvalidValue;
+  if (o.epi == EPI_KNORM && (!o.col_block || !o.vec)) return cudaErrorInvalidValue;
+  if ((o.ldy % 4) || ((uintptr_t)o.y % 16) || (o.col_block && (o.block_stride % 4))) return cudaErrorInvalidValue;
+  if (o.epi == EPI_ACT && (N & 1)) return cudaErrorInvalidValue;
+  TcEpi e{o, N};
+  const int tiles = ((M + TC_BM - 1) / TC_BM) * ((N + 127) / 128);
+  const int grid = tiles < tc_sm_count() ? tiles : tc_sm_count();
+  tc_gemm_kernel<128><<<grid, TC_THREADS, tc_smem_bytes(128), st>>>(
+      *reinterpret_cast<const CUtensorMap *>(A.hi), *reinterpret_cast<const CUtensorMap *>(A.lo),
+      *reinterpret_cast<const CUtensorMap *>(B.hi), *reinterpret_cast<const CUtensorMap *>(B.lo), M, N, A.Kp, e, err);
+  return cudaGetLastError();
+}
+
+cudaError_t init_tc_kernels() {
+  return cudaFuncSetAttribute(tc_gemm_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              (int)tc_smem_bytes(128));
+}
+
+}  // namespace ndl

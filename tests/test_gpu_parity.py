@@ -119,11 +119,12 @@ def test_int4_quantize_ties_round_away():
     assert np.array_equal(dd.cpu().numpy(), data)
 
 
-@pytest.mark.parametrize("act", [0, 1, 2])
-def test_ffn_forward_vs_oracle(act):
-    # ffn.rs:19-56 over T tokens (the MLP block), d=512 -> 2048 -> 512.
-    T, d, ff = 64, 512, 2048
-    rng = np.random.default_rng(act)
+@pytest.mark.parametrize("act,T", [(0, 64), (1, 64), (2, 64), (0, 256), (1, 200)])
+def test_ffn_forward_vs_oracle(act, T):
+    # ffn.rs:19-56 over T tokens (the MLP block), d=512 -> 2048 -> 512;
+    # T >= 128 runs the tensor-core GEMM.
+    d, ff = 512, 2048
+    rng = np.random.default_rng(act + T)
     x = rng.standard_normal((T, d)).astype(np.float32)
     g, u, dn = wl.random_int4(rng, d, ff), wl.random_int4(rng, d, ff), wl.random_int4(rng, ff, d)
     ref = np.stack([orc.ffn_forward(g, u, dn, d, ff, x[t], act) for t in range(T)])
@@ -247,6 +248,21 @@ def test_batch_rows_are_independent(full):
     for r in (0, 17, 39):
         one, _, lg = eng.run_batch_ids([prompts[r]], 4, want_logits=True)
         assert close(all_lg[r, 0], lg[0, 0])
+
+
+def test_batched_decode_tensor_core_vs_oracle(full):
+    # 160 requests: the decode projections run as 160-row tensor-core GEMMs.
+    eng, ref = full
+    ids_in, off = wl.random_prompts(160, 8, 96, 8192, seed=12)
+    prompts = [ids_in[off[i]:off[i + 1]] for i in range(160)]
+    steps = 5
+    masks = wl.random_masks(160, steps, 8192, 0.05, seed=13)
+    ids, lens, lg = eng.run_batch_ids(prompts, steps, mask_bits=masks, want_logits=True)
+    tol = 2 * (ATOL + RTOL * 10.0)
+    for r in (0, 1, 77, 159):
+        rid, rmarg, rlg = ref.generate(prompts[r], steps, mask_bits=masks[r], want_logits=True)
+        assert tokens_match(ids[r], rid, rmarg, tol), r
+        assert close(lg[r, 0], rlg[0]), max_excess(lg[r, 0], rlg[0])
 
 
 def test_argument_errors(full):

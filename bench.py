@@ -194,6 +194,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--profile-run", action="store_true",
+                    help="one untimed run of the workload and exit (for ncu launch lists)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl != "reference":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
@@ -228,6 +230,14 @@ def main():
     batch = eng.prepare_batch(ids, off, args.max_new, masks, flags=0)
     stream = torch.cuda.ExternalStream(batch.stream, device=local)
     tokens_per_step = args.requests * args.max_new
+    if args.profile_run:
+        batch.run()
+        batch.sync()
+        print(json.dumps({"profile_run": True, "kernel_launches": batch.kernel_launches(),
+                          "requests": args.requests}), flush=True)
+        batch.close()
+        eng.close()
+        return 0
 
     # Per-kernel-class breakdown (one instrumented run each) to find the
     # dominant kernel, then warm-up runs.

@@ -127,6 +127,28 @@ int needle_ffn_forward(const float *x, size_t T, size_t d_model, size_t d_ff, co
                        const uint8_t *down_data, const float *down_scales, int activation, float *out,
                        void *stream);
 
+/* The MLP block of needle_ffn_forward for callers that cannot allocate device
+ * memory during a call (a fixed device-memory budget handed over at start-up,
+ * latency-critical steps that cannot take an allocator call or an
+ * out-of-memory failure, embedders with their own memory manager).  No
+ * counterpart in the reference, which has no device memory.  Arguments and
+ * results are those of needle_ffn_forward; the difference:
+ *   - the [T][d_ff] hidden activation lives in a fixed device array compiled
+ *     into the library (1,048,576 floats = 4 MiB, held on every GPU that
+ *     loads the library until the process exits); T * d_ff above that is
+ *     rejected with an error; nothing is allocated and the matmuls run on the
+ *     CUDA cores;
+ *   - the first call on each device looks up that array's device address
+ *     (cudaGetSymbolAddress) and sets kernel attributes; make that first call
+ *     before any stream capture;
+ *   - every call shares the one array, which keeps the last call's contents:
+ *     calls whose work overlaps on the GPU (different streams, or threads
+ *     without ordering) race on it and must be serialised by the caller. */
+int needle_ffn_forward_noalloc(const float *x, size_t T, size_t d_model, size_t d_ff, const uint8_t *gate_data,
+                               const float *gate_scales, const uint8_t *up_data, const float *up_scales,
+                               const uint8_t *down_data, const float *down_scales, int activation, float *out,
+                               void *stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

@@ -78,6 +78,7 @@ def lib():
             "needle_int4_quantize": (I, [P, S, S, P, P, P]),
             "needle_int4_dequantize": (I, [P, P, S, S, S, P, P]),
             "needle_ffn_forward": (I, [P, S, S, S, P, P, P, P, P, P, I, P, P]),
+            "needle_ffn_forward_noalloc": (I, [P, S, S, S, P, P, P, P, P, P, I, P, P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -298,3 +299,10 @@ def int4_dequantize(data_ptr, scales_ptr, K, N, G, out_ptr, stream=None):
 
 def ffn_forward(x_ptr, T, d, ff, g, u, dn, act, out_ptr, stream=None):
     _check(lib().needle_ffn_forward(x_ptr, T, d, ff, g[0], g[1], u[0], u[1], dn[0], dn[1], act, out_ptr, stream))
+
+
+def ffn_forward_noalloc(x_ptr, T, d, ff, g, u, dn, act, out_ptr, stream=None):
+    """As ffn_forward, with the hidden activation in the library's fixed device
+    array (no allocation; T * d_ff <= 1,048,576; overlapping calls race)."""
+    _check(lib().needle_ffn_forward_noalloc(x_ptr, T, d, ff, g[0], g[1], u[0], u[1], dn[0], dn[1], act, out_ptr,
+                                            stream))

@@ -15,6 +15,7 @@
 #include <vector>
 
 #include "../../include/needle_b200.h"
+#include "capi_internal.h"
 #include "engine.h"
 
 using namespace ndl;
@@ -150,6 +151,9 @@ int run_batch(NeedleHandle *h, const uint32_t *ids, const uint64_t *off, size_t 
 }
 
 }  // namespace
+
+void ndl::capi_set_last_error(const std::string &msg) { set_err(msg); }
+void ndl::capi_clear_last_error() { clear_err(); }
 
 extern "C" {
 

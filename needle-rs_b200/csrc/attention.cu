@@ -335,40 +335,20 @@ __global__ void __launch_bounds__(256) dec_self_attn_kernel(const float *__restr
   }
 }
 
-// ── decoder cross-attention (attn.rs:281-337) ──────────────────────────────
-// CTA = (request, KV head).  The dominant HBM reader of batched decode: each
-// CTA streams its request's encoder K then V rows (HD f32 each) exactly once.
-// Specialised for HD == 64: a half-warp reads one 256-byte row with float4s.
-template <int REP>
-__global__ void __launch_bounds__(256) cross_attn_kernel(const float *__restrict__ q, const float *__restrict__ qn,
-                                                         const float *__restrict__ kplane,
-                                                         const float *__restrict__ vplane,
-                                                         const int64_t *__restrict__ seq_off, float *out,
-                                                         AttnDims a) {
-  constexpr int HD = 64;
-  extern __shared__ __align__(16) float sm[];
-  const int b = blockIdx.y, g = blockIdx.x;
-  const int64_t off = seq_off[b];
-  const int T = (int)(seq_off[b + 1] - off);
-  const int kvd = a.KVH * HD, qd = a.H * HD;
-  float *qs = sm;               // [REP][64]
-  float *red = sm + REP * HD;   // [16][REP][64] PV partials, also reductions
-  float *sc = red + 16 * REP * HD;  // [REP][T]
+// ── decoder attention over a K/V row range, head dim 64 ────────────────────
+// Shared by cross-attention (attn.rs:281-337; rows = the request's encoder
+// K/V) and decoder self-attention (attn.rs:100-183; rows = the request's
+// cache).  The REP query heads of one KV head (GQA) share every K and V row
+// read: a half-warp reads one 256-byte row with float4s, four rows in
+// flight per half-warp.  qs: [REP][64] normed queries in shared memory.
+// Exact softmax as ops.rs:5-36 (max, exp, sum, scale), then P V.
+template <int REP, int NT>
+__device__ __forceinline__ void attend_hd64(const float *qs, const float *__restrict__ kb,
+                                            const float *__restrict__ vb, int kvd, int T, float scale, float *sc,
+                                            float *red, float *out_row) {
+  constexpr int HD = 64, NHW = NT / 16, NW = NT / 32, UNR = 4, SPAN = NHW * UNR;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int hw = tid >> 4, hl = tid & 15;  // half-warp index (0..15), lane in half
-
-  // q heads of this group + q_norm (attn.rs:296-300)
-  if (warp < REP) {
-    int h = g * REP + warp;
-    float v[128];
-    const float *src = q + (int64_t)b * qd + h * HD;
-    v[lane] = src[lane];
-    v[lane + 32] = src[lane + 32];
-    norm_rope_head(v, HD, qn, nullptr, nullptr, false, lane);
-    qs[warp * HD + lane] = v[lane];
-    qs[warp * HD + lane + 32] = v[lane + 32];
-  }
-  __syncthreads();
+  const int hw = tid >> 4, hl = tid & 15;
   float qr[REP][4];
 #pragma unroll
   for (int j = 0; j < REP; ++j) {
@@ -378,22 +358,20 @@ __global__ void __launch_bounds__(256) cross_attn_kernel(const float *__restrict
     qr[j][2] = t.z;
     qr[j][3] = t.w;
   }
-  const float scale = a.scale;
-  const float *kb = kplane + off * kvd + g * HD + hl * 4;
-  // scores: in each 64-token block, half-warp hw handles tokens hw + 16u
-  // (u = 0..3, four rows in flight).  The loop bound is uniform over the
-  // block so both halves of a warp always reach the shuffles together.
-  for (int base = 0; base < T; base += 64) {
-    const int t0 = base + hw;
-    float4 kv[4];
+  kb += hl * 4;
+  vb += hl * 4;
+  // Scores.  The loop bound is uniform over the block so both halves of a
+  // warp always reach the shuffles together.
+  for (int base = 0; base < T; base += SPAN) {
+    float4 kv[UNR];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      int t = t0 + u * 16;
+    for (int u = 0; u < UNR; ++u) {
+      int t = base + hw + u * NHW;
       kv[u] = t < T ? __ldg(reinterpret_cast<const float4 *>(kb + (int64_t)t * kvd)) : make_float4(0, 0, 0, 0);
     }
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      int t = t0 + u * 16;
+    for (int u = 0; u < UNR; ++u) {
+      int t = base + hw + u * NHW;
 #pragma unroll
       for (int j = 0; j < REP; ++j) {
         float d = qr[j][0] * kv[u].x + qr[j][1] * kv[u].y + qr[j][2] * kv[u].z + qr[j][3] * kv[u].w;
@@ -404,61 +382,57 @@ __global__ void __launch_bounds__(256) cross_attn_kernel(const float *__restrict
     }
   }
   __syncthreads();
-  // softmax per head (ops.rs:5-36): block max and sum
-  float *stat = red;  // reuse: [REP][8] maxes then sums
+  float *stat = red;  // [REP][NW]: maxes, then sums
   float mx[REP], inv[REP];
 #pragma unroll
   for (int j = 0; j < REP; ++j) {
     float m = -INFINITY;
-    for (int t = tid; t < T; t += 256) m = fmaxf(m, sc[j * T + t]);
+    for (int t = tid; t < T; t += NT) m = fmaxf(m, sc[j * T + t]);
     m = warp_max(m);
-    if (lane == 0) stat[j * 8 + warp] = m;
+    if (lane == 0) stat[j * NW + warp] = m;
   }
   __syncthreads();
 #pragma unroll
   for (int j = 0; j < REP; ++j) {
-    float m = stat[j * 8];
-    for (int w = 1; w < 8; ++w) m = fmaxf(m, stat[j * 8 + w]);
+    float m = stat[j * NW];
+    for (int w = 1; w < NW; ++w) m = fmaxf(m, stat[j * NW + w]);
     mx[j] = m;
   }
   __syncthreads();
 #pragma unroll
   for (int j = 0; j < REP; ++j) {
-    float s = 0.0f;
-    for (int t = tid; t < T; t += 256) {
+    float sum = 0.0f;
+    for (int t = tid; t < T; t += NT) {
       float p = expf(sc[j * T + t] - mx[j]);
       sc[j * T + t] = p;
-      s += p;
+      sum += p;
     }
-    s = warp_sum(s);
-    if (lane == 0) stat[j * 8 + warp] = s;
+    sum = warp_sum(sum);
+    if (lane == 0) stat[j * NW + warp] = sum;
   }
   __syncthreads();
 #pragma unroll
   for (int j = 0; j < REP; ++j) {
-    float s = 0.0f;
-    for (int w = 0; w < 8; ++w) s += stat[j * 8 + w];
-    inv[j] = 1.0f / s;
+    float sum = 0.0f;
+    for (int w = 0; w < NW; ++w) sum += stat[j * NW + w];
+    inv[j] = 1.0f / sum;
   }
   __syncthreads();
-  // O = P V: half-warp hw accumulates tokens hw, hw+16, ... for dims hl*4..
   float acc[REP][4];
 #pragma unroll
   for (int j = 0; j < REP; ++j)
 #pragma unroll
     for (int e = 0; e < 4; ++e) acc[j][e] = 0.0f;
-  const float *vb = vplane + off * kvd + g * HD + hl * 4;
-  for (int base = 0; base < T; base += 64) {
-    const int t0 = base + hw;
-    float4 vv[4];
+  for (int base = 0; base < T; base += SPAN) {
+    float4 vv[UNR];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      int t = t0 + u * 16;
+    for (int u = 0; u < UNR; ++u) {
+      int t = base + hw + u * NHW;
       vv[u] = t < T ? __ldg(reinterpret_cast<const float4 *>(vb + (int64_t)t * kvd)) : make_float4(0, 0, 0, 0);
     }
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      int t = t0 + u * 16;
+    for (int u = 0; u < UNR; ++u) {
+      int t = base + hw + u * NHW;
       if (t < T) {
 #pragma unroll
         for (int j = 0; j < REP; ++j) {
@@ -476,12 +450,94 @@ __global__ void __launch_bounds__(256) cross_attn_kernel(const float *__restrict
     *reinterpret_cast<float4 *>(red + (hw * REP + j) * HD + hl * 4) =
         make_float4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]);
   __syncthreads();
-  for (int i = tid; i < REP * HD; i += 256) {
+  for (int i = tid; i < REP * HD; i += NT) {
     int j = i / HD, d = i - j * HD;
-    float s = 0.0f;
-    for (int w = 0; w < 16; ++w) s += red[(w * REP + j) * HD + d];
-    out[(int64_t)b * qd + (g * REP + j) * HD + d] = s;
+    float sum = 0.0f;
+    for (int w = 0; w < NHW; ++w) sum += red[(w * REP + j) * HD + d];
+    out_row[j * HD + d] = sum;
   }
+}
+
+// Decoder cross-attention (attn.rs:281-337).  CTA = (request, KV head).  The
+// dominant HBM reader of batched decode: each CTA streams its request's
+// encoder K then V rows exactly once.
+template <int REP>
+__global__ void __launch_bounds__(256) cross_attn_kernel(const float *__restrict__ q, const float *__restrict__ qn,
+                                                         const float *__restrict__ kplane,
+                                                         const float *__restrict__ vplane,
+                                                         const int64_t *__restrict__ seq_off, float *out,
+                                                         AttnDims a) {
+  constexpr int HD = 64;
+  extern __shared__ __align__(16) float sm[];
+  const int b = blockIdx.y, g = blockIdx.x;
+  const int64_t off = seq_off[b];
+  const int T = (int)(seq_off[b + 1] - off);
+  const int kvd = a.KVH * HD, qd = a.H * HD;
+  float *qs = sm;                   // [REP][64]
+  float *red = sm + REP * HD;       // [16][REP][64]
+  float *sc = red + 16 * REP * HD;  // [REP][T]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp < REP) {  // q heads of this group, q_norm (attn.rs:296-300); no RoPE
+    float *v = qs + warp * HD;
+    const float *src = q + (int64_t)b * qd + (g * REP + warp) * HD;
+    v[lane] = src[lane];
+    v[lane + 32] = src[lane + 32];
+    __syncwarp();
+    norm_rope_head(v, HD, qn, nullptr, nullptr, false, lane);
+  }
+  __syncthreads();
+  attend_hd64<REP, 256>(qs, kplane + off * kvd + g * HD, vplane + off * kvd + g * HD, kvd, T, a.scale, sc, red,
+                        out + (int64_t)b * qd + g * REP * HD);
+}
+
+// Decoder self-attention, head dim 64 (attn.rs:100-183).  CTA = (request, KV
+// head), 128 threads: warps 0..REP-1 ZCRMSNorm + RoPE (position pos[b]) the
+// group's query heads, warp REP does the same to the key and appends k, v to
+// the cache row pos[b] (push_kv saturates at cap, attn.rs:53-61), then the
+// group attends over the cache.
+template <int REP>
+__global__ void __launch_bounds__(128) self_attn_hd64_kernel(const float *__restrict__ qkv,
+                                                             const int32_t *__restrict__ step,
+                                                             const float *__restrict__ qn,
+                                                             const float *__restrict__ kn,
+                                                             const float *__restrict__ rc,
+                                                             const float *__restrict__ rs, float *kc, float *vc,
+                                                             int cap, float *out, AttnDims a) {
+  constexpr int HD = 64;
+  extern __shared__ __align__(16) float sm[];
+  const int b = blockIdx.y, g = blockIdx.x;
+  const int qd = a.H * HD, kvd = a.KVH * HD, ld = qd + 2 * kvd;
+  float *qs = sm;                  // [REP][64]
+  float *red = sm + REP * HD;      // [8][REP][64]
+  float *sc = red + 8 * REP * HD;  // [REP][cap]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int pos = step[b];
+  const bool append = pos < cap;
+  const float *row = qkv + (int64_t)b * ld;
+  float *kcb = kc + (int64_t)b * cap * kvd + g * HD;
+  float *vcb = vc + (int64_t)b * cap * kvd + g * HD;
+  const float *cr = rc + (int64_t)pos * (HD / 2), *sr = rs + (int64_t)pos * (HD / 2);
+  if (warp < REP) {
+    float *v = qs + warp * HD;
+    const float *src = row + (g * REP + warp) * HD;
+    v[lane] = src[lane];
+    v[lane + 32] = src[lane + 32];
+    __syncwarp();
+    norm_rope_head(v, HD, qn, cr, sr, true, lane);
+  } else if (warp == REP && append) {
+    float *kd = kcb + (int64_t)pos * kvd;
+    const float *ks = row + qd + g * HD, *vs = row + qd + kvd + g * HD;
+    kd[lane] = ks[lane];
+    kd[lane + 32] = ks[lane + 32];
+    __syncwarp();
+    norm_rope_head(kd, HD, kn, cr, sr, true, lane);
+    float *vd = vcb + (int64_t)pos * kvd;
+    vd[lane] = vs[lane];
+    vd[lane + 32] = vs[lane + 32];
+  }
+  __syncthreads();  // the appended row is visible to the whole block
+  attend_hd64<REP, 128>(qs, kcb, vcb, kvd, append ? pos + 1 : cap, a.scale, sc, red,
+                        out + (int64_t)b * qd + g * REP * HD);
 }
 
 // Generic cross-attention for head dims other than 64 (small test models).
@@ -550,6 +606,7 @@ cudaError_t init_attention_kernels() {
   set((const void *)encoder_attn_kernel);
   set((const void *)dec_self_attn_kernel);
   set((const void *)cross_attn_kernel<2>);
+  set((const void *)self_attn_hd64_kernel<2>);
   set((const void *)cross_attn_generic_kernel);
   return e;
 }
@@ -604,6 +661,13 @@ cudaError_t decoder_self_attention(const float *qkv, const int32_t *step, const 
                                    float *vc, int cap, int B, float *out, AttnDims a, cudaStream_t st) {
   if (B <= 0) return cudaSuccess;
   if (a.HD > 128 || (a.HD & 1) || cap <= 0) return cudaErrorInvalidValue;
+  if (a.HD == 64 && a.H == 2 * a.KVH) {
+    size_t sm = ((size_t)2 * 64 + (size_t)8 * 2 * 64 + (size_t)2 * cap) * sizeof(float);
+    if (sm > kMaxDynSmem) return cudaErrorInvalidValue;
+    self_attn_hd64_kernel<2><<<dim3(a.KVH, B), 128, sm, st>>>(qkv, step, q_norm, k_norm, rope_cos, rope_sin, kc,
+                                                               vc, cap, out, a);
+    return cudaGetLastError();
+  }
   size_t sm = ((size_t)a.H * a.HD + (size_t)a.H * cap) * sizeof(float);
   if (sm > kMaxDynSmem) return cudaErrorInvalidValue;
   dec_self_attn_kernel<<<B, 256, sm, st>>>(qkv, step, q_norm, k_norm, rope_cos, rope_sin, kc, vc, cap, out, a);

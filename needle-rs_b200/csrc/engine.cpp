@@ -342,6 +342,19 @@ std::unique_ptr<DevModel> load_model(std::vector<uint8_t> raw, int device, std::
   }
   m->emb_bf16_exact = st.is_bf16_exact("embedding");
   if (!L.upload(m->emb, emb.data(), emb.size())) return nullptr;
+  {
+    const int Kp = tc_padded_k(d);
+    __nv_bfloat16 *hi = nullptr, *lo = nullptr;
+    if (!L.dalloc(hi, (size_t)V * Kp) || !L.dalloc(lo, (size_t)V * Kp)) return nullptr;
+    if (tc_split_rows(m->emb, d, V, d, Kp, hi, lo, m->stream) != cudaSuccess ||
+        cudaStreamSynchronize(m->stream) != cudaSuccess) {
+      err = "embedding staging failed";
+      return nullptr;
+    }
+    m->emb_hi = hi;
+    m->emb_lo = lo;
+    m->emb_tc_ready = tc_make_planes(hi, lo, V, Kp, 128, m->emb_tc) == cudaSuccess;
+  }
 
   auto load_ffn = [&](const std::string &p, Lin &gu, Lin &down, float *&norm, float &gate) {
     HostQW g, u, dn;
@@ -834,7 +847,24 @@ bool Batch::decode_step(std::string &err, bool capture) {
   NDL_LK(rms_norm_rows(x_, d, h_, d, m.dec_final_norm, B, d, st));  // model.rs:263
   cudaEvent_t ev;
   if (!tbegin(TIME_HEAD, capture, ev, err)) return false;
-  NDL_LK(head_argmax(h_, B, m.emb, c.vocab_size, d, mask_, W_, logits_, spec_.max_new, pos_, keys_, st));
+  const TcPlanes *hp = nullptr;
+  if (B >= kTcMinRows && m.emb_tc_ready)
+    for (auto &t : tc_maps_)
+      if (t.Kp == m.emb_tc.Kp && B <= t.rows) hp = &t;
+  if (hp) {  // logits on the tensor cores, mask + argmax in the epilogue
+    NDL_LK(tc_split_rows(h_, d, B, d, hp->Kp, tc_hi_, tc_lo_, st));
+    MatmulOut o;
+    o.epi = EPI_ARGMAX;
+    o.mask = mask_;
+    o.mask_words = W_;
+    o.max_new = spec_.max_new;
+    o.pos = pos_;
+    o.keys = keys_;
+    o.logits = logits_;
+    NDL_LK(tc_matmul(*hp, B, m.emb_tc, c.vocab_size, o, m.kerr, st, m.emb_bf16_exact));
+  } else {
+    NDL_LK(head_argmax(h_, B, m.emb, c.vocab_size, d, mask_, W_, logits_, spec_.max_new, pos_, keys_, st));
+  }
   if (!tend(ev, 2.0 * B * c.vocab_size * (double)d,
             (double)c.vocab_size * d * 4 + (double)B * d * 4 + (mask_ ? (double)B * W_ * 8 : 0.0), err))
     return false;

@@ -69,6 +69,11 @@ struct DevModel {
   float embed_scale = 0.0f;
   float *emb = nullptr;        // [V][d] f32
   bool emb_bf16_exact = false;
+  // tensor-core staging of the embedding for the batched head: bf16 hi/lo
+  // planes [V][Kp] (lo all zero when the embedding is bf16-exact)
+  void *emb_hi = nullptr, *emb_lo = nullptr;
+  bool emb_tc_ready = false;
+  TcPlanes emb_tc;
   std::vector<EncLayerDev> enc;
   std::vector<DecLayerDev> dec;
   Lin cross_kv;                // all decoder layers' cross wk|wv: [d, L*2*KVH*HD]

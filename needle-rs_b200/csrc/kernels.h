@@ -34,6 +34,9 @@ enum Epilogue : int {
   EPI_ACT = 2,    // columns interleaved (gate_i, up_i) -> y[i] = act(gate_i, up_i)
   EPI_KNORM = 3,  // y = acc, then per-64-column ZCRMSNorm with `vec` on blocks
                   // whose column-block index is even (the K half of K|V pairs)
+  EPI_ARGMAX = 4, // output head: acc = logit of (row m, vocab n); add the mask,
+                  // reduce to atomicMax(keys[m], (total-order key, n)); logits
+                  // optionally stored (engine.rs:294-304)
 };
 
 enum Activation : int { ACT_DRELU = 0, ACT_SWIGLU = 1, ACT_GELU = 2 };
@@ -47,6 +50,14 @@ struct MatmulOut {
   float gate = 0.0f;
   int act = ACT_DRELU;
   const float *vec = nullptr;  // EPI_KNORM: k_norm scale [64]
+  // EPI_ARGMAX: request m is at step pos[m]; mask row (or NULL) at
+  // mask + (m*max_new + pos[m]) * mask_words; logits (or NULL) at
+  // logits + (m*max_new + pos[m]) * N.
+  const uint64_t *mask = nullptr;
+  int mask_words = 0, max_new = 0;
+  const int32_t *pos = nullptr;
+  unsigned long long *keys = nullptr;
+  float *logits = nullptr;
 };
 
 // Y[M, N] (epilogue) X[M, K] @ W.  x row stride ldx (floats).
@@ -73,8 +84,10 @@ cudaError_t tc_split_rows(const float *x, int64_t ldx, int M, int K, int Kp, voi
 // Y[M, N] (epilogue) A @ B^T with A planes [M][Kp] and B planes [N][Kp]
 // (tcgen05, 3-term bf16 split, f32 accumulation).  *err is set if a bounded
 // wait inside the kernel expired.
+// b_lo_zero: B's lo plane is all zero (a bf16-exact operand such as the
+// embedding), so the hi*lo product is skipped.
 cudaError_t tc_matmul(const TcPlanes &A, int M, const TcPlanes &B, int N, const MatmulOut &o, int *err,
-                      cudaStream_t st);
+                      cudaStream_t st, bool b_lo_zero = false);
 cudaError_t init_tc_kernels();
 
 // Device packing / unpacking (quant.rs:63-155), bit-exact with the reference.

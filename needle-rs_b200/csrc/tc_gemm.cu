@@ -203,11 +203,39 @@ __device__ __forceinline__ void epi_row(const TcEpi &e, int m, int n0, float *v,
   }
 }
 
+// EPI_ARGMAX over 32 columns n0.. of row m: masked logits -> best key.
+__device__ __forceinline__ unsigned long long epi_argmax32(const TcEpi &e, int m, int n0, const float *v) {
+  const MatmulOut &o = e.o;
+  const int step = o.pos[m];
+  const uint64_t *mrow = o.mask ? o.mask + ((int64_t)m * o.max_new + step) * o.mask_words : nullptr;
+  float *lrow = o.logits ? o.logits + ((int64_t)m * o.max_new + step) * e.N : nullptr;
+  uint64_t bits = ~0ull;
+  if (mrow) {  // the 32 columns lie in one or two 64-bit words
+    uint64_t w0 = mrow[n0 >> 6];
+    uint64_t w1 = ((n0 & 63) + 32 > 64) ? mrow[(n0 >> 6) + 1] : 0ull;
+    int sh = n0 & 63;
+    bits = sh ? ((w0 >> sh) | (w1 << (64 - sh))) : w0;
+  }
+  unsigned long long best = 0ull;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    int n = n0 + j;
+    if (n < e.N) {
+      // the engine always adds the mask vector (0.0 when allowed), so -0.0 -> +0.0
+      float mv = v[j] + (((bits >> j) & 1ull) ? 0.0f : kMaskBlocked);
+      if (lrow) lrow[n] = mv;
+      unsigned long long k = argmax_key(mv, (uint32_t)n);
+      best = k > best ? k : best;
+    }
+  }
+  return best;
+}
+
 template <int BN>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
                    const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl, int M, int N,
-                   int Kp, TcEpi e, int *err) {
+                   int Kp, TcEpi e, int *err, int b_lo_zero) {
   constexpr int A_BYTES = TC_BM * TC_BK * 2, B_BYTES = BN * TC_BK * 2;
   constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
   constexpr uint32_t IDESC = umma_idesc(BN);
@@ -303,7 +331,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           for (int k = 0; k < TC_BK / 16; ++k) {
             const uint64_t adv = (uint64_t)((k * 32) >> 4);  // 16 bf16 = 32 bytes along K
             umma_bf16(d, ah + adv, bh + adv, IDESC, (kb | k) ? 1u : 0u);
-            umma_bf16(d, ah + adv, bl + adv, IDESC, 1u);
+            if (!b_lo_zero) umma_bf16(d, ah + adv, bl + adv, IDESC, 1u);
             umma_bf16(d, al + adv, bh + adv, IDESC, 1u);
           }
           umma_commit(&empty[stage]);  // frees the stage once these MMAs complete
@@ -326,14 +354,23 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const int mt = t / num_n, nt = t - mt * num_n;
       const int m = mt * TC_BM + q * 32 + lane;
       const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
-      const bool knorm = e.o.epi == EPI_KNORM;
+      const bool knorm = e.o.epi == EPI_KNORM, amax = e.o.epi == EPI_ARGMAX;
+      unsigned long long best = 0ull;
       for (int c = 0; c < BN; c += (knorm ? 64 : 32)) {
         float v[64];
         tmem_ld32(base + c, v);
         if (knorm) tmem_ld32(base + c + 32, v + 32);
         const int n0 = nt * BN + c;
-        if (m < M && n0 < N) epi_row(e, m, n0, v, knorm ? 64 : 32);
+        if (m < M && n0 < N) {
+          if (amax) {
+            unsigned long long k = epi_argmax32(e, m, n0, v);
+            best = k > best ? k : best;
+          } else {
+            epi_row(e, m, n0, v, knorm ? 64 : 32);
+          }
+        }
       }
+      if (amax && m < M) atomicMax(e.o.keys + m, best);
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       mbar_arrive(&tempty[buf]);
     }
@@ -456,20 +493,25 @@ cudaError_t tc_split_rows(const float *x, int64_t ldx, int M, int K, int Kp, voi
 }
 
 cudaError_t tc_matmul(const TcPlanes &A, int M, const TcPlanes &B, int N, const MatmulOut &o, int *err,
-                      cudaStream_t st) {
+                      cudaStream_t st, bool b_lo_zero) {
   if (M <= 0 || N <= 0) return cudaSuccess;
   if (A.Kp != B.Kp || A.box_rows != TC_BM || B.box_rows != 128 || M > A.rows || N > B.rows)
     return cudaErrorInvalidValue;
   if (o.col_block && (o.col_block % 64)) return cudaErrorInvalidValue;
   if (o.epi == EPI_KNORM && (!o.col_block || !o.vec)) return cudaErrorInvalidValue;
-  if ((o.ldy % 4) || ((uintptr_t)o.y % 16) || (o.col_block && (o.block_stride % 4))) return cudaErrorInvalidValue;
+  if (o.epi == EPI_ARGMAX) {
+    if (!o.keys || !o.pos || (o.mask && o.mask_words * 64 < N)) return cudaErrorInvalidValue;
+  } else if ((o.ldy % 4) || ((uintptr_t)o.y % 16) || (o.col_block && (o.block_stride % 4))) {
+    return cudaErrorInvalidValue;
+  }
   if (o.epi == EPI_ACT && (N & 1)) return cudaErrorInvalidValue;
   TcEpi e{o, N};
   const int tiles = ((M + TC_BM - 1) / TC_BM) * ((N + 127) / 128);
   const int grid = tiles < tc_sm_count() ? tiles : tc_sm_count();
   tc_gemm_kernel<128><<<grid, TC_THREADS, tc_smem_bytes(128), st>>>(
       *reinterpret_cast<const CUtensorMap *>(A.hi), *reinterpret_cast<const CUtensorMap *>(A.lo),
-      *reinterpret_cast<const CUtensorMap *>(B.hi), *reinterpret_cast<const CUtensorMap *>(B.lo), M, N, A.Kp, e, err);
+      *reinterpret_cast<const CUtensorMap *>(B.hi), *reinterpret_cast<const CUtensorMap *>(B.lo), M, N, A.Kp, e, err,
+      b_lo_zero ? 1 : 0);
   return cudaGetLastError();
 }
 

@@ -593,6 +593,29 @@ bool Batch::prepare(const BatchSpec &spec, std::string &err) {
     chunks_.push_back(ch);
     r = ch.r1;
   }
+  // tensor-core encoder attention: head dim 64, work items (request, 128-row
+  // query tile, Q head) per chunk
+  tc_attn_ = hd == 64 && (c.num_heads % c.num_kv_heads) == 0;
+  if (tc_attn_) {
+    std::vector<int32_t> it;
+    std::vector<size_t> start;
+    for (auto &ch : chunks_) {
+      start.push_back(it.size() / 4);
+      for (int r = ch.r0; r < ch.r1; ++r) {
+        int T = (int)(off_h_[r + 1] - off_h_[r]);
+        for (int qt = 0; qt < (T + 127) / 128; ++qt)
+          for (int h = 0; h < c.num_heads; ++h) it.insert(it.end(), {r - ch.r0, qt, h, 0});
+      }
+    }
+    int32_t *dit = alloc<int32_t>(it.size(), err);
+    if (!dit) return false;
+    NDL_CK(cudaMemcpyAsync(dit, it.data(), it.size() * 4, cudaMemcpyHostToDevice, st));
+    for (size_t i = 0; i < chunks_.size(); ++i) {
+      size_t end = i + 1 < chunks_.size() ? start[i + 1] : it.size() / 4;
+      chunks_[i].items = dit + 4 * start[i];
+      chunks_[i].n_items = (int)(end - start[i]);
+    }
+  }
   int64_t nrel = 0;
   for (auto &ch : chunks_) nrel += ch.r1 - ch.r0 + 1;
   int64_t *rel = alloc<int64_t>(nrel, err);
@@ -610,6 +633,18 @@ bool Batch::prepare(const BatchSpec &spec, std::string &err) {
       !(pqkv_ = alloc<float>(ct * qkvd, err)) || !(patt_ = alloc<float>(ct * qd, err)))
     return false;
   if (!c.no_feedforward && !(pffn_ = alloc<float>(ct * c.ffn_dim, err))) return false;
+  if (tc_attn_) {
+    void *pb[6];
+    const int64_t slab = ct;
+    for (int i = 0; i < 6; ++i) {
+      size_t n = (size_t)(i < 2 ? c.num_heads : c.num_kv_heads) * slab * 64;
+      if (!(pb[i] = alloc<__nv_bfloat16>(n, err))) return false;
+      // rows past a chunk's last request are read (and given zero weight)
+      // by the last query tile: keep them finite
+      NDL_CK(cudaMemsetAsync(pb[i], 0, n * 2, st));
+    }
+    if (attn_planes_make(pb, c.num_heads, c.num_kv_heads, (int)slab, attn_planes_) != cudaSuccess) tc_attn_ = false;
+  }
   if (L > 0 && !(kv_planes_ = alloc<float>((size_t)2 * L * ttot_ * kvd, err))) return false;
   {  // tensor-core staging planes, shared by every batched GEMM of the call
     const int64_t rows = std::max<int64_t>(ct, B);
@@ -734,11 +769,19 @@ bool Batch::prefill(std::string &err) {
       o.y = pqkv_;
       o.ldy = qkvd;
       if (!mm(TIME_PREFILL_MATMUL, false, pxn_, d, rows, E.qkv, o, err)) return false;
-      NDL_LK(qk_norm_rope_rows(pqkv_, rows, tok_pos_ + ch.tok0, E.q_norm, E.k_norm, m.rope_cos, m.rope_sin, m.ad, st));
+      if (!tc_attn_)
+        NDL_LK(qk_norm_rope_rows(pqkv_, rows, tok_pos_ + ch.tok0, E.q_norm, E.k_norm, m.rope_cos, m.rope_sin, m.ad,
+                                 st));
+      else
+        NDL_LK(qkv_post(pqkv_, rows, tok_pos_ + ch.tok0, E.q_norm, E.k_norm, m.rope_cos, m.rope_sin, m.ad,
+                        attn_planes_, st));
       {
         cudaEvent_t ev;
         if (!tbegin(TIME_ENCODER_ATTENTION, false, ev, err)) return false;
-        NDL_LK(encoder_attention(pqkv_, ch.rel_off, nr, ch.tmax, patt_, m.ad, st));
+        if (tc_attn_)
+          NDL_LK(encoder_attention_tc(attn_planes_, ch.rel_off, ch.items, ch.n_items, patt_, m.ad, m_->kerr, st));
+        else
+          NDL_LK(encoder_attention(pqkv_, ch.rel_off, nr, ch.tmax, patt_, m.ad, st));
         double Tq = 0.0;  // sum of T^2 over the chunk's requests
         for (int r = ch.r0; r < ch.r1; ++r) Tq += std::pow((double)(off_h_[r + 1] - off_h_[r]), 2.0);
         if (!tend(ev, 4.0 * Tq * c.num_heads * hd, (double)rows * (qkvd + qd) * 4, err)) return false;

@@ -181,6 +181,8 @@ class Batch {
     int64_t tok0, ntok;
     int tmax;
     int64_t *rel_off;  // device [r1-r0+1], chunk-relative offsets
+    void *items;       // device int4 work items of the tensor-core encoder attention
+    int n_items;
   };
   std::vector<Chunk> chunks_;
   int64_t chunk_tok_max_ = 0;
@@ -191,6 +193,9 @@ class Batch {
   // decoder state
   float *self_k_ = nullptr, *self_v_ = nullptr;  // [L][B][cap][KVH*HD]
   float *x_ = nullptr, *xn_ = nullptr, *qkv_ = nullptr, *att_ = nullptr, *q_ = nullptr, *h_ = nullptr, *ffn_ = nullptr;
+  // tensor-core encoder attention planes (per prefill chunk)
+  bool tc_attn_ = false;
+  AttnPlanes attn_planes_;
   // tensor-core activation staging (bf16 hi/lo planes) and its TMA maps
   void *tc_hi_ = nullptr, *tc_lo_ = nullptr;
   std::vector<TcPlanes> tc_maps_;  // one per distinct padded K

@@ -241,6 +241,7 @@ cudaError_t init_kernels() {
   if (e == cudaSuccess) e = init_attention_kernels();
   if (e == cudaSuccess) e = init_head_kernels();
   if (e == cudaSuccess) e = init_tc_kernels();
+  if (e == cudaSuccess) e = init_tc_attn_kernels();
   return e;
 }
 

@@ -11,6 +11,11 @@ namespace ndl {
 
 constexpr uint32_t kEosId = 1;  // tokenizer.rs:23 EOS_ID, also the decoder start token
 
+struct AttnDims {
+  int H = 8, KVH = 4, HD = 64;
+  float scale = 0.125f;  // powf(hd, -0.5) computed on the host (attn.rs:142)
+};
+
 // Packed INT4 weight in the reference layout (quant.rs:45-58):
 //   w[pair * N + n]: low nibble = row 2*pair, high nibble = row 2*pair+1
 //   s[g * N + n]:    f32 scale of group g = row / gs, gs = min(32, K)
@@ -90,6 +95,26 @@ cudaError_t tc_matmul(const TcPlanes &A, int M, const TcPlanes &B, int N, const 
                       cudaStream_t st, bool b_lo_zero = false);
 cudaError_t init_tc_kernels();
 
+// ── tensor-core encoder attention (tc_attn.cu) ──
+// Per-head bf16 hi/lo planes of the normed + RoPE'd Q, K and the V of one
+// prefill chunk: Q [H][slab][64], K and V [KVH][slab][64] (buf: qh ql kh kl
+// vh vl), with their TMA maps.
+struct AttnPlanes {
+  void *buf[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+  int slab = 0;
+  TcPlanes q, k, v;
+};
+cudaError_t attn_planes_make(void *const bufs[6], int H, int KVH, int slab, AttnPlanes &p);
+// ZCRMSNorm + RoPE (positions pos[row]) of the Q and K heads of fused QKV
+// rows, then the bf16 hi/lo split of Q, K and V into the planes.  HD = 64.
+cudaError_t qkv_post(const float *qkv, int rows, const int32_t *pos, const float *q_norm, const float *k_norm,
+                     const float *rope_cos, const float *rope_sin, AttnDims a, const AttnPlanes &p, cudaStream_t st);
+// Bidirectional attention over the planes: items = int4 (request, 128-row
+// query tile, Q head, 0) against chunk-relative seq_off; out [rows][H*64].
+cudaError_t encoder_attention_tc(const AttnPlanes &p, const int64_t *seq_off, const void *items, int n_items,
+                                 float *out, AttnDims a, int *err, cudaStream_t st);
+cudaError_t init_tc_attn_kernels();
+
 // Device packing / unpacking (quant.rs:63-155), bit-exact with the reference.
 cudaError_t int4_quantize(const float *w, int K, int N, uint8_t *data, float *scales, cudaStream_t st);
 cudaError_t int4_dequantize(const uint8_t *data, const float *scales, int K, int N, int G, float *out,
@@ -103,10 +128,7 @@ cudaError_t rms_norm_rows(const float *x, int64_t ldx, float *out, int64_t ldo, 
 cudaError_t embed_rows(const uint32_t *ids, const float *emb, float *x, int rows, int d, float embed_scale,
                        cudaStream_t st);
 
-struct AttnDims {
-  int H = 8, KVH = 4, HD = 64;
-  float scale = 0.125f;  // powf(hd, -0.5) computed on the host (attn.rs:142)
-};
+
 
 // Largest dynamic shared memory any kernel here is allowed to request.
 constexpr int kMaxDynSmem = 200 * 1024;

@@ -1,0 +1,406 @@
+// tc_attn.cu — encoder self-attention on the tcgen05 tensor cores.
+//
+// Reference: self_attn_full (crates/needle-core/src/attn.rs:189-273): per
+// token and Q head, scores = (q . k) * hd^-0.5 over every key of the request
+// (bidirectional, GQA: Q head h reads KV head h / (H / KVH)), softmax, P V.
+//
+// Layout.  qkv_post_kernel turns the f32 output of the fused QKV projection
+// into per-head bf16 planes with the ZCRMSNorm + RoPE of attn.rs:218-235
+// applied in f32 first: Q [H][rows][64], K and V [KVH][rows][64], each as a
+// hi/lo pair (hi = bf16(v), lo = bf16(v - hi)).
+//
+// Kernel.  Persistent; a work item is (request, 128-query tile, Q head).
+// 256 threads: warp 0 TMA (Q tile once, then K/V tiles of 128 keys through a
+// 2-stage ring), warp 1 TMEM allocation + MMA issue, warps 4-7 softmax (one
+// thread per query row).  Per key tile j:
+//   S_j = Q K_j^T                       tcgen05.mma M128 N128 K16, A and B
+//                                       K-major, f32 in TMEM (2 buffers, so
+//                                       S_{j+1} runs during softmax_j)
+//   p = exp(S*scale - m), online max/sum per row in registers
+//   P_j -> shared memory as bf16 hi/lo (K-major, 128-byte swizzle)
+//   O_j = P_j V_j                       M128 N64 K16, V read MN-major straight
+//                                       from its [key][dim] tile
+//   O = O * exp(m_old - m_new) + O_j    in registers
+// Each product is the 3-term split hi*hi + hi*lo + lo*hi (about 1e-6
+// relative), so the f32 reference is matched within the logit tolerance.
+// Keys past the request's end get probability 0; query rows past it are
+// computed on neighbouring rows and never stored.  TMA loads never use
+// cluster multicast; every wait is bounded (error flag, then unwind).
+#include <cuda.h>
+#include <cuda_bf16.h>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "tc_common.cuh"
+
+namespace ndl {
+namespace {
+
+using namespace tc;
+
+constexpr int AT_BM = 128, AT_BN = 128, AT_HD = 64, AT_THREADS = 256;
+constexpr int AT_TILE = AT_BM * AT_HD * 2;              // one 128 x 64 bf16 plane tile: 16 KB
+constexpr int AT_Q = 0;                                  // Q hi, Q lo
+constexpr int AT_KV = 2 * AT_TILE;                       // 2 stages x (K hi, K lo, V hi, V lo)
+constexpr int AT_STAGE = 4 * AT_TILE;
+constexpr int AT_P = AT_KV + 2 * AT_STAGE;               // P hi (2 x 16 KB), P lo (2 x 16 KB)
+constexpr int AT_BAR = AT_P + 4 * AT_TILE;               // 229376
+constexpr size_t AT_SMEM = 1024 + AT_BAR + 256;
+
+__device__ __forceinline__ void norm_rope64(float &x0, float &x1, const float *__restrict__ nsc,
+                                            const float *__restrict__ cr, const float *__restrict__ sr, bool rope,
+                                            int lane) {
+  // ZCRMSNorm over a 64-wide head held as (lane, lane + 32) pairs, then the
+  // split-half rotation (norm.rs:23-30, rope.rs:63-75).
+  float ss = x0 * x0 + x1 * x1;
+  ss = warp_sum(ss);
+  float inv = 1.0f / sqrtf(ss / 64.0f + 1e-6f);
+  float a = ((1.0f + __ldg(nsc + lane)) * x0) * inv;
+  float b = ((1.0f + __ldg(nsc + lane + 32)) * x1) * inv;
+  if (rope) {
+    float c = __ldg(cr + lane), s = __ldg(sr + lane);
+    float l = a * c - b * s;
+    float r = b * c + a * s;
+    a = l;
+    b = r;
+  }
+  x0 = a;
+  x1 = b;
+}
+
+__device__ __forceinline__ void split_store(__nv_bfloat16 *hi, __nv_bfloat16 *lo, int64_t i, float v) {
+  __nv_bfloat16 h = __float2bfloat16_rn(v);
+  hi[i] = h;
+  lo[i] = __float2bfloat16_rn(v - __bfloat162float(h));
+}
+
+// One warp per (row, head) over the H + 2*KVH heads of a fused QKV row.
+__global__ void qkv_post_kernel(const float *__restrict__ qkv, int rows, int slab, const int32_t *__restrict__ pos,
+                                const float *__restrict__ qn, const float *__restrict__ kn,
+                                const float *__restrict__ rc, const float *__restrict__ rs, AttnDims a,
+                                __nv_bfloat16 *qh, __nv_bfloat16 *ql, __nv_bfloat16 *kh, __nv_bfloat16 *kl,
+                                __nv_bfloat16 *vh, __nv_bfloat16 *vl) {
+  const int heads = a.H + 2 * a.KVH;
+  int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (w >= (int64_t)rows * heads) return;
+  const int lane = threadIdx.x & 31;
+  const int row = (int)(w / heads), h = (int)(w % heads);
+  const float *src = qkv + (int64_t)row * heads * AT_HD + h * AT_HD;
+  float x0 = src[lane], x1 = src[lane + 32];
+  const int p = pos[row];
+  const float *cr = rc + (int64_t)p * 32, *sr = rs + (int64_t)p * 32;
+  __nv_bfloat16 *dh, *dl;
+  int64_t base;
+  if (h < a.H) {
+    norm_rope64(x0, x1, qn, cr, sr, true, lane);
+    dh = qh;
+    dl = ql;
+    base = ((int64_t)h * slab + row) * AT_HD;
+  } else if (h < a.H + a.KVH) {
+    norm_rope64(x0, x1, kn, cr, sr, true, lane);
+    dh = kh;
+    dl = kl;
+    base = ((int64_t)(h - a.H) * slab + row) * AT_HD;
+  } else {
+    dh = vh;
+    dl = vl;
+    base = ((int64_t)(h - a.H - a.KVH) * slab + row) * AT_HD;
+  }
+  split_store(dh, dl, base + lane, x0);
+  split_store(dh, dl, base + lane + 32, x1);
+}
+
+// 8 probabilities of row r, keys kk0..kk0+7 of the tile, into the K-major
+// 128-byte-swizzled P tiles (hi and lo): [2 blocks of 64 keys][128 rows][128 B].
+__device__ __forceinline__ void store_p8(uint8_t *ph, uint8_t *pl, int r, int kk0, const float *p) {
+  uint32_t hw[4], lw[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __nv_bfloat16 h0 = __float2bfloat16_rn(p[2 * i]), h1 = __float2bfloat16_rn(p[2 * i + 1]);
+    __nv_bfloat16 l0 = __float2bfloat16_rn(p[2 * i] - __bfloat162float(h0));
+    __nv_bfloat16 l1 = __float2bfloat16_rn(p[2 * i + 1] - __bfloat162float(h1));
+    hw[i] = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
+    lw[i] = (uint32_t)__bfloat16_as_ushort(l0) | ((uint32_t)__bfloat16_as_ushort(l1) << 16);
+  }
+  const int blk = kk0 >> 6, chunk = ((kk0 & 63) >> 3) ^ (r & 7);
+  const int off = blk * AT_TILE + (r >> 3) * 1024 + (r & 7) * 128 + chunk * 16;
+  *reinterpret_cast<uint4 *>(ph + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+  *reinterpret_cast<uint4 *>(pl + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+}
+
+__global__ void __launch_bounds__(AT_THREADS, 1)
+    enc_attn_tc_kernel(const __grid_constant__ CUtensorMap tmQh, const __grid_constant__ CUtensorMap tmQl,
+                       const __grid_constant__ CUtensorMap tmKh, const __grid_constant__ CUtensorMap tmKl,
+                       const __grid_constant__ CUtensorMap tmVh, const __grid_constant__ CUtensorMap tmVl,
+                       const int64_t *__restrict__ seq_off, const int4 *__restrict__ items, int n_items, int slab,
+                       float *out, AttnDims a, int *err) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *sm = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t *q_full = (uint64_t *)(sm + AT_BAR);
+  uint64_t *q_empty = q_full + 1;
+  uint64_t *kv_full = q_full + 2;   // [2]
+  uint64_t *kv_empty = q_full + 4;  // [2]
+  uint64_t *s_full = q_full + 6;    // [2]
+  uint64_t *s_empty = q_full + 8;   // [2]
+  uint64_t *p_full = q_full + 10;
+  uint64_t *o_full = q_full + 11;
+  uint64_t *o_empty = q_full + 12;
+  uint32_t *tmem_slot = (uint32_t *)(q_full + 13);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rep = a.H / a.KVH;
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+      mbar_init(&s_full[s], 1);
+      mbar_init(&s_empty[s], 128);
+    }
+    mbar_init(p_full, 128);
+    mbar_init(o_full, 1);
+    mbar_init(o_empty, 128);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {  // S: 2 x 128 columns, O tile: 64 columns
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(512));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *(volatile uint32_t *)tmem_slot;
+  const uint32_t t_o = tmem + 256;
+
+  if (warp == 0) {
+    if (lane == 0) {  // ── TMA producer ──
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++it) {
+        const int4 item = items[w];
+        const int64_t off = seq_off[item.x];
+        const int T = (int)(seq_off[item.x + 1] - off);
+        const int nk = (T + AT_BN - 1) / AT_BN, g = item.z / rep;
+        if (!(ok = mbar_wait(q_empty, (it & 1) ^ 1, err))) break;
+        mbar_expect_tx(q_full, 2 * AT_TILE);
+        const int qrow = item.z * slab + (int)off + item.y * AT_BM;
+        tma_load_2d(sm + AT_Q, &tmQh, q_full, 0, qrow);
+        tma_load_2d(sm + AT_Q + AT_TILE, &tmQl, q_full, 0, qrow);
+        for (int j = 0; j < nk; ++j) {
+          if (!(ok = mbar_wait(&kv_empty[stage], phase ^ 1, err))) break;
+          uint8_t *st = sm + AT_KV + stage * AT_STAGE;
+          const int krow = g * slab + (int)off + j * AT_BN;
+          mbar_expect_tx(&kv_full[stage], AT_STAGE);
+          tma_load_2d(st, &tmKh, &kv_full[stage], 0, krow);
+          tma_load_2d(st + AT_TILE, &tmKl, &kv_full[stage], 0, krow);
+          tma_load_2d(st + 2 * AT_TILE, &tmVh, &kv_full[stage], 0, krow);
+          tma_load_2d(st + 3 * AT_TILE, &tmVl, &kv_full[stage], 0, krow);
+          if (++stage == 2) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // drain: every issued copy consumed before the CTA exits
+      for (int s = 0; s < 2 && ok; ++s) {
+        ok = mbar_wait(&kv_empty[stage], phase ^ 1, err);
+        if (++stage == 2) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (ok) mbar_wait(q_empty, (it & 1) ^ 1, err);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // ── MMA issuer ──
+      constexpr uint32_t ID_S = umma_idesc(AT_BM, AT_BN);
+      constexpr uint32_t ID_PV = umma_idesc(AT_BM, AT_HD, true);
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t jj = 0, pv = 0;
+      int it = 0;
+      bool ok = true;
+      int pv_stage = 0;
+      // O_t = P_t V_t for the tile whose K/V sit in stage `st`
+      auto do_pv = [&](int st) -> bool {
+        if (!mbar_wait(p_full, pv & 1, err) || !mbar_wait(o_empty, (pv & 1) ^ 1, err)) return false;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        uint8_t *kvs = sm + AT_KV + st * AT_STAGE;
+#pragma unroll
+        for (int ks = 0; ks < AT_BN / 16; ++ks) {
+          const int pb = (ks >> 2) * AT_TILE + (ks & 3) * 32;
+          const uint64_t ph = umma_desc(sm + AT_P + pb), pl = umma_desc(sm + AT_P + 2 * AT_TILE + pb);
+          const uint64_t vh = umma_desc_mn(kvs + 2 * AT_TILE + ks * 2048);
+          const uint64_t vl = umma_desc_mn(kvs + 3 * AT_TILE + ks * 2048);
+          umma_bf16(t_o, ph, vh, ID_PV, ks ? 1u : 0u);
+          umma_bf16(t_o, ph, vl, ID_PV, 1u);
+          umma_bf16(t_o, pl, vh, ID_PV, 1u);
+        }
+        umma_commit(o_full);
+        umma_commit(&kv_empty[st]);  // S and PV of this tile are done with its K/V
+        ++pv;
+        return true;
+      };
+      for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++it) {
+        const int4 item = items[w];
+        const int T = (int)(seq_off[item.x + 1] - seq_off[item.x]);
+        const int nk = (T + AT_BN - 1) / AT_BN;
+        if (!(ok = mbar_wait(q_full, it & 1, err))) break;
+        for (int j = 0; j < nk && ok; ++j) {
+          const int sb = jj & 1;
+          if (!(ok = mbar_wait(&kv_full[stage], phase, err))) break;
+          if (!(ok = mbar_wait(&s_empty[sb], ((jj >> 1) & 1) ^ 1, err))) break;
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          uint8_t *kvs = sm + AT_KV + stage * AT_STAGE;
+          const uint32_t d = tmem + (uint32_t)(sb * AT_BN);
+#pragma unroll
+          for (int ks = 0; ks < AT_HD / 16; ++ks) {
+            const uint64_t adv = (uint64_t)((ks * 32) >> 4);
+            const uint64_t qh = umma_desc(sm + AT_Q) + adv, ql = umma_desc(sm + AT_Q + AT_TILE) + adv;
+            const uint64_t kh = umma_desc(kvs) + adv, kl = umma_desc(kvs + AT_TILE) + adv;
+            umma_bf16(d, qh, kh, ID_S, ks ? 1u : 0u);
+            umma_bf16(d, qh, kl, ID_S, 1u);
+            umma_bf16(d, ql, kh, ID_S, 1u);
+          }
+          umma_commit(&s_full[sb]);
+          if (j == nk - 1) umma_commit(q_empty);
+          ++jj;
+          if (j > 0 && !(ok = do_pv(pv_stage))) break;
+          pv_stage = stage;
+          if (++stage == 2) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (ok) ok = do_pv(pv_stage);
+      }
+    }
+  } else if (warp >= 4) {  // ── softmax ──
+    const int q = warp - 4, r = q * 32 + lane;
+    const uint32_t lanes = (uint32_t)(q * 32) << 16;
+    uint32_t jj = 0, pv = 0;
+    for (int w = blockIdx.x; w < n_items; w += gridDim.x) {
+      const int4 item = items[w];
+      const int64_t off = seq_off[item.x];
+      const int T = (int)(seq_off[item.x + 1] - off);
+      const int nk = (T + AT_BN - 1) / AT_BN;
+      float m = -INFINITY, l = 0.0f;
+      float o[AT_HD];
+#pragma unroll
+      for (int e = 0; e < AT_HD; ++e) o[e] = 0.0f;
+      bool ok = true;
+      for (int j = 0; j < nk; ++j) {
+        const int sb = jj & 1;
+        if (!(ok = mbar_wait(&s_full[sb], (jj >> 1) & 1, err))) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t ts = tmem + lanes + (uint32_t)(sb * AT_BN);
+        const int kvalid = T - j * AT_BN;  // keys of this tile that belong to the request
+        float v[32];
+        float mx = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          tmem_ld32(ts + c * 32, v);
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (c * 32 + e < kvalid) mx = fmaxf(mx, v[e] * a.scale);
+        }
+        const float m_new = fmaxf(m, mx);
+        const float corr = expf(m - m_new);  // 0 on the first tile (m = -inf)
+        float psum = 0.0f;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          tmem_ld32(ts + c * 32, v);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            float p = (c * 32 + e < kvalid) ? expf(v[e] * a.scale - m_new) : 0.0f;
+            v[e] = p;
+            psum += p;
+          }
+#pragma unroll
+          for (int e8 = 0; e8 < 4; ++e8) store_p8(sm + AT_P, sm + AT_P + 2 * AT_TILE, r, c * 32 + e8 * 8, v + e8 * 8);
+        }
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        mbar_arrive(&s_empty[sb]);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // P visible to the tensor cores
+        mbar_arrive(p_full);
+        l = l * corr + psum;
+        m = m_new;
+        ++jj;
+        if (!(ok = mbar_wait(o_full, pv & 1, err))) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        tmem_ld32(t_o + lanes, v);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) o[e] = o[e] * corr + v[e];
+        tmem_ld32(t_o + lanes + 32, v);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) o[32 + e] = o[32 + e] * corr + v[e];
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        mbar_arrive(o_empty);
+        ++pv;
+      }
+      if (!ok) break;
+      const int qr = item.y * AT_BM + r;
+      if (qr < T) {
+        const float inv = 1.0f / l;
+        float4 *dst = reinterpret_cast<float4 *>(out + (off + qr) * (int64_t)(a.H * AT_HD) + item.z * AT_HD);
+#pragma unroll
+        for (int e = 0; e < AT_HD / 4; ++e)
+          dst[e] = make_float4(o[4 * e] * inv, o[4 * e + 1] * inv, o[4 * e + 2] * inv, o[4 * e + 3] * inv);
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+  }
+}
+
+}  // namespace
+
+cudaError_t attn_planes_make(void *const bufs[6], int H, int KVH, int slab, AttnPlanes &p) {
+  p.slab = slab;
+  for (int i = 0; i < 6; ++i) p.buf[i] = bufs[i];
+  cudaError_t e = tc_make_planes(bufs[0], bufs[1], H * slab, 64, 128, p.q);
+  if (e == cudaSuccess) e = tc_make_planes(bufs[2], bufs[3], KVH * slab, 64, 128, p.k);
+  if (e == cudaSuccess) e = tc_make_planes(bufs[4], bufs[5], KVH * slab, 64, 128, p.v);
+  return e;
+}
+
+cudaError_t qkv_post(const float *qkv, int rows, const int32_t *pos, const float *q_norm, const float *k_norm,
+                     const float *rope_cos, const float *rope_sin, AttnDims a, const AttnPlanes &p, cudaStream_t st) {
+  if (rows <= 0) return cudaSuccess;
+  if (a.HD != 64 || rows > p.slab) return cudaErrorInvalidValue;
+  int64_t threads = (int64_t)rows * (a.H + 2 * a.KVH) * 32;
+  auto B = [&](int i) { return (__nv_bfloat16 *)p.buf[i]; };
+  qkv_post_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(qkv, rows, p.slab, pos, q_norm, k_norm, rope_cos,
+                                                                       rope_sin, a, B(0), B(1), B(2), B(3), B(4),
+                                                                       B(5));
+  return cudaGetLastError();
+}
+
+cudaError_t encoder_attention_tc(const AttnPlanes &p, const int64_t *seq_off, const void *items, int n_items,
+                                 float *out, AttnDims a, int *err, cudaStream_t st) {
+  if (n_items <= 0) return cudaSuccess;
+  if (a.HD != 64 || (a.H % a.KVH)) return cudaErrorInvalidValue;
+  int sms = 148, dev = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int grid = n_items < sms ? n_items : sms;
+  auto M = [](const unsigned char *m) { return *reinterpret_cast<const CUtensorMap *>(m); };
+  enc_attn_tc_kernel<<<grid, AT_THREADS, AT_SMEM, st>>>(M(p.q.hi), M(p.q.lo), M(p.k.hi), M(p.k.lo), M(p.v.hi),
+                                                        M(p.v.lo), seq_off, (const int4 *)items, n_items, p.slab, out,
+                                                        a, err);
+  return cudaGetLastError();
+}
+
+cudaError_t init_tc_attn_kernels() {
+  return cudaFuncSetAttribute(enc_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)AT_SMEM);
+}
+
+}  // namespace ndl

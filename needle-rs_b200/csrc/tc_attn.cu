@@ -10,9 +10,11 @@
 // hi/lo pair (hi = bf16(v), lo = bf16(v - hi)).
 //
 // Kernel.  Persistent; a work item is (request, 128-query tile, Q head).
-// 256 threads: warp 0 TMA (Q tile once, then K/V tiles of 128 keys through a
-// 2-stage ring), warp 1 TMEM allocation + MMA issue, warps 4-7 softmax (one
-// thread per query row).  Per key tile j:
+// 320 threads: warp 0 TMA (Q tile once, then K/V tiles of 128 keys through a
+// 2-stage ring), warp 1 TMEM allocation + MMA issue, warps 2-9 softmax in two
+// warpgroups: thread = one query row and one half (64 keys) of each S tile;
+// the halves exchange row maxima through shared memory and split the 64
+// output columns.  Per key tile j:
 //   S_j = Q K_j^T                       tcgen05.mma M128 N128 K16, A and B
 //                                       K-major, f32 in TMEM (2 buffers, so
 //                                       S_{j+1} runs during softmax_j)
@@ -38,14 +40,16 @@ namespace {
 
 using namespace tc;
 
-constexpr int AT_BM = 128, AT_BN = 128, AT_HD = 64, AT_THREADS = 256;
+constexpr int AT_BM = 128, AT_BN = 128, AT_HD = 64, AT_THREADS = 320;
 constexpr int AT_TILE = AT_BM * AT_HD * 2;              // one 128 x 64 bf16 plane tile: 16 KB
 constexpr int AT_Q = 0;                                  // Q hi, Q lo
 constexpr int AT_KV = 2 * AT_TILE;                       // 2 stages x (K hi, K lo, V hi, V lo)
 constexpr int AT_STAGE = 4 * AT_TILE;
 constexpr int AT_P = AT_KV + 2 * AT_STAGE;               // P hi (2 x 16 KB), P lo (2 x 16 KB)
-constexpr int AT_BAR = AT_P + 4 * AT_TILE;               // 229376
+constexpr int AT_XCH = AT_P + 4 * AT_TILE;               // row-max / row-sum exchange [2][128] f32
+constexpr int AT_BAR = AT_XCH + 2 * 128 * 4;             // 230400
 constexpr size_t AT_SMEM = 1024 + AT_BAR + 256;
+static_assert(AT_SMEM <= 232448, "exceeds the 227 KB of dynamic shared memory per block");
 
 __device__ __forceinline__ void norm_rope64(float &x0, float &x1, const float *__restrict__ nsc,
                                             const float *__restrict__ cr, const float *__restrict__ sr, bool rope,
@@ -128,6 +132,39 @@ __device__ __forceinline__ void store_p8(uint8_t *ph, uint8_t *pl, int r, int kk
   *reinterpret_cast<uint4 *>(pl + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
 }
 
+// Rendezvous of the 256 softmax threads on an mbarrier (a bounded wait, so a
+// warpgroup that unwinds on an error can never strand the other).
+__device__ __forceinline__ bool xsync(uint64_t *bar, uint32_t &uses, int *err) {
+  mbar_arrive(bar);
+  return mbar_wait(bar, (uses++) & 1, err);
+}
+
+// Two x32 TMEM loads (64 consecutive columns) with a single wait.
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float *v) {
+  uint32_t r[64];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+        "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+        "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+        "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+      : "r"(taddr + 32));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 __global__ void __launch_bounds__(AT_THREADS, 1)
     enc_attn_tc_kernel(const __grid_constant__ CUtensorMap tmQh, const __grid_constant__ CUtensorMap tmQl,
                        const __grid_constant__ CUtensorMap tmKh, const __grid_constant__ CUtensorMap tmKl,
@@ -145,7 +182,8 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
   uint64_t *p_full = q_full + 10;
   uint64_t *o_full = q_full + 11;
   uint64_t *o_empty = q_full + 12;
-  uint32_t *tmem_slot = (uint32_t *)(q_full + 13);
+  uint64_t *xbar = q_full + 13;  // the two softmax warpgroups' exchange rendezvous
+  uint32_t *tmem_slot = (uint32_t *)(q_full + 14);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rep = a.H / a.KVH;
@@ -156,11 +194,12 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
       mbar_init(&s_full[s], 1);
-      mbar_init(&s_empty[s], 128);
+      mbar_init(&s_empty[s], 256);
     }
-    mbar_init(p_full, 128);
+    mbar_init(p_full, 256);
     mbar_init(o_full, 1);
-    mbar_init(o_empty, 128);
+    mbar_init(o_empty, 256);
+    mbar_init(xbar, 256);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {  // S: 2 x 128 columns, O tile: 64 columns
@@ -279,52 +318,52 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         if (ok) ok = do_pv(pv_stage);
       }
     }
-  } else if (warp >= 4) {  // ── softmax ──
-    const int q = warp - 4, r = q * 32 + lane;
-    const uint32_t lanes = (uint32_t)(q * 32) << 16;
-    uint32_t jj = 0, pv = 0;
+  } else {  // ── softmax: warps 2-9, two warpgroups ──
+    const int quarter = warp & 3, wg = (warp - 2) >> 2;
+    const int r = quarter * 32 + lane;  // TMEM lane = query row of the tile
+    const uint32_t lanes = (uint32_t)(quarter * 32) << 16;
+    float *xch = (float *)(sm + AT_XCH);  // [2 groups][128]: row maxima, then row sums
+    uint32_t jj = 0, pv = 0, xu = 0;
     for (int w = blockIdx.x; w < n_items; w += gridDim.x) {
       const int4 item = items[w];
       const int64_t off = seq_off[item.x];
       const int T = (int)(seq_off[item.x + 1] - off);
       const int nk = (T + AT_BN - 1) / AT_BN;
       float m = -INFINITY, l = 0.0f;
-      float o[AT_HD];
+      float o[32];
 #pragma unroll
-      for (int e = 0; e < AT_HD; ++e) o[e] = 0.0f;
+      for (int e = 0; e < 32; ++e) o[e] = 0.0f;
       bool ok = true;
       for (int j = 0; j < nk; ++j) {
         const int sb = jj & 1;
         if (!(ok = mbar_wait(&s_full[sb], (jj >> 1) & 1, err))) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t ts = tmem + lanes + (uint32_t)(sb * AT_BN);
-        const int kvalid = T - j * AT_BN;  // keys of this tile that belong to the request
-        float v[32];
+        float v[64];
+        tmem_ld64(tmem + lanes + (uint32_t)(sb * AT_BN + wg * 64), v);
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        mbar_arrive(&s_empty[sb]);  // S is in registers: the MMA may reuse the buffer
+        const int kvalid = T - j * AT_BN - wg * 64;  // keys of this half that belong to the request
         float mx = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          tmem_ld32(ts + c * 32, v);
-#pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (c * 32 + e < kvalid) mx = fmaxf(mx, v[e] * a.scale);
+        for (int e = 0; e < 64; ++e) {
+          v[e] *= a.scale;
+          if (e < kvalid) mx = fmaxf(mx, v[e]);
         }
-        const float m_new = fmaxf(m, mx);
+        xch[wg * 128 + r] = mx;
+        if (!(ok = xsync(xbar, xu, err))) break;
+        const float m_new = fmaxf(m, fmaxf(mx, xch[(wg ^ 1) * 128 + r]));
+        if (!(ok = xsync(xbar, xu, err))) break;  // both halves read before the next write
         const float corr = expf(m - m_new);  // 0 on the first tile (m = -inf)
         float psum = 0.0f;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          tmem_ld32(ts + c * 32, v);
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            float p = (c * 32 + e < kvalid) ? expf(v[e] * a.scale - m_new) : 0.0f;
-            v[e] = p;
-            psum += p;
-          }
-#pragma unroll
-          for (int e8 = 0; e8 < 4; ++e8) store_p8(sm + AT_P, sm + AT_P + 2 * AT_TILE, r, c * 32 + e8 * 8, v + e8 * 8);
+        for (int e = 0; e < 64; ++e) {
+          float p = (e < kvalid) ? expf(v[e] - m_new) : 0.0f;
+          v[e] = p;
+          psum += p;
         }
-        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-        mbar_arrive(&s_empty[sb]);
+#pragma unroll
+        for (int e8 = 0; e8 < 8; ++e8)
+          store_p8(sm + AT_P, sm + AT_P + 2 * AT_TILE, r, wg * 64 + e8 * 8, v + e8 * 8);
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // P visible to the tensor cores
         mbar_arrive(p_full);
         l = l * corr + psum;
@@ -332,23 +371,26 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         ++jj;
         if (!(ok = mbar_wait(o_full, pv & 1, err))) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        tmem_ld32(t_o + lanes, v);
+        tmem_ld32(t_o + lanes + (uint32_t)(wg * 32), v);
 #pragma unroll
         for (int e = 0; e < 32; ++e) o[e] = o[e] * corr + v[e];
-        tmem_ld32(t_o + lanes + 32, v);
-#pragma unroll
-        for (int e = 0; e < 32; ++e) o[32 + e] = o[32 + e] * corr + v[e];
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
         mbar_arrive(o_empty);
         ++pv;
       }
       if (!ok) break;
+      // combine the two halves' row sums
+      xch[wg * 128 + r] = l;
+      if (!xsync(xbar, xu, err)) break;
+      const float ltot = l + xch[(wg ^ 1) * 128 + r];
+      if (!xsync(xbar, xu, err)) break;  // the exchange area is reused by the next item
       const int qr = item.y * AT_BM + r;
       if (qr < T) {
-        const float inv = 1.0f / l;
-        float4 *dst = reinterpret_cast<float4 *>(out + (off + qr) * (int64_t)(a.H * AT_HD) + item.z * AT_HD);
+        const float inv = 1.0f / ltot;
+        float4 *dst =
+            reinterpret_cast<float4 *>(out + (off + qr) * (int64_t)(a.H * AT_HD) + item.z * AT_HD + wg * 32);
 #pragma unroll
-        for (int e = 0; e < AT_HD / 4; ++e)
+        for (int e = 0; e < 8; ++e)
           dst[e] = make_float4(o[4 * e] * inv, o[4 * e + 1] * inv, o[4 * e + 2] * inv, o[4 * e + 3] * inv);
       }
     }

@@ -6,7 +6,6 @@
 namespace ndl {
 namespace tc {
 
-constexpr uint32_t kWaitLimit = 1u << 24;  // bounded spin (x ~100 ns backoff: seconds)
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -30,15 +29,30 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *b, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait; false (and *err set) when the limit expires.
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait: mbarrier.try_wait already suspends the thread in hardware
+// until the phase completes or a short timeout, so it is polled without a
+// sleep.  Gives up (sets *err, returns false) after kWaitNs of wall time, or
+// as soon as another role of the kernel has given up.
+constexpr uint64_t kWaitNs = 4000000000ull;  // 4 s
 __device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity, int *err) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+  if (mbar_try_wait(b, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(b, parity)) return true;
-    if (i > 32) __nanosleep(64);
-    if ((i & 1023) == 0 && *(volatile int *)err) return false;  // another role gave up
+    if ((i & 255) == 0) {
+      if (*(volatile int *)err) return false;
+      if (globaltimer_ns() - t0 > kWaitNs) {
+        atomicExch(err, 1);
+        return false;
+      }
+    }
   }
-  atomicExch(err, 1);
-  return false;
 }
 
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y) {

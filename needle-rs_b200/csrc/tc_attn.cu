@@ -18,11 +18,13 @@
 //   S_j = Q K_j^T                       tcgen05.mma M128 N128 K16, A and B
 //                                       K-major, f32 in TMEM (2 buffers, so
 //                                       S_{j+1} runs during softmax_j)
-//   p = exp(S*scale - m), online max/sum per row in registers
-//   P_j -> shared memory as bf16 hi/lo (K-major, 128-byte swizzle)
-//   O_j = P_j V_j                       M128 N64 K16, V read MN-major straight
-//                                       from its [key][dim] tile
-//   O = O * exp(m_old - m_new) + O_j    in registers
+//   p = exp(S*scale - m) (hardware exp2), online max/sum per row in registers
+//   P_j -> TMEM as bf16 hi/lo over its own S buffer (tcgen05.st)
+//   O_j = P_j V_j                       M128 N64 K16, A = P from TMEM, V read
+//                                       MN-major straight from its [key][dim]
+//                                       tile, into one of two O buffers
+//   O = O * exp(m_old - m_new) + O_j    in registers, one tile behind, so PV_j
+//                                       runs during the softmax of tile j+1
 // Each product is the 3-term split hi*hi + hi*lo + lo*hi (about 1e-6
 // relative), so the f32 reference is matched within the logit tolerance.
 // Keys past the request's end get probability 0; query rows past it are
@@ -45,9 +47,8 @@ constexpr int AT_TILE = AT_BM * AT_HD * 2;              // one 128 x 64 bf16 pla
 constexpr int AT_Q = 0;                                  // Q hi, Q lo
 constexpr int AT_KV = 2 * AT_TILE;                       // 2 stages x (K hi, K lo, V hi, V lo)
 constexpr int AT_STAGE = 4 * AT_TILE;
-constexpr int AT_P = AT_KV + 2 * AT_STAGE;               // P hi (2 x 16 KB), P lo (2 x 16 KB)
-constexpr int AT_XCH = AT_P + 4 * AT_TILE;               // row-max / row-sum exchange [2][128] f32
-constexpr int AT_BAR = AT_XCH + 2 * 128 * 4;             // 230400
+constexpr int AT_XCH = AT_KV + 2 * AT_STAGE;             // row-max / row-sum exchange [2][128] f32
+constexpr int AT_BAR = AT_XCH + 2 * 128 * 4;
 constexpr size_t AT_SMEM = 1024 + AT_BAR + 256;
 static_assert(AT_SMEM <= 232448, "exceeds the 227 KB of dynamic shared memory per block");
 
@@ -114,22 +115,28 @@ __global__ void qkv_post_kernel(const float *__restrict__ qkv, int rows, int sla
   split_store(dh, dl, base + lane + 32, x1);
 }
 
-// 8 probabilities of row r, keys kk0..kk0+7 of the tile, into the K-major
-// 128-byte-swizzled P tiles (hi and lo): [2 blocks of 64 keys][128 rows][128 B].
-__device__ __forceinline__ void store_p8(uint8_t *ph, uint8_t *pl, int r, int kk0, const float *p) {
-  uint32_t hw[4], lw[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    __nv_bfloat16 h0 = __float2bfloat16_rn(p[2 * i]), h1 = __float2bfloat16_rn(p[2 * i + 1]);
-    __nv_bfloat16 l0 = __float2bfloat16_rn(p[2 * i] - __bfloat162float(h0));
-    __nv_bfloat16 l1 = __float2bfloat16_rn(p[2 * i + 1] - __bfloat162float(h1));
-    hw[i] = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
-    lw[i] = (uint32_t)__bfloat16_as_ushort(l0) | ((uint32_t)__bfloat16_as_ushort(l1) << 16);
-  }
-  const int blk = kk0 >> 6, chunk = ((kk0 & 63) >> 3) ^ (r & 7);
-  const int off = blk * AT_TILE + (r >> 3) * 1024 + (r & 7) * 128 + chunk * 16;
-  *reinterpret_cast<uint4 *>(ph + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-  *reinterpret_cast<uint4 *>(pl + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+// 32 x 32-bit columns of this thread's TMEM lane (tcgen05.st 32x32b.x32).
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t *r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]),
+      "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]),
+      "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+// tcgen05.mma kind::f16 with the A operand in TMEM (M lanes, K packed two
+// bf16 per 32-bit column) and B from shared memory.
+__device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                             uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc));
 }
 
 // Rendezvous of the 256 softmax threads on an mbarrier (a bounded wait, so a
@@ -178,12 +185,12 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
   uint64_t *kv_full = q_full + 2;   // [2]
   uint64_t *kv_empty = q_full + 4;  // [2]
   uint64_t *s_full = q_full + 6;    // [2]
-  uint64_t *s_empty = q_full + 8;   // [2]
-  uint64_t *p_full = q_full + 10;
-  uint64_t *o_full = q_full + 11;
-  uint64_t *o_empty = q_full + 12;
-  uint64_t *xbar = q_full + 13;  // the two softmax warpgroups' exchange rendezvous
-  uint32_t *tmem_slot = (uint32_t *)(q_full + 14);
+  uint64_t *s_empty = q_full + 8;   // [2]  S/P buffer free (PV of its tile done)
+  uint64_t *p_full = q_full + 10;   // [2]  P written over the S buffer
+  uint64_t *o_full = q_full + 12;   // [2]
+  uint64_t *o_empty = q_full + 14;  // [2]
+  uint64_t *xbar = q_full + 16;     // the two softmax warpgroups' exchange rendezvous
+  uint32_t *tmem_slot = (uint32_t *)(q_full + 17);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rep = a.H / a.KVH;
@@ -194,15 +201,15 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
       mbar_init(&s_full[s], 1);
-      mbar_init(&s_empty[s], 256);
+      mbar_init(&s_empty[s], 1);
+      mbar_init(&p_full[s], 256);
+      mbar_init(&o_full[s], 1);
+      mbar_init(&o_empty[s], 256);
     }
-    mbar_init(p_full, 256);
-    mbar_init(o_full, 1);
-    mbar_init(o_empty, 256);
     mbar_init(xbar, 256);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 1) {  // S: 2 x 128 columns, O tile: 64 columns
+  if (warp == 1) {  // S/P: 2 x 128 columns, O: 2 x 64 columns
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(512));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -211,7 +218,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *(volatile uint32_t *)tmem_slot;
-  const uint32_t t_o = tmem + 256;
+  const uint32_t t_o = tmem + 256;  // O buffer b at t_o + 64 b
 
   if (warp == 0) {
     if (lane == 0) {  // ── TMA producer ──
@@ -263,23 +270,27 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       uint32_t jj = 0, pv = 0;
       int it = 0;
       bool ok = true;
-      int pv_stage = 0;
-      // O_t = P_t V_t for the tile whose K/V sit in stage `st`
-      auto do_pv = [&](int st) -> bool {
-        if (!mbar_wait(p_full, pv & 1, err) || !mbar_wait(o_empty, (pv & 1) ^ 1, err)) return false;
+      int pv_stage = 0, pv_sb = 0;
+      // O_t = P_t V_t for the tile t whose S/P buffer is `sb` and whose K/V
+      // sit in stage `st`; O_t goes to O buffer (pv & 1).
+      auto do_pv = [&](int st, int sb) -> bool {
+        const int ob = pv & 1;
+        if (!mbar_wait(&p_full[sb], (pv >> 1) & 1, err) || !mbar_wait(&o_empty[ob], ((pv >> 1) & 1) ^ 1, err))
+          return false;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         uint8_t *kvs = sm + AT_KV + st * AT_STAGE;
+        const uint32_t d = t_o + (uint32_t)(ob * AT_HD);
+        const uint32_t ph = tmem + (uint32_t)(sb * AT_BN), pl = ph + 64;
 #pragma unroll
         for (int ks = 0; ks < AT_BN / 16; ++ks) {
-          const int pb = (ks >> 2) * AT_TILE + (ks & 3) * 32;
-          const uint64_t ph = umma_desc(sm + AT_P + pb), pl = umma_desc(sm + AT_P + 2 * AT_TILE + pb);
           const uint64_t vh = umma_desc_mn(kvs + 2 * AT_TILE + ks * 2048);
           const uint64_t vl = umma_desc_mn(kvs + 3 * AT_TILE + ks * 2048);
-          umma_bf16(t_o, ph, vh, ID_PV, ks ? 1u : 0u);
-          umma_bf16(t_o, ph, vl, ID_PV, 1u);
-          umma_bf16(t_o, pl, vh, ID_PV, 1u);
+          umma_bf16_ts(d, ph + ks * 8, vh, ID_PV, ks ? 1u : 0u);
+          umma_bf16_ts(d, ph + ks * 8, vl, ID_PV, 1u);
+          umma_bf16_ts(d, pl + ks * 8, vh, ID_PV, 1u);
         }
-        umma_commit(o_full);
+        umma_commit(&o_full[ob]);
+        umma_commit(&s_empty[sb]);   // the S/P buffer may take the tile after next
         umma_commit(&kv_empty[st]);  // S and PV of this tile are done with its K/V
         ++pv;
         return true;
@@ -308,14 +319,15 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
           umma_commit(&s_full[sb]);
           if (j == nk - 1) umma_commit(q_empty);
           ++jj;
-          if (j > 0 && !(ok = do_pv(pv_stage))) break;
+          if (j > 0 && !(ok = do_pv(pv_stage, pv_sb))) break;
           pv_stage = stage;
+          pv_sb = sb;
           if (++stage == 2) {
             stage = 0;
             phase ^= 1;
           }
         }
-        if (ok) ok = do_pv(pv_stage);
+        if (ok) ok = do_pv(pv_stage, pv_sb);
       }
     }
   } else {  // ── softmax: warps 2-9, two warpgroups ──
@@ -324,13 +336,28 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     const uint32_t lanes = (uint32_t)(quarter * 32) << 16;
     float *xch = (float *)(sm + AT_XCH);  // [2 groups][128]: row maxima, then row sums
     uint32_t jj = 0, pv = 0, xu = 0;
+    // O += O_t (computed by the MMA with the row maxima of tile t), after
+    // rescaling the running sum by corr_t = exp(m_{t-1} - m_t).
+    float o[32];
+    auto add_o = [&](float corr) -> bool {
+      const int ob = pv & 1;
+      if (!mbar_wait(&o_full[ob], (pv >> 1) & 1, err)) return false;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      float v[32];
+      tmem_ld32(t_o + lanes + (uint32_t)(ob * AT_HD + wg * 32), v);
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      mbar_arrive(&o_empty[ob]);
+#pragma unroll
+      for (int e = 0; e < 32; ++e) o[e] = o[e] * corr + v[e];
+      ++pv;
+      return true;
+    };
     for (int w = blockIdx.x; w < n_items; w += gridDim.x) {
       const int4 item = items[w];
       const int64_t off = seq_off[item.x];
       const int T = (int)(seq_off[item.x + 1] - off);
       const int nk = (T + AT_BN - 1) / AT_BN;
-      float m = -INFINITY, l = 0.0f;
-      float o[32];
+      float m = -INFINITY, l = 0.0f, corr_prev = 0.0f;
 #pragma unroll
       for (int e = 0; e < 32; ++e) o[e] = 0.0f;
       bool ok = true;
@@ -340,8 +367,6 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         float v[64];
         tmem_ld64(tmem + lanes + (uint32_t)(sb * AT_BN + wg * 64), v);
-        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-        mbar_arrive(&s_empty[sb]);  // S is in registers: the MMA may reuse the buffer
         const int kvalid = T - j * AT_BN - wg * 64;  // keys of this half that belong to the request
         float mx = -INFINITY;
 #pragma unroll
@@ -350,35 +375,43 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
           if (e < kvalid) mx = fmaxf(mx, v[e]);
         }
         xch[wg * 128 + r] = mx;
+        // after this rendezvous both halves hold their S in registers, so P
+        // may overwrite the S buffer
         if (!(ok = xsync(xbar, xu, err))) break;
         const float m_new = fmaxf(m, fmaxf(mx, xch[(wg ^ 1) * 128 + r]));
         if (!(ok = xsync(xbar, xu, err))) break;  // both halves read before the next write
-        const float corr = expf(m - m_new);  // 0 on the first tile (m = -inf)
+        const float corr = expf(m - m_new);       // 0 on the first tile (m = -inf)
+        // Probabilities with the hardware exp2 intrinsic: __expf's error,
+        // 2 + |1.17 x| ulp for x = s - max <= 0, is ~1e-6 relative where p is
+        // not negligible, far inside the logit tolerance.
         float psum = 0.0f;
+        uint32_t ph[32], pl[32];
 #pragma unroll
-        for (int e = 0; e < 64; ++e) {
-          float p = (e < kvalid) ? expf(v[e] - m_new) : 0.0f;
-          v[e] = p;
-          psum += p;
+        for (int i = 0; i < 32; ++i) {
+          float p0 = (2 * i < kvalid) ? __expf(v[2 * i] - m_new) : 0.0f;
+          float p1 = (2 * i + 1 < kvalid) ? __expf(v[2 * i + 1] - m_new) : 0.0f;
+          psum += p0 + p1;
+          __nv_bfloat162 h = __floats2bfloat162_rn(p0, p1);
+          float2 hf = __bfloat1622float2(h);
+          __nv_bfloat162 lo = __floats2bfloat162_rn(p0 - hf.x, p1 - hf.y);
+          ph[i] = *reinterpret_cast<uint32_t *>(&h);
+          pl[i] = *reinterpret_cast<uint32_t *>(&lo);
         }
-#pragma unroll
-        for (int e8 = 0; e8 < 8; ++e8)
-          store_p8(sm + AT_P, sm + AT_P + 2 * AT_TILE, r, wg * 64 + e8 * 8, v + e8 * 8);
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // P visible to the tensor cores
-        mbar_arrive(p_full);
+        // P over the S buffer: hi plane in columns [0, 64), lo in [64, 128),
+        // this half's 64 keys at column offset wg * 32
+        const uint32_t tp = tmem + lanes + (uint32_t)(sb * AT_BN + wg * 32);
+        tmem_st32(tp, ph);
+        tmem_st32(tp + 64, pl);
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        mbar_arrive(&p_full[sb]);
         l = l * corr + psum;
         m = m_new;
         ++jj;
-        if (!(ok = mbar_wait(o_full, pv & 1, err))) break;
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        tmem_ld32(t_o + lanes + (uint32_t)(wg * 32), v);
-#pragma unroll
-        for (int e = 0; e < 32; ++e) o[e] = o[e] * corr + v[e];
-        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-        mbar_arrive(o_empty);
-        ++pv;
+        if (j > 0 && !(ok = add_o(corr_prev))) break;  // O of the previous tile
+        corr_prev = corr;
       }
-      if (!ok) break;
+      if (!ok || !add_o(corr_prev)) break;
       // combine the two halves' row sums
       xch[wg * 128 + r] = l;
       if (!xsync(xbar, xu, err)) break;

@@ -77,7 +77,9 @@ int64_t needle_batch_kernel_launches(NeedleBatch *batch);
 /* Time one kernel class in later runs: CUDA events around each of its
  * launches on the batch's stream (decode steps then launch eagerly, without
  * a CUDA graph).  Classes: 0 none, 1 decoder cross-attention, 2 prefill
- * INT4 matmuls, 3 decode INT4 matmuls, 4 output head, 5 encoder attention.
+ * INT4 matmuls, 3 decode INT4 matmuls, 4 output head, 5 encoder attention,
+ * 6 decoder self-attention, 7 elementwise kernels (norms, embedding, q/k
+ * post-processing, step bookkeeping).
  * needle_batch_kernel_timing reports, for the last run, the summed device
  * time, the launch count and the algorithmic flops and bytes of those
  * launches (bytes: every operand read once and every result written once). */

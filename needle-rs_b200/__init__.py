@@ -252,7 +252,8 @@ class Batch:
         return int(lib().needle_batch_kernel_launches(self._b))
 
     def time_kernel(self, kernel_class):
-        """0 none, 1 cross-attention, 2 prefill matmul, 3 decode matmul, 4 head, 5 encoder attention."""
+        """0 none, 1 cross-attention, 2 prefill matmul, 3 decode matmul, 4 head, 5 encoder attention,
+        6 decoder self-attention, 7 elementwise kernels."""
         _check(lib().needle_batch_time_kernel(self._b, int(kernel_class)))
 
     def kernel_timing(self):
@@ -274,7 +275,8 @@ class Batch:
             pass
 
 
-TIME_CROSS_ATTENTION, TIME_PREFILL_MATMUL, TIME_DECODE_MATMUL, TIME_HEAD, TIME_ENCODER_ATTENTION = 1, 2, 3, 4, 5
+(TIME_CROSS_ATTENTION, TIME_PREFILL_MATMUL, TIME_DECODE_MATMUL, TIME_HEAD, TIME_ENCODER_ATTENTION,
+ TIME_SELF_ATTENTION, TIME_ELEMENTWISE) = 1, 2, 3, 4, 5, 6, 7
 
 
 def shard_requests(offsets, shards):

@@ -4,6 +4,8 @@
 // All arithmetic is f32; expf/sqrtf/division are the IEEE-accurate device
 // versions (no fast-math), so results differ from the reference only by
 // summation order.
+#include <cuda_bf16.h>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -49,6 +51,45 @@ __global__ void rms_norm_kernel(const float *__restrict__ x, int64_t ldx, float 
   ss = warp_sum(ss);
   float inv = 1.0f / sqrtf(ss / (float)d + 1e-6f);
   for (int i = lane; i < d; i += 32) orow[i] = ((1.0f + __ldg(scale + i)) * xr[i]) * inv;
+}
+
+// ZCRMSNorm of 512-wide rows written straight as the bf16 hi/lo planes the
+// tensor-core GEMM consumes (row stride ldp), optionally also as f32.
+__global__ void rms_norm_planes_kernel(const float *__restrict__ x, int64_t ldx, __nv_bfloat16 *hi, __nv_bfloat16 *lo,
+                                       int64_t ldp, float *out, int64_t ldo, const float *__restrict__ scale,
+                                       int rows) {
+  int row = (int)(((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float *xr = x + (int64_t)row * ldx;
+  float v[16];
+  float ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float4 t = *reinterpret_cast<const float4 *>(xr + i * 128 + lane * 4);
+    v[i * 4 + 0] = t.x;
+    v[i * 4 + 1] = t.y;
+    v[i * 4 + 2] = t.z;
+    v[i * 4 + 3] = t.w;
+  }
+#pragma unroll
+  for (int i = 0; i < 16; ++i) ss += v[i] * v[i];
+  ss = warp_sum(ss);
+  float inv = 1.0f / sqrtf(ss / 512.0f + 1e-6f);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float4 s4 = __ldg(reinterpret_cast<const float4 *>(scale + i * 128 + lane * 4));
+    float r0 = ((1.0f + s4.x) * v[i * 4 + 0]) * inv;
+    float r1 = ((1.0f + s4.y) * v[i * 4 + 1]) * inv;
+    float r2 = ((1.0f + s4.z) * v[i * 4 + 2]) * inv;
+    float r3 = ((1.0f + s4.w) * v[i * 4 + 3]) * inv;
+    if (out) *reinterpret_cast<float4 *>(out + (int64_t)row * ldo + i * 128 + lane * 4) = make_float4(r0, r1, r2, r3);
+    __nv_bfloat162 h01 = __floats2bfloat162_rn(r0, r1), h23 = __floats2bfloat162_rn(r2, r3);
+    float2 f01 = __bfloat1622float2(h01), f23 = __bfloat1622float2(h23);
+    __nv_bfloat162 l01 = __floats2bfloat162_rn(r0 - f01.x, r1 - f01.y), l23 = __floats2bfloat162_rn(r2 - f23.x, r3 - f23.y);
+    const int64_t o = (int64_t)row * ldp + i * 128 + lane * 4;
+    *reinterpret_cast<uint2 *>(hi + o) = make_uint2(*reinterpret_cast<uint32_t *>(&h01), *reinterpret_cast<uint32_t *>(&h23));
+    *reinterpret_cast<uint2 *>(lo + o) = make_uint2(*reinterpret_cast<uint32_t *>(&l01), *reinterpret_cast<uint32_t *>(&l23));
+  }
 }
 
 __global__ void embed_kernel(const uint32_t *__restrict__ ids, const float *__restrict__ emb, float *x, int rows,
@@ -625,6 +666,16 @@ cudaError_t head_norm_rows(float *x, int rows, int64_t ld, int heads, int HD, co
   if (HD > 128 || (HD & 1)) return cudaErrorInvalidValue;
   int64_t threads = (int64_t)rows * heads * 32;
   head_norm_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(x, rows, ld, heads, HD, scale);
+  return cudaGetLastError();
+}
+
+cudaError_t rms_norm_planes(const float *x, int64_t ldx, void *hi, void *lo, int64_t ldp, float *out, int64_t ldo,
+                            const float *scale, int rows, int d, cudaStream_t st) {
+  if (rows <= 0) return cudaSuccess;
+  if (d != 512 || (ldx & 3) || (ldp & 3) || (out && (ldo & 3))) return cudaErrorInvalidValue;
+  int64_t threads = (int64_t)rows * 32;
+  rms_norm_planes_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(
+      x, ldx, (__nv_bfloat16 *)hi, (__nv_bfloat16 *)lo, ldp, out, ldo, scale, rows);
   return cudaGetLastError();
 }
 

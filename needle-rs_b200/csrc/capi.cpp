@@ -307,7 +307,7 @@ void *needle_batch_stream(NeedleBatch *nb) { return nb ? (void *)nb->batch->stre
 int64_t needle_batch_kernel_launches(NeedleBatch *nb) { return nb ? nb->batch->kernels_launched() : -1; }
 
 int needle_batch_time_kernel(NeedleBatch *nb, int kernel_class) {
-  if (!nb || kernel_class < 0 || kernel_class > 5) return -1;
+  if (!nb || kernel_class < 0 || kernel_class > 7) return -1;
   nb->timed_cls = kernel_class;
   return 0;
 }

@@ -702,6 +702,15 @@ bool Batch::reset_decoder(std::string &err) {
   return true;
 }
 
+// Launch of a timed class with no algorithmic work accounting.
+#define NDL_TK(cls, capture, call)                                                   \
+  do {                                                                               \
+    cudaEvent_t ev_;                                                                 \
+    if (!tbegin(cls, capture, ev_, err)) return false;                               \
+    NDL_LK(call);                                                                    \
+    if (!tend(ev_, 0.0, 0.0, err)) return false;                                     \
+  } while (0)
+
 #define NDL_LK(call)                                                                 \
   do {                                                                               \
     cudaError_t e_ = (call);                                                         \
@@ -754,6 +763,27 @@ bool Batch::mm(int cls, bool capture, const float *x, int64_t ldx, int M, const 
   return tend(a, mm_flops(M, w), mm_bytes(M, w), err);
 }
 
+const TcPlanes *Batch::tc_map(int Kp, int rows) const {
+  for (auto &t : tc_maps_)
+    if (t.Kp == Kp && rows <= t.rows) return &t;
+  return nullptr;
+}
+
+// Matmul whose input is either already staged as bf16 hi/lo planes (`planes`,
+// written by the producing kernel) or f32 rows (x, ldx).
+bool Batch::mm_in(int cls, bool capture, const TcPlanes *planes, const float *x, int64_t ldx, int M, const Lin &w,
+                  const MatmulOut &o, std::string &err) {
+  if (!planes) return mm(cls, capture, x, ldx, M, w, o, err);
+  if (!w.tc_ready || planes->Kp != w.tc.Kp || (o.col_block && o.col_block % 64)) {
+    err = "internal: staged matmul input without a tensor-core weight";
+    return false;
+  }
+  cudaEvent_t a;
+  if (!tbegin(cls, capture, a, err)) return false;
+  NDL_LK(tc_matmul(*planes, M, w.tc, w.N, o, m_->kerr, st_));
+  return tend(a, mm_flops(M, w), mm_bytes(M, w), err);
+}
+
 bool Batch::prefill(std::string &err) {
   const DevModel &m = *m_;
   const Config &c = m.cfg;
@@ -762,24 +792,52 @@ bool Batch::prefill(std::string &err) {
   cudaStream_t st = st_;
   for (const Chunk &ch : chunks_) {
     const int rows = (int)ch.ntok, nr = ch.r1 - ch.r0;
-    NDL_LK(embed_rows(ids_ + ch.tok0, m.emb, px_, rows, d, m.embed_scale, st));
+    // inputs of the tensor-core matmuls staged straight by their producers
+    const TcPlanes *pd = (rows >= kTcMinRows && d == 512) ? tc_map(tc_padded_k(d), rows) : nullptr;
+    const TcPlanes *pq = (rows >= kTcMinRows && tc_attn_) ? tc_map(tc_padded_k(qd), rows) : nullptr;
+    auto norm = [&](const float *scale, float *f32_out) -> bool {
+      if (pd) {
+        NDL_TK(TIME_ELEMENTWISE, false,
+               rms_norm_planes(px_, d, tc_hi_, tc_lo_, pd->Kp, f32_out, d, scale, rows, d, st));
+      } else {
+        NDL_TK(TIME_ELEMENTWISE, false, rms_norm_rows(px_, d, pxn_, d, scale, rows, d, st));
+      }
+      return true;
+    };
+    NDL_TK(TIME_ELEMENTWISE, false, embed_rows(ids_ + ch.tok0, m.emb, px_, rows, d, m.embed_scale, st));
     for (const EncLayerDev &E : m.enc) {  // layers.rs:46-93
-      NDL_LK(rms_norm_rows(px_, d, pxn_, d, E.norm, rows, d, st));
+      if (!norm(E.norm, nullptr)) return false;
       MatmulOut o;
       o.y = pqkv_;
       o.ldy = qkvd;
-      if (!mm(TIME_PREFILL_MATMUL, false, pxn_, d, rows, E.qkv, o, err)) return false;
-      if (!tc_attn_)
-        NDL_LK(qk_norm_rope_rows(pqkv_, rows, tok_pos_ + ch.tok0, E.q_norm, E.k_norm, m.rope_cos, m.rope_sin, m.ad,
+      const bool fused_post = tc_attn_ && pd != nullptr;
+      if (fused_post) {  // norm + RoPE + bf16 split of Q/K/V in the matmul epilogue
+        o.epi = EPI_QKV;
+        o.pos = tok_pos_ + ch.tok0;
+        o.q_norm = E.q_norm;
+        o.k_norm = E.k_norm;
+        o.rope_cos = m.rope_cos;
+        o.rope_sin = m.rope_sin;
+        for (int i = 0; i < 6; ++i) o.planes[i] = attn_planes_.buf[i];
+        o.slab = attn_planes_.slab;
+        o.heads_q = c.num_heads;
+        o.heads_kv = c.num_kv_heads;
+      }
+      if (!mm_in(TIME_PREFILL_MATMUL, false, pd, pxn_, d, rows, E.qkv, o, err)) return false;
+      if (fused_post) {
+      } else if (!tc_attn_)
+        NDL_TK(TIME_ELEMENTWISE, false, qk_norm_rope_rows(pqkv_, rows, tok_pos_ + ch.tok0, E.q_norm, E.k_norm, m.rope_cos, m.rope_sin, m.ad,
                                  st));
       else
-        NDL_LK(qkv_post(pqkv_, rows, tok_pos_ + ch.tok0, E.q_norm, E.k_norm, m.rope_cos, m.rope_sin, m.ad,
+        NDL_TK(TIME_ELEMENTWISE, false, qkv_post(pqkv_, rows, tok_pos_ + ch.tok0, E.q_norm, E.k_norm, m.rope_cos, m.rope_sin, m.ad,
                         attn_planes_, st));
       {
         cudaEvent_t ev;
         if (!tbegin(TIME_ENCODER_ATTENTION, false, ev, err)) return false;
         if (tc_attn_)
-          NDL_LK(encoder_attention_tc(attn_planes_, ch.rel_off, ch.items, ch.n_items, patt_, m.ad, m_->kerr, st));
+          NDL_LK(encoder_attention_tc(attn_planes_, ch.rel_off, ch.items, ch.n_items, pq ? nullptr : patt_,
+                                      pq ? tc_hi_ : nullptr, pq ? tc_lo_ : nullptr, pq ? pq->Kp : 0, m.ad,
+                                      m_->kerr, st));
         else
           NDL_LK(encoder_attention(pqkv_, ch.rel_off, nr, ch.tmax, patt_, m.ad, st));
         double Tq = 0.0;  // sum of T^2 over the chunk's requests
@@ -791,15 +849,15 @@ bool Batch::prefill(std::string &err) {
       r.ldy = d;
       r.epi = EPI_RESID;
       r.gate = E.gate;
-      if (!mm(TIME_PREFILL_MATMUL, false, patt_, qd, rows, E.o, r, err)) return false;
+      if (!mm_in(TIME_PREFILL_MATMUL, false, tc_attn_ ? pq : nullptr, patt_, qd, rows, E.o, r, err)) return false;
       if (E.ffn) {
-        NDL_LK(rms_norm_rows(px_, d, pxn_, d, E.ffn_norm, rows, d, st));
+        if (!norm(E.ffn_norm, nullptr)) return false;
         MatmulOut a;
         a.y = pffn_;
         a.ldy = c.ffn_dim;
         a.epi = EPI_ACT;
         a.act = c.activation;
-        if (!mm(TIME_PREFILL_MATMUL, false, pxn_, d, rows, E.gate_up, a, err)) return false;
+        if (!mm_in(TIME_PREFILL_MATMUL, false, pd, pxn_, d, rows, E.gate_up, a, err)) return false;
         MatmulOut f;
         f.y = px_;
         f.ldy = d;
@@ -808,7 +866,7 @@ bool Batch::prefill(std::string &err) {
         if (!mm(TIME_PREFILL_MATMUL, false, pffn_, c.ffn_dim, rows, E.down, f, err)) return false;
       }
     }
-    NDL_LK(rms_norm_rows(px_, d, pxn_, d, m.enc_final_norm, rows, d, st));  // model.rs:184-186
+    if (!norm(m.enc_final_norm, enc_out_ ? pxn_ : nullptr)) return false;  // model.rs:184-186
     if (enc_out_)
       NDL_CK(cudaMemcpyAsync(enc_out_ + ch.tok0 * d, pxn_, (size_t)rows * d * 4, cudaMemcpyDeviceToDevice, st));
     if (L > 0) {  // fill_cross_kv (model.rs:196-231): all layers' K|V in one matmul
@@ -820,10 +878,10 @@ bool Batch::prefill(std::string &err) {
       const bool fused_norm = (hd == 64) && (kvd % 64 == 0);
       o.epi = fused_norm ? EPI_KNORM : EPI_STORE;
       o.vec = m.cross_knorm;
-      if (!mm(TIME_PREFILL_MATMUL, false, pxn_, d, rows, m.cross_kv, o, err)) return false;
+      if (!mm_in(TIME_PREFILL_MATMUL, false, pd, pxn_, d, rows, m.cross_kv, o, err)) return false;
       if (!fused_norm)
         for (int l = 0; l < L; ++l)
-          NDL_LK(head_norm_rows(kv_planes_ + (size_t)2 * l * ttot_ * kvd + ch.tok0 * kvd, rows, kvd,
+          NDL_TK(TIME_ELEMENTWISE, false, head_norm_rows(kv_planes_ + (size_t)2 * l * ttot_ * kvd + ch.tok0 * kvd, rows, kvd,
                                 c.num_kv_heads, hd, m.cross_knorm + (size_t)l * hd, st));
     }
   }
@@ -836,15 +894,24 @@ bool Batch::decode_step(std::string &err, bool capture) {
   const int B = spec_.n_req, d = c.d_model, hd = c.head_dim(), qd = c.num_heads * hd, kvd = c.num_kv_heads * hd;
   const int qkvd = qd + 2 * kvd;
   cudaStream_t st = st_;
+  const TcPlanes *pd = (B >= kTcMinRows && d == 512) ? tc_map(tc_padded_k(d), B) : nullptr;
+  auto norm = [&](const float *scale, float *f32_out) -> bool {
+    if (pd) {
+      NDL_TK(TIME_ELEMENTWISE, capture, rms_norm_planes(x_, d, tc_hi_, tc_lo_, pd->Kp, f32_out, d, scale, B, d, st));
+    } else {
+      NDL_TK(TIME_ELEMENTWISE, capture, rms_norm_rows(x_, d, f32_out ? f32_out : xn_, d, scale, B, d, st));
+    }
+    return true;
+  };
   for (size_t l = 0; l < m.dec.size(); ++l) {  // layers.rs:100-149
     const DecLayerDev &D = m.dec[l];
-    NDL_LK(rms_norm_rows(x_, d, xn_, d, D.sa_norm, B, d, st));
+    if (!norm(D.sa_norm, nullptr)) return false;
     MatmulOut o;
     o.y = qkv_;
     o.ldy = qkvd;
-    if (!mm(TIME_DECODE_MATMUL, capture, xn_, d, B, D.sa_qkv, o, err)) return false;
+    if (!mm_in(TIME_DECODE_MATMUL, capture, pd, xn_, d, B, D.sa_qkv, o, err)) return false;
     size_t coff = l * (size_t)B * cap_ * kvd;
-    NDL_LK(decoder_self_attention(qkv_, pos_, D.sa_qn, D.sa_kn, m.rope_cos, m.rope_sin, self_k_ + coff,
+    NDL_TK(TIME_SELF_ATTENTION, capture, decoder_self_attention(qkv_, pos_, D.sa_qn, D.sa_kn, m.rope_cos, m.rope_sin, self_k_ + coff,
                                   self_v_ + coff, cap_, B, att_, m.ad, st));
     MatmulOut r;
     r.y = x_;
@@ -852,11 +919,11 @@ bool Batch::decode_step(std::string &err, bool capture) {
     r.epi = EPI_RESID;
     r.gate = D.sa_gate;
     if (!mm(TIME_DECODE_MATMUL, capture, att_, qd, B, D.sa_o, r, err)) return false;
-    NDL_LK(rms_norm_rows(x_, d, xn_, d, D.ca_norm, B, d, st));
+    if (!norm(D.ca_norm, nullptr)) return false;
     MatmulOut qo;
     qo.y = q_;
     qo.ldy = qd;
-    if (!mm(TIME_DECODE_MATMUL, capture, xn_, d, B, D.ca_q, qo, err)) return false;
+    if (!mm_in(TIME_DECODE_MATMUL, capture, pd, xn_, d, B, D.ca_q, qo, err)) return false;
     const float *kp = kv_planes_ + (size_t)2 * l * ttot_ * kvd, *vp = kp + (size_t)ttot_ * kvd;
     cudaEvent_t ev;
     if (!tbegin(TIME_CROSS_ATTENTION, capture, ev, err)) return false;
@@ -872,13 +939,13 @@ bool Batch::decode_step(std::string &err, bool capture) {
     r2.gate = D.ca_gate;
     if (!mm(TIME_DECODE_MATMUL, capture, att_, qd, B, D.ca_o, r2, err)) return false;
     if (D.ffn) {
-      NDL_LK(rms_norm_rows(x_, d, xn_, d, D.ffn_norm, B, d, st));
+      if (!norm(D.ffn_norm, nullptr)) return false;
       MatmulOut a;
       a.y = ffn_;
       a.ldy = c.ffn_dim;
       a.epi = EPI_ACT;
       a.act = c.activation;
-      if (!mm(TIME_DECODE_MATMUL, capture, xn_, d, B, D.gate_up, a, err)) return false;
+      if (!mm_in(TIME_DECODE_MATMUL, capture, pd, xn_, d, B, D.gate_up, a, err)) return false;
       MatmulOut f;
       f.y = x_;
       f.ldy = d;
@@ -887,7 +954,7 @@ bool Batch::decode_step(std::string &err, bool capture) {
       if (!mm(TIME_DECODE_MATMUL, capture, ffn_, c.ffn_dim, B, D.down, f, err)) return false;
     }
   }
-  NDL_LK(rms_norm_rows(x_, d, h_, d, m.dec_final_norm, B, d, st));  // model.rs:263
+  if (!norm(m.dec_final_norm, h_)) return false;  // model.rs:263
   cudaEvent_t ev;
   if (!tbegin(TIME_HEAD, capture, ev, err)) return false;
   const TcPlanes *hp = nullptr;
@@ -895,7 +962,7 @@ bool Batch::decode_step(std::string &err, bool capture) {
     for (auto &t : tc_maps_)
       if (t.Kp == m.emb_tc.Kp && B <= t.rows) hp = &t;
   if (hp) {  // logits on the tensor cores, mask + argmax in the epilogue
-    NDL_LK(tc_split_rows(h_, d, B, d, hp->Kp, tc_hi_, tc_lo_, st));
+    if (!pd) NDL_LK(tc_split_rows(h_, d, B, d, hp->Kp, tc_hi_, tc_lo_, st));
     MatmulOut o;
     o.epi = EPI_ARGMAX;
     o.mask = mask_;
@@ -911,7 +978,7 @@ bool Batch::decode_step(std::string &err, bool capture) {
   if (!tend(ev, 2.0 * B * c.vocab_size * (double)d,
             (double)c.vocab_size * d * 4 + (double)B * d * 4 + (mask_ ? (double)B * W_ * 8 : 0.0), err))
     return false;
-  NDL_LK(finish_step(keys_, B, spec_.max_new, (spec_.flags & BATCH_STOP_ON_EOS) ? 1 : 0, out_ids_, lens_, done_,
+  NDL_TK(TIME_ELEMENTWISE, capture, finish_step(keys_, B, spec_.max_new, (spec_.flags & BATCH_STOP_ON_EOS) ? 1 : 0, out_ids_, lens_, done_,
                      pos_, n_done_, teacher_, m.emb, x_, d, m.embed_scale, st));
   return true;
 }

@@ -102,6 +102,8 @@ enum TimedClass : int {
   TIME_DECODE_MATMUL = 3,    // decoder INT4 projections
   TIME_HEAD = 4,             // output head + mask + argmax
   TIME_ENCODER_ATTENTION = 5,
+  TIME_SELF_ATTENTION = 6,   // decoder self-attention with its cache append
+  TIME_ELEMENTWISE = 7,      // norms, embedding, q/k post-processing, step bookkeeping
 };
 
 enum BatchFlags : uint32_t {
@@ -159,6 +161,9 @@ class Batch {
   bool decode_step(std::string &err, bool capture);
   bool mm(int cls, bool capture, const float *x, int64_t ldx, int M, const Lin &w, const MatmulOut &o,
           std::string &err);
+  bool mm_in(int cls, bool capture, const TcPlanes *planes, const float *x, int64_t ldx, int M, const Lin &w,
+             const MatmulOut &o, std::string &err);
+  const TcPlanes *tc_map(int Kp, int rows) const;
   template <class T>
   T *alloc(size_t n, std::string &err);
 

@@ -42,6 +42,9 @@ enum Epilogue : int {
   EPI_ARGMAX = 4, // output head: acc = logit of (row m, vocab n); add the mask,
                   // reduce to atomicMax(keys[m], (total-order key, n)); logits
                   // optionally stored (engine.rs:294-304)
+  EPI_QKV = 5,    // fused Q|K|V projection of the encoder: per 64-column head,
+                  // ZCRMSNorm + RoPE (Q, K) then bf16 hi/lo into the attention
+                  // planes (tensor-core path only)
 };
 
 enum Activation : int { ACT_DRELU = 0, ACT_SWIGLU = 1, ACT_GELU = 2 };
@@ -63,6 +66,11 @@ struct MatmulOut {
   const int32_t *pos = nullptr;
   unsigned long long *keys = nullptr;
   float *logits = nullptr;
+  // EPI_QKV: row m has position pos[m] (rope tables [pos][32]); planes as in
+  // AttnPlanes: Q [H][slab][64], K and V [KVH][slab][64], hi/lo each.
+  const float *q_norm = nullptr, *k_norm = nullptr, *rope_cos = nullptr, *rope_sin = nullptr;
+  void *planes[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+  int slab = 0, heads_q = 0, heads_kv = 0;
 };
 
 // Y[M, N] (epilogue) X[M, K] @ W.  x row stride ldx (floats).
@@ -110,9 +118,12 @@ cudaError_t attn_planes_make(void *const bufs[6], int H, int KVH, int slab, Attn
 cudaError_t qkv_post(const float *qkv, int rows, const int32_t *pos, const float *q_norm, const float *k_norm,
                      const float *rope_cos, const float *rope_sin, AttnDims a, const AttnPlanes &p, cudaStream_t st);
 // Bidirectional attention over the planes: items = int4 (request, 128-row
-// query tile, Q head, 0) against chunk-relative seq_off; out [rows][H*64].
+// query tile, Q head, 0) against chunk-relative seq_off.  The result goes to
+// bf16 hi/lo planes [rows][ldp] (the O projection's input) when out_hi is
+// set, else to f32 out [rows][H*64].
 cudaError_t encoder_attention_tc(const AttnPlanes &p, const int64_t *seq_off, const void *items, int n_items,
-                                 float *out, AttnDims a, int *err, cudaStream_t st);
+                                 float *out, void *out_hi, void *out_lo, int ldp, AttnDims a, int *err,
+                                 cudaStream_t st);
 cudaError_t init_tc_attn_kernels();
 
 // Device packing / unpacking (quant.rs:63-155), bit-exact with the reference.
@@ -123,6 +134,11 @@ cudaError_t int4_dequantize(const uint8_t *data, const float *scales, int K, int
 // out[r, :] = ZCRMSNorm(x[r, :], scale)   (norm.rs:23-30), d = row length.
 cudaError_t rms_norm_rows(const float *x, int64_t ldx, float *out, int64_t ldo, const float *scale, int rows,
                           int d, cudaStream_t st);
+
+// The same norm for d = 512 written as bf16 hi/lo planes (row stride ldp) for
+// the tensor-core GEMM, and also as f32 to `out` when it is not NULL.
+cudaError_t rms_norm_planes(const float *x, int64_t ldx, void *hi, void *lo, int64_t ldp, float *out, int64_t ldo,
+                            const float *scale, int rows, int d, cudaStream_t st);
 
 // x[t, :] = E[ids[t], :] * embed_scale  (model.rs:78-85, 158-164)
 cudaError_t embed_rows(const uint32_t *ids, const float *emb, float *x, int rows, int d, float embed_scale,

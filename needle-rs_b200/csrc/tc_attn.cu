@@ -177,7 +177,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                        const __grid_constant__ CUtensorMap tmKh, const __grid_constant__ CUtensorMap tmKl,
                        const __grid_constant__ CUtensorMap tmVh, const __grid_constant__ CUtensorMap tmVl,
                        const int64_t *__restrict__ seq_off, const int4 *__restrict__ items, int n_items, int slab,
-                       float *out, AttnDims a, int *err) {
+                       float *out, __nv_bfloat16 *out_hi, __nv_bfloat16 *out_lo, int ldp, AttnDims a, int *err) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *sm = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t *q_full = (uint64_t *)(sm + AT_BAR);
@@ -420,11 +420,31 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       const int qr = item.y * AT_BM + r;
       if (qr < T) {
         const float inv = 1.0f / ltot;
-        float4 *dst =
-            reinterpret_cast<float4 *>(out + (off + qr) * (int64_t)(a.H * AT_HD) + item.z * AT_HD + wg * 32);
+        if (out_hi) {  // bf16 hi/lo planes of the O projection's input
+          const int64_t base = (off + qr) * (int64_t)ldp + item.z * AT_HD + wg * 32;
+          uint32_t hw[16], lw[16];
 #pragma unroll
-        for (int e = 0; e < 8; ++e)
-          dst[e] = make_float4(o[4 * e] * inv, o[4 * e + 1] * inv, o[4 * e + 2] * inv, o[4 * e + 3] * inv);
+          for (int e = 0; e < 16; ++e) {
+            float x0 = o[2 * e] * inv, x1 = o[2 * e + 1] * inv;
+            __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+            float2 hf = __bfloat1622float2(h);
+            __nv_bfloat162 lo = __floats2bfloat162_rn(x0 - hf.x, x1 - hf.y);
+            hw[e] = *reinterpret_cast<uint32_t *>(&h);
+            lw[e] = *reinterpret_cast<uint32_t *>(&lo);
+          }
+          uint4 *dh = reinterpret_cast<uint4 *>(out_hi + base), *dl = reinterpret_cast<uint4 *>(out_lo + base);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            dh[e] = make_uint4(hw[4 * e], hw[4 * e + 1], hw[4 * e + 2], hw[4 * e + 3]);
+            dl[e] = make_uint4(lw[4 * e], lw[4 * e + 1], lw[4 * e + 2], lw[4 * e + 3]);
+          }
+        } else {
+          float4 *dst =
+              reinterpret_cast<float4 *>(out + (off + qr) * (int64_t)(a.H * AT_HD) + item.z * AT_HD + wg * 32);
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            dst[e] = make_float4(o[4 * e] * inv, o[4 * e + 1] * inv, o[4 * e + 2] * inv, o[4 * e + 3] * inv);
+        }
       }
     }
   }
@@ -460,9 +480,12 @@ cudaError_t qkv_post(const float *qkv, int rows, const int32_t *pos, const float
 }
 
 cudaError_t encoder_attention_tc(const AttnPlanes &p, const int64_t *seq_off, const void *items, int n_items,
-                                 float *out, AttnDims a, int *err, cudaStream_t st) {
+                                 float *out, void *out_hi, void *out_lo, int ldp, AttnDims a, int *err,
+                                 cudaStream_t st) {
   if (n_items <= 0) return cudaSuccess;
   if (a.HD != 64 || (a.H % a.KVH)) return cudaErrorInvalidValue;
+  if (out_hi && (!out_lo || (ldp % 8) || ((uintptr_t)out_hi % 16) || ((uintptr_t)out_lo % 16)))
+    return cudaErrorInvalidValue;
   int sms = 148, dev = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -470,7 +493,7 @@ cudaError_t encoder_attention_tc(const AttnPlanes &p, const int64_t *seq_off, co
   auto M = [](const unsigned char *m) { return *reinterpret_cast<const CUtensorMap *>(m); };
   enc_attn_tc_kernel<<<grid, AT_THREADS, AT_SMEM, st>>>(M(p.q.hi), M(p.q.lo), M(p.k.hi), M(p.k.lo), M(p.v.hi),
                                                         M(p.v.lo), seq_off, (const int4 *)items, n_items, p.slab, out,
-                                                        a, err);
+                                                        (__nv_bfloat16 *)out_hi, (__nv_bfloat16 *)out_lo, ldp, a, err);
   return cudaGetLastError();
 }
 

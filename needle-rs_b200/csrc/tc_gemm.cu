@@ -66,11 +66,14 @@ __device__ __forceinline__ float act_apply_tc(int act, float g, float u) {
   return rg * ru;
 }
 
-// Epilogue of `cnt` (32 or 64) consecutive columns n0.. of row m.
-__device__ __forceinline__ void epi_row(const TcEpi &e, int m, int n0, float *v, int cnt) {
+// Epilogue of `cnt` (32 or 64) consecutive columns n0.. of row m (cnt is a
+// template parameter so the row stays in registers).
+template <int cnt>
+__device__ __forceinline__ void epi_row(const TcEpi &e, int m, int n0, float *v) {
   const MatmulOut &o = e.o;
   if (o.epi == EPI_ACT) {
     float *p = o.y + (int64_t)m * o.ldy + (n0 >> 1);
+#pragma unroll
     for (int j = 0; j + 1 < cnt; j += 2)
       if (n0 + j + 1 < e.N) p[j >> 1] = act_apply_tc(o.act, v[j], v[j + 1]);
     return;
@@ -78,14 +81,21 @@ __device__ __forceinline__ void epi_row(const TcEpi &e, int m, int n0, float *v,
   if (o.epi == EPI_KNORM) {
     int blk = n0 / o.col_block;
     if ((blk & 1) == 0) {  // K block: ZCRMSNorm each 64-column head (norm.rs:23-30)
-      const float *sc = o.vec + (int64_t)(blk >> 1) * 64;
+      const float4 *sc = reinterpret_cast<const float4 *>(o.vec + (int64_t)(blk >> 1) * 64);
+#pragma unroll
       for (int h = 0; h + 64 <= cnt; h += 64) {
         float ss = 0.0f;
-#pragma unroll 16
+#pragma unroll
         for (int j = 0; j < 64; ++j) ss += v[h + j] * v[h + j];
         float inv = 1.0f / sqrtf(ss / 64.0f + 1e-6f);
-#pragma unroll 16
-        for (int j = 0; j < 64; ++j) v[h + j] = ((1.0f + __ldg(sc + j)) * v[h + j]) * inv;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          float4 s4 = __ldg(sc + j);
+          v[h + 4 * j + 0] = ((1.0f + s4.x) * v[h + 4 * j + 0]) * inv;
+          v[h + 4 * j + 1] = ((1.0f + s4.y) * v[h + 4 * j + 1]) * inv;
+          v[h + 4 * j + 2] = ((1.0f + s4.z) * v[h + 4 * j + 2]) * inv;
+          v[h + 4 * j + 3] = ((1.0f + s4.w) * v[h + 4 * j + 3]) * inv;
+        }
       }
     }
   }
@@ -100,6 +110,7 @@ __device__ __forceinline__ void epi_row(const TcEpi &e, int m, int n0, float *v,
   if (n0 + cnt <= e.N) {
     float4 *p4 = reinterpret_cast<float4 *>(p);
     if (o.epi == EPI_RESID) {
+#pragma unroll
       for (int j = 0; j < cnt / 4; ++j) {
         float4 r = p4[j];
         r.x += o.gate * v[4 * j + 0];
@@ -109,10 +120,74 @@ __device__ __forceinline__ void epi_row(const TcEpi &e, int m, int n0, float *v,
         p4[j] = r;
       }
     } else {
+#pragma unroll
       for (int j = 0; j < cnt / 4; ++j) p4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
     }
   } else {
     for (int j = 0; j < cnt && n0 + j < e.N; ++j) p[j] = (o.epi == EPI_RESID) ? p[j] + o.gate * v[j] : v[j];
+  }
+}
+
+// EPI_QKV on the 64 columns (one head) n0.. of row m: ZCRMSNorm + RoPE for
+// Q and K heads (attn.rs:218-235), then bf16 hi/lo into the attention planes.
+__device__ __forceinline__ void epi_qkv64(const TcEpi &e, int m, int n0, float *v) {
+  const MatmulOut &o = e.o;
+  const int hh = n0 >> 6, H = o.heads_q, KVH = o.heads_kv;
+  int plane;
+  int64_t base;
+  if (hh < H + KVH) {
+    const float4 *sc = reinterpret_cast<const float4 *>(hh < H ? o.q_norm : o.k_norm);
+    float ss = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 64; ++j) ss += v[j] * v[j];
+    float inv = 1.0f / sqrtf(ss / 64.0f + 1e-6f);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      float4 s4 = __ldg(sc + j);
+      v[4 * j + 0] = ((1.0f + s4.x) * v[4 * j + 0]) * inv;
+      v[4 * j + 1] = ((1.0f + s4.y) * v[4 * j + 1]) * inv;
+      v[4 * j + 2] = ((1.0f + s4.z) * v[4 * j + 2]) * inv;
+      v[4 * j + 3] = ((1.0f + s4.w) * v[4 * j + 3]) * inv;
+    }
+    const int p = o.pos[m];
+    const float4 *cr = reinterpret_cast<const float4 *>(o.rope_cos + (int64_t)p * 32);
+    const float4 *sr = reinterpret_cast<const float4 *>(o.rope_sin + (int64_t)p * 32);
+#pragma unroll
+    for (int i4 = 0; i4 < 8; ++i4) {
+      float4 c4 = __ldg(cr + i4), s4 = __ldg(sr + i4);
+      const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, ssn[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = 4 * i4 + u;
+        float x0 = v[i], x1 = v[i + 32];
+        float l = x0 * cc[u] - x1 * ssn[u];
+        float r = x1 * cc[u] + x0 * ssn[u];
+        v[i] = l;
+        v[i + 32] = r;
+      }
+    }
+    plane = hh < H ? 0 : 2;
+    base = ((int64_t)(hh < H ? hh : hh - H) * o.slab + m) * 64;
+  } else {
+    plane = 4;
+    base = ((int64_t)(hh - H - KVH) * o.slab + m) * 64;
+  }
+  uint4 *dh = reinterpret_cast<uint4 *>((__nv_bfloat16 *)o.planes[plane] + base);
+  uint4 *dl = reinterpret_cast<uint4 *>((__nv_bfloat16 *)o.planes[plane + 1] + base);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    uint32_t hw[4], lw[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float x0 = v[8 * q + 2 * i], x1 = v[8 * q + 2 * i + 1];
+      __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+      float2 hf = __bfloat1622float2(h);
+      __nv_bfloat162 lo = __floats2bfloat162_rn(x0 - hf.x, x1 - hf.y);
+      hw[i] = *reinterpret_cast<uint32_t *>(&h);
+      lw[i] = *reinterpret_cast<uint32_t *>(&lo);
+    }
+    dh[q] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    dl[q] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
   }
 }
 
@@ -267,19 +342,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const int mt = t / num_n, nt = t - mt * num_n;
       const int m = mt * TC_BM + q * 32 + lane;
       const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
-      const bool knorm = e.o.epi == EPI_KNORM, amax = e.o.epi == EPI_ARGMAX;
+      const bool amax = e.o.epi == EPI_ARGMAX;
+      const bool wide = e.o.epi == EPI_KNORM || e.o.epi == EPI_QKV;  // whole 64-column heads
       unsigned long long best = 0ull;
-      for (int c = 0; c < BN; c += (knorm ? 64 : 32)) {
+      for (int c = 0; c < BN; c += (wide ? 64 : 32)) {
         float v[64];
         tmem_ld32(base + c, v);
-        if (knorm) tmem_ld32(base + c + 32, v + 32);
+        if (wide) tmem_ld32(base + c + 32, v + 32);
         const int n0 = nt * BN + c;
         if (m < M && n0 < N) {
           if (amax) {
             unsigned long long k = epi_argmax32(e, m, n0, v);
             best = k > best ? k : best;
+          } else if (e.o.epi == EPI_QKV) {
+            epi_qkv64(e, m, n0, v);
+          } else if (wide) {
+            epi_row<64>(e, m, n0, v);
           } else {
-            epi_row(e, m, n0, v, knorm ? 64 : 32);
+            epi_row<32>(e, m, n0, v);
           }
         }
       }
@@ -414,6 +494,12 @@ cudaError_t tc_matmul(const TcPlanes &A, int M, const TcPlanes &B, int N, const 
   if (o.epi == EPI_KNORM && (!o.col_block || !o.vec)) return cudaErrorInvalidValue;
   if (o.epi == EPI_ARGMAX) {
     if (!o.keys || !o.pos || (o.mask && o.mask_words * 64 < N)) return cudaErrorInvalidValue;
+  } else if (o.epi == EPI_QKV) {
+    if (N != (o.heads_q + 2 * o.heads_kv) * 64 || !o.pos || !o.q_norm || !o.k_norm || !o.rope_cos || !o.rope_sin ||
+        M > o.slab)
+      return cudaErrorInvalidValue;
+    for (int i = 0; i < 6; ++i)
+      if (!o.planes[i] || ((uintptr_t)o.planes[i] % 16)) return cudaErrorInvalidValue;
   } else if ((o.ldy % 4) || ((uintptr_t)o.y % 16) || (o.col_block && (o.block_stride % 4))) {
     return cudaErrorInvalidValue;
   }

@@ -37,6 +37,11 @@ CLASS_NAMES = {1: "cross_attention", 2: "prefill_matmul", 3: "decode_matmul", 4:
                5: "encoder_attention", 6: "self_attention", 7: "elementwise"}
 # classes whose algorithmic work is accounted (candidates for the roofline line)
 ROOFLINE_CLASSES = (1, 2, 3, 4, 5)
+# DRAM bytes (read + write) per algorithmic byte, from one ncu capture of the
+# class's kernel on the 256-request case; a launch reads each encoder K/V row
+# once, so its traffic grows in proportion to the rows and scales to the full
+# launch.  cross_attention: profiles/cross_attn_decode_256req.md
+DRAM_PER_ALG_BYTE = {1: 1.030}
 METRIC = "generated tokens/s"
 
 
@@ -333,6 +338,9 @@ def main():
     roof.update({"kernel": CLASS_NAMES[dom], "achieved": achieved, "peak": peak, "frac": achieved / peak,
                  "peak_source": pk_src, "launches": dom_n, "avg_launch_us": avg_s * 1e6,
                  "algorithmic_per_launch": (dom_by if roof["bound"] == "hbm" else dom_fl) / max(dom_n, 1)})
+    if dom in DRAM_PER_ALG_BYTE:
+        roof["traffic"] = DRAM_PER_ALG_BYTE[dom] * dom_by / max(dom_n, 1)
+        roof["traffic_source"] = "ncu dram__bytes_read.sum + dram__bytes_write.sum per algorithmic byte, 256-request capture, scaled"
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

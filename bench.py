@@ -146,6 +146,176 @@ def run_reference(args):
     return 0
 
 
+L2_BYTES = 126e6
+
+
+def _graph_ms(torch, launch, reps=5):
+    """Capture launch(stream_handle) into a CUDA graph; mean ms per replay
+    (CUDA events on the replaying stream, a synchronize on both sides)."""
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        launch(s.cuda_stream)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        launch(s.cuda_stream)
+    with torch.cuda.stream(s):
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(reps):
+            g.replay()
+        e1.record(s)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    del g
+    return ms
+
+
+def _cpu_us(fn, budget_s=0.3, min_reps=3):
+    fn()
+    t0, n = time.perf_counter(), 0
+    while n < min_reps or time.perf_counter() - t0 < budget_s:
+        fn()
+        n += 1
+    return 1e6 * (time.perf_counter() - t0) / n
+
+
+def op_suite(args, nb, wl, torch, np, pk, eng, blob):
+    """The other INT4-path workloads, measured beside the headline line.
+
+    int4_gemv   one INT4 matvec, x f32 [1, 512], W [N=2048, K=512] group-32
+                (quant.rs:160-297): a chain of R launches over R distinct
+                weight copies (R x 665,600 B > 2 x L2) captured in one CUDA
+                graph, each launch a separate op; plain launches and
+                programmatic-dependent ("overlap") launches.
+    int4_sweep  M in {1, 8, 64, 512, 4096} x (N, K) in {(512,512), (2048,512),
+                (512,2048), (8192,512)} through a prepared plan: CUDA-core
+                matvec / tile kernels below 128 rows, tcgen05 above; chains of
+                R ops on distinct weight and x copies (over 2 x L2 per replay).
+    single_request  one request, 256-token prompt, 64 greedy steps, no mask,
+                through needle_run_batch_ids (host buffers).
+    mlp_block   ffn_forward over T = 256 tokens, d 512 -> 2048 -> 512, drelu.
+    Each carries the oracle's single-thread time of the same work (cpu_us:
+    the reference path restated in C++, AVX2 order)."""
+    import oracle
+
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
+    hbm, tcp = pk["hbm_gbs"], pk.get("bf16_tflops", 1590.0)
+    out = {}
+
+    def alg_bytes(M, N, K):
+        return N * K / 2 + (K // 32) * N * 4 + M * K * 4 + M * N * 4
+
+    # ── config 0: INT4 GEMV ──
+    M, N, K = 1, 2048, 512
+    x, packed, scales = wl.int4_case(M, N, K, seed=0)
+    R = 512
+    W = dev(np.broadcast_to(packed.reshape(1, -1), (R, packed.size)))
+    S = dev(np.broadcast_to(scales.reshape(1, -1), (R, scales.size)))
+    xd = dev(x)
+    Y = torch.empty((R, N), device="cuda")
+    G = scales.shape[0]
+
+    def chain(overlap):
+        def launch(st):
+            for r in range(R):
+                nb.int4_matmul(xd.data_ptr(), M, K, W[r].data_ptr(), S[r].data_ptr(), N, G, Y[r].data_ptr(),
+                               stream=st, overlap=overlap)
+        return launch
+
+    ref = oracle.matmul(packed, scales, K, N, x, path=1)
+    res = {"shape": [M, N, K], "copies": R, "bytes_per_op": alg_bytes(M, N, K)}
+    for name, ov in (("plain", False), ("overlap", True)):
+        ms = _graph_ms(torch, chain(ov))
+        gbs = R * alg_bytes(M, N, K) / (ms / 1e3) / 1e9
+        res[name] = {"us_per_op": 1e3 * ms / R, "GB/s": gbs, "frac_of_measured_hbm": gbs / hbm,
+                     "frac_of_8TBs": gbs / 8000.0}
+    got = Y[R - 1].cpu().numpy()
+    res["max_abs_err_vs_oracle"] = float(np.max(np.abs(got - ref)))
+    res["cpu_us"] = _cpu_us(lambda: oracle.matmul(packed, scales, K, N, x, path=1))
+    out["int4_gemv"] = res
+    del W, S, Y
+
+    # ── config 4: shape sweep ──
+    sweep = []
+    for M in (1, 8, 64, 512, 4096):
+        for (N, K) in ((512, 512), (2048, 512), (512, 2048), (8192, 512)):
+            x, packed, scales = wl.int4_case(M, N, K, seed=M + N + K)
+            G = scales.shape[0]
+            per = packed.nbytes + scales.nbytes + x.nbytes
+            R = int(min(1024, max(2, -(-2 * L2_BYTES // per))))
+            Wd = dev(np.broadcast_to(packed.reshape(1, -1), (R, packed.size)))
+            Sd = dev(np.broadcast_to(scales.reshape(1, -1), (R, scales.size)))
+            Xd = dev(np.broadcast_to(x.reshape(1, -1), (R, x.size)))
+            Yd = torch.empty((M, N), device="cuda")
+            plans = [nb.Int4Plan(Wd[r].data_ptr(), Sd[r].data_ptr(), K, N, G, M) for r in range(R)]
+
+            def launch(st, plans=plans, Xd=Xd, Yd=Yd, M=M):
+                for r, pl in enumerate(plans):
+                    pl.matmul(Xd[r].data_ptr(), M, Yd.data_ptr(), stream=st, overlap=M <= 8)
+            ms = _graph_ms(torch, launch, reps=3)
+            plans[0].status()
+            t = ms / 1e3 / R
+            rows = min(M, 64)
+            cpu = _cpu_us(lambda: oracle.matmul(packed, scales, K, N, x[:rows], path=1), budget_s=0.2,
+                          min_reps=1) * (M / rows)
+            path = "tcgen05" if M >= 128 else ("cuda-core gemv" if M <= 8 else "cuda-core tile")
+            gbs = alg_bytes(M, N, K) / t / 1e9
+            tfl = 2.0 * M * N * K / t / 1e12
+            sweep.append({"M": M, "N": N, "K": K, "path": path, "us": 1e6 * t, "GB/s": gbs,
+                          "frac_hbm": gbs / hbm, "TFLOP/s": tfl, "frac_bf16": tfl / tcp, "cpu_us": cpu,
+                          "copies": R})
+            for pl in plans:
+                pl.close()
+            del Wd, Sd, Xd, Yd
+    out["int4_sweep"] = sweep
+    torch.cuda.empty_cache()
+
+    # ── config 1: one request ──
+    ids, off = wl.random_prompts(1, 256, 256, 8192, seed=11)
+    prompt = [ids.tolist()]
+    eng.run_batch_ids(prompt, 64)
+    times = []
+    for _ in range(5):
+        t0 = time.perf_counter()
+        gpu_ids, _ = eng.run_batch_ids(prompt, 64)
+        times.append(time.perf_counter() - t0)
+    if _ORACLE.get("key") != id(blob):
+        _ORACLE.update(key=id(blob), model=oracle.Model(data=blob))
+    t0 = time.perf_counter()
+    ref_ids = _ORACLE["model"].generate(ids, 64)[0]
+    cpu_s = time.perf_counter() - t0
+    ms = 1e3 * statistics.median(times)
+    out["single_request"] = {"prompt": 256, "steps": 64, "ms": ms, "tokens/s": 64 / (ms / 1e3),
+                             "cpu_ms": 1e3 * cpu_s, "cpu_cores": 1,
+                             "first_tokens_match": bool(np.array_equal(np.asarray(gpu_ids[0][:8]),
+                                                                       np.asarray(ref_ids[:8])))}
+
+    # ── config 2: MLP block ──
+    T, d, ff = 256, 512, 2048
+    rng = np.random.default_rng(2)
+    x = rng.standard_normal((T, d)).astype(np.float32)
+    g, u, dn = wl.random_int4(rng, d, ff), wl.random_int4(rng, d, ff), wl.random_int4(rng, ff, d)
+    gd, ud, dd = [dev(a) for a in g], [dev(a) for a in u], [dev(a) for a in dn]
+    xd, od = dev(x), torch.empty((T, d), device="cuda")
+
+    def mlp(st):
+        for _ in range(8):
+            nb.ffn_forward_noalloc(xd.data_ptr(), T, d, ff, [a.data_ptr() for a in gd], [a.data_ptr() for a in ud],
+                                   [a.data_ptr() for a in dd], 0, od.data_ptr(), stream=st)
+    ms = _graph_ms(torch, mlp) / 8
+    ref0 = oracle.ffn_forward(g, u, dn, d, ff, x[0], 0)
+    cpu = _cpu_us(lambda: [oracle.ffn_forward(g, u, dn, d, ff, x[t], 0) for t in range(16)], budget_s=0.3,
+                  min_reps=1) * (T / 16)
+    fl = 3 * 2.0 * T * d * ff
+    out["mlp_block"] = {"T": T, "d": d, "d_ff": ff, "activation": "drelu", "us": 1e3 * ms,
+                        "TFLOP/s": fl / (ms / 1e3) / 1e12, "cpu_us": cpu,
+                        "max_abs_err_row0": float(np.max(np.abs(od[0].cpu().numpy() - ref0)))}
+    return out
+
+
 class Clocks:
     """nvidia-smi sampler for the timed region."""
 
@@ -201,6 +371,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-ops", action="store_true", help="skip the INT4 op / single-request / MLP measurements")
     ap.add_argument("--profile-run", action="store_true",
                     help="one untimed run of the workload and exit (for ncu launch lists)")
     args = ap.parse_args()
@@ -349,6 +520,25 @@ def main():
                "sample": f"first {n} of the {args.requests} requests ({t:.1f} s), one request per host thread; "
                          "the reference Rust path restated in C++ (oracle/)"}
 
+    # ── the decode path against the HBM roofline: its algorithmic bytes (the
+    # encoder K/V rows read by cross-attention every step, the self-attention
+    # K/V cache, the decode projections and the head) over the summed time of
+    # those kernel classes in the breakdown run ──
+    L_dec = 8
+    self_kv = L_dec * args.requests * (args.max_new * (args.max_new + 1) // 2) * 2 * 256 * 4
+    dec_cls = ("cross_attention", "self_attention", "decode_matmul", "head_mask_argmax")
+    dec_ms = sum(breakdown[c]["ms"] for c in dec_cls)
+    dec_bytes = (breakdown["cross_attention"]["bytes"] + self_kv + breakdown["decode_matmul"]["bytes"]
+                 + breakdown["head_mask_argmax"]["bytes"])
+    dec_gbs = dec_bytes / (dec_ms / 1e3) / 1e9
+    decode_path = {"bytes_per_step": dec_bytes, "ms_per_step": dec_ms, "GB/s": dec_gbs,
+                   "frac_of_measured_hbm": dec_gbs / pk["hbm_gbs"], "frac_of_8TBs": dec_gbs / 8000.0,
+                   "classes": list(dec_cls)}
+
+    ops = None
+    if rank == 0 and world == 1 and not args.no_ops:
+        ops = op_suite(args, nb, wl, torch, np, pk, eng, blob)
+
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -356,6 +546,7 @@ def main():
             "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config_desc(args),
             "e2e": e2e, "gpu_launches": int(launches), "roofline": roof, "cpu_baseline": cpu, "clocks": clk,
             "kernel_breakdown_ms": {k: round(v["ms"], 3) for k, v in breakdown.items()},
+            "decode_path": decode_path, "ops": ops,
         }
         print(json.dumps(line), flush=True)
     batch.close()

@@ -113,6 +113,31 @@ int needle_run_batch_ids_logits(NeedleHandle *handle, const uint32_t *prompt_ids
 /* y[M][N] = x[M][K] @ W  (QuantizedWeight::matmul, quant.rs:400-410). */
 int needle_int4_matmul(const float *x, size_t M, size_t K, const uint8_t *w_data, const float *w_scales, size_t N,
                        size_t num_groups, float *y, void *stream);
+/* needle_int4_matmul with launch flags.  NEEDLE_INT4_OVERLAP lets the launch
+ * begin while the previous kernel in the stream is still running: its weight
+ * and scale loads are issued at once, x is read only after that kernel has
+ * finished (programmatic dependent launch).  The caller promises that no work
+ * still in flight in the stream writes w_data or w_scales.  Used below 128
+ * rows; ignored by the tensor-core path. */
+#define NEEDLE_INT4_OVERLAP 1u
+int needle_int4_matmul_ex(const float *x, size_t M, size_t K, const uint8_t *w_data, const float *w_scales, size_t N,
+                          size_t num_groups, float *y, uint32_t flags, void *stream);
+
+/* A prepared INT4 weight for repeated matmuls (the engine's own form of a
+ * projection: QuantizedWeight kept in the reference layout plus, for the
+ * tensor-core path, its bf16 hi/lo staging and a workspace for up to max_m
+ * rows of x).  needle_int4_plan_matmul is asynchronous in `stream` and
+ * allocates nothing; calls on one plan must be ordered (one stream), since
+ * they share the workspace.  needle_int4_plan_status synchronises the device
+ * and returns -1 if a bounded wait inside a tensor-core launch expired since
+ * the last check. */
+typedef struct NeedleInt4Plan NeedleInt4Plan;
+NeedleInt4Plan *needle_int4_plan_create(const uint8_t *w_data, const float *w_scales, size_t K, size_t N,
+                                        size_t num_groups, size_t max_m, void *stream);
+int needle_int4_plan_matmul(NeedleInt4Plan *plan, const float *x, size_t M, float *y, uint32_t flags, void *stream);
+int needle_int4_plan_status(NeedleInt4Plan *plan);
+void needle_int4_plan_free(NeedleInt4Plan *plan);
+
 /* Pack w[K][N] f32 (QuantizedWeight::quantize, quant.rs:63-128), bit-exact:
  * data [(Kp/2)][N], scales [Kp/gs][N] with Kp = K padded to gs. */
 int needle_int4_quantize(const float *w, size_t K, size_t N, uint8_t *data, float *scales, void *stream);

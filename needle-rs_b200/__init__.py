@@ -75,6 +75,11 @@ def lib():
             "needle_shard_requests": (I, [P, S, I, P]),
             "needle_debug_forward": (I, [P, P, S, P, S, P, P]),
             "needle_int4_matmul": (I, [P, S, S, P, P, S, S, P, P]),
+            "needle_int4_matmul_ex": (I, [P, S, S, P, P, S, S, P, U32, P]),
+            "needle_int4_plan_create": (P, [P, P, S, S, S, S, P]),
+            "needle_int4_plan_matmul": (I, [P, P, S, P, U32, P]),
+            "needle_int4_plan_status": (I, [P]),
+            "needle_int4_plan_free": (None, [P]),
             "needle_int4_quantize": (I, [P, S, S, P, P, P]),
             "needle_int4_dequantize": (I, [P, P, S, S, S, P, P]),
             "needle_ffn_forward": (I, [P, S, S, S, P, P, P, P, P, P, I, P, P]),
@@ -287,8 +292,45 @@ def shard_requests(offsets, shards):
 
 
 # ── kernel-level ops on device pointers (ints) ──
-def int4_matmul(x_ptr, M, K, w_ptr, s_ptr, N, G, y_ptr, stream=None):
-    _check(lib().needle_int4_matmul(x_ptr, M, K, w_ptr, s_ptr, N, G, y_ptr, stream))
+INT4_OVERLAP = 1
+
+
+def int4_matmul(x_ptr, M, K, w_ptr, s_ptr, N, G, y_ptr, stream=None, overlap=False):
+    """y[M][N] = x[M][K] @ W on device pointers (QuantizedWeight::matmul).
+    overlap: launch with programmatic dependent launch (weights must not be
+    written by work still in flight in the stream)."""
+    if overlap:
+        _check(lib().needle_int4_matmul_ex(x_ptr, M, K, w_ptr, s_ptr, N, G, y_ptr, INT4_OVERLAP, stream))
+    else:
+        _check(lib().needle_int4_matmul(x_ptr, M, K, w_ptr, s_ptr, N, G, y_ptr, stream))
+
+
+class Int4Plan:
+    """A prepared INT4 weight (device pointers in the reference layout) for
+    repeated asynchronous matmuls of up to max_m rows."""
+
+    def __init__(self, w_ptr, s_ptr, K, N, G, max_m, stream=None):
+        self.K, self.N, self.max_m = K, N, max_m
+        self._h = lib().needle_int4_plan_create(w_ptr, s_ptr, K, N, G, max_m, stream)
+        if not self._h:
+            raise NeedleError(last_error() or "needle_int4_plan_create failed")
+
+    def matmul(self, x_ptr, M, y_ptr, stream=None, overlap=False):
+        _check(lib().needle_int4_plan_matmul(self._h, x_ptr, M, y_ptr, INT4_OVERLAP if overlap else 0, stream))
+
+    def status(self):
+        _check(lib().needle_int4_plan_status(self._h))
+
+    def close(self):
+        if self._h:
+            lib().needle_int4_plan_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def int4_quantize(w_ptr, K, N, data_ptr, scales_ptr, stream=None):

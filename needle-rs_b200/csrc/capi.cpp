@@ -457,6 +457,123 @@ int needle_int4_matmul(const float *x, size_t M, size_t K, const uint8_t *w, con
   return matmul_any(x, (int64_t)K, (int)M, W, o, (cudaStream_t)stream) ? 0 : -1;
 }
 
+int needle_int4_matmul_ex(const float *x, size_t M, size_t K, const uint8_t *w, const float *s, size_t N, size_t G,
+                          float *y, uint32_t flags, void *stream) {
+  clear_err();
+  if (!x || !w || !s || !y || M == 0 || K == 0 || N == 0 || G == 0 || M > INT32_MAX || K > INT32_MAX ||
+      N > INT32_MAX || G > INT32_MAX || (flags & ~NEEDLE_INT4_OVERLAP)) {
+    set_err("invalid matmul arguments");
+    return -1;
+  }
+  if (!ensure_kernels()) return -1;
+  Int4Weight W{w, s, (int)K, (int)N, (int)G, (int)(K < 32 ? K : 32)};
+  MatmulOut o;
+  o.y = y;
+  o.ldy = (int64_t)N;
+  if (M < (size_t)kTcMinRows)
+    return dev_check(int4_matmul(x, (int64_t)K, (int)M, W, o, (cudaStream_t)stream, (flags & NEEDLE_INT4_OVERLAP) != 0))
+               ? 0
+               : -1;
+  return matmul_any(x, (int64_t)K, (int)M, W, o, (cudaStream_t)stream) ? 0 : -1;
+}
+
+}  // extern "C"
+
+struct NeedleInt4Plan {
+  int device = 0;
+  ndl::Int4Weight W{};
+  int Kp = 0, max_m = 0;
+  void *buf = nullptr;  // weight hi/lo planes, then x hi/lo planes
+  ndl::TcPlanes A, B;
+  bool tc = false;
+  int *flag = nullptr;
+};
+
+extern "C" {
+
+NeedleInt4Plan *needle_int4_plan_create(const uint8_t *w, const float *s, size_t K, size_t N, size_t G, size_t max_m,
+                                        void *stream) {
+  clear_err();
+  if (!w || !s || K == 0 || N == 0 || G == 0 || max_m == 0 || K > INT32_MAX || N > INT32_MAX || G > INT32_MAX ||
+      max_m > INT32_MAX) {
+    set_err("invalid plan arguments");
+    return nullptr;
+  }
+  if (!ensure_kernels()) return nullptr;
+  auto *p = new NeedleInt4Plan();
+  cudaGetDevice(&p->device);
+  p->W = Int4Weight{w, s, (int)K, (int)N, (int)G, (int)(K < 32 ? K : 32)};
+  p->max_m = (int)max_m;
+  p->tc = max_m >= (size_t)kTcMinRows;
+  if (p->tc) {
+    cudaStream_t st = (cudaStream_t)stream;
+    p->Kp = tc_padded_k((int)K);
+    const size_t wbytes = N * (size_t)p->Kp * 2, xbytes = max_m * (size_t)p->Kp * 2;
+    p->flag = device_err_flag();
+    if (!p->flag || !dev_check(cudaMalloc(&p->buf, 2 * wbytes + 2 * xbytes + 1024))) {
+      if (!p->flag) set_err("device error flag allocation failed");
+      delete p;
+      return nullptr;
+    }
+    char *b = (char *)(((uintptr_t)p->buf + 255) & ~(uintptr_t)255);
+    void *wh = b, *wl = b + wbytes, *xh = b + 2 * wbytes, *xl = b + 2 * wbytes + xbytes;
+    if (!dev_check(tc_make_planes(wh, wl, (int)N, p->Kp, 128, p->B)) ||
+        !dev_check(tc_make_planes(xh, xl, (int)max_m, p->Kp, 128, p->A)) ||
+        !dev_check(tc_prep_weight(p->W, p->Kp, wh, wl, st)) || !dev_check(cudaStreamSynchronize(st))) {
+      cudaFree(p->buf);
+      delete p;
+      return nullptr;
+    }
+  }
+  return p;
+}
+
+int needle_int4_plan_matmul(NeedleInt4Plan *p, const float *x, size_t M, float *y, uint32_t flags, void *stream) {
+  clear_err();
+  if (!p || !x || !y || M == 0 || M > (size_t)p->max_m || (flags & ~NEEDLE_INT4_OVERLAP)) {
+    set_err("invalid plan matmul arguments");
+    return -1;
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  MatmulOut o;
+  o.y = y;
+  o.ldy = (int64_t)p->W.N;
+  if (!p->tc || M < (size_t)kTcMinRows || ((uintptr_t)y % 16) != 0 || (p->W.N % 4) != 0)
+    return dev_check(int4_matmul(x, (int64_t)p->W.K, (int)M, p->W, o, st, (flags & NEEDLE_INT4_OVERLAP) != 0)) ? 0
+                                                                                                              : -1;
+  if (!dev_check(tc_split_rows(x, (int64_t)p->W.K, (int)M, p->W.K, p->Kp, const_cast<void *>(p->A.hi_ptr), const_cast<void *>(p->A.lo_ptr), st)) ||
+      !dev_check(tc_matmul(p->A, (int)M, p->B, p->W.N, o, p->flag, st)))
+    return -1;
+  return 0;
+}
+
+int needle_int4_plan_status(NeedleInt4Plan *p) {
+  clear_err();
+  if (!p) {
+    set_err("null plan");
+    return -1;
+  }
+  if (!p->flag) return dev_check(cudaDeviceSynchronize()) ? 0 : -1;
+  int kerr = 0;
+  if (!dev_check(cudaDeviceSynchronize()) || !dev_check(cudaMemcpy(&kerr, p->flag, sizeof(int), cudaMemcpyDeviceToHost)))
+    return -1;
+  if (kerr) {
+    cudaMemset(p->flag, 0, sizeof(int));
+    set_err("a tensor-core GEMM wait timed out");
+    return -1;
+  }
+  return 0;
+}
+
+void needle_int4_plan_free(NeedleInt4Plan *p) {
+  if (!p) return;
+  if (p->buf) {
+    cudaDeviceSynchronize();
+    cudaFree(p->buf);
+  }
+  delete p;
+}
+
 int needle_int4_quantize(const float *w, size_t K, size_t N, uint8_t *data, float *scales, void *stream) {
   clear_err();
   if (!w || !data || !scales || K == 0 || N == 0 || K > INT32_MAX || N > INT32_MAX) {

@@ -343,6 +343,172 @@ __global__ void __launch_bounds__(256) gemv_kernel(const float *__restrict__ x, 
   }
 }
 
+// Decode matvec for M <= 8 rows on 16-byte weight loads.  CTA = 256
+// threads: CX column threads x (256 / CX) pair slices.  Each thread owns 16
+// consecutive output columns (one 16-byte load per pair row: 16 packed
+// bytes) and a contiguous run of pair rows; nibbles are unpacked in
+// registers, slices are reduced with warp shuffles and then across the 8
+// warps in shared memory.  The first batch of weight and scale loads is
+// issued before griddepcontrol.wait, so under programmatic dependent launch
+// it overlaps the previous kernel in the stream; x is read (and y written)
+// only after the wait.  Requires N % 16 == 0 and 16-byte aligned weights and
+// scales.
+template <int MR, int CX>
+__global__ void __launch_bounds__(256) gemv16_kernel(const float *__restrict__ x, int64_t ldx, int M, int K,
+                                                     Int4Weight W, EpiCtx e) {
+  constexpr int PY = 256 / CX;  // pair slices per CTA
+  constexpr int NC = 16 * CX;   // columns per CTA
+  constexpr int PF = MR >= 4 ? 4 : 8;  // pair rows loaded per batch
+  extern __shared__ __align__(16) float sm[];
+  asm volatile("griddepcontrol.launch_dependents;");
+  const int N = W.N, Kp = W.G * W.gs, npairs = Kp >> 1;
+  const int tid = threadIdx.x, tx = tid % CX, ty = tid / CX;
+  const int n0 = blockIdx.x * NC, n = n0 + 16 * tx;
+  const bool col_ok = n < N;
+  const int pp = (npairs + PY - 1) / PY;
+  const int p_beg = min(npairs, ty * pp), p_end = min(npairs, p_beg + pp);
+  float *xs = sm;                                   // [M][Kp]
+  float *red = sm + (((size_t)M * Kp + 3) & ~(size_t)3);  // [8 warps][MR][NC], 16-byte aligned
+
+  uint4 wb[PF];
+  auto load_batch = [&](int pb) {
+#pragma unroll
+    for (int i = 0; i < PF; ++i) {
+      const int pi = pb + i;
+      wb[i] = (col_ok && pi < p_end) ? __ldg(reinterpret_cast<const uint4 *>(W.w + (int64_t)pi * N + n))
+                                     : make_uint4(0u, 0u, 0u, 0u);
+    }
+  };
+  float sc[16];
+  int gcur = -1;
+  auto load_scales = [&](int g) {
+    if (col_ok) {
+      const float4 *sp = reinterpret_cast<const float4 *>(W.s + (int64_t)g * N + n);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float4 v = __ldg(sp + q);
+        sc[4 * q] = v.x;
+        sc[4 * q + 1] = v.y;
+        sc[4 * q + 2] = v.z;
+        sc[4 * q + 3] = v.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) sc[j] = 0.0f;
+    }
+    gcur = g;
+  };
+  load_batch(p_beg);
+  if (p_beg < p_end) load_scales((2 * p_beg) / W.gs);
+
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  for (int i = tid; i < M * Kp; i += 256) {
+    int m = i / Kp, k = i - m * Kp;
+    xs[i] = k < K ? x[(int64_t)m * ldx + k] : 0.0f;
+  }
+  __syncthreads();
+
+  float acc[MR][16];
+#pragma unroll
+  for (int m = 0; m < MR; ++m)
+#pragma unroll
+    for (int j = 0; j < 16; ++j) acc[m][j] = 0.0f;
+
+  for (int p = p_beg; p < p_end; p += PF) {
+    if (p != p_beg) load_batch(p);
+#pragma unroll
+    for (int i = 0; i < PF; ++i) {
+      const int pi = p + i;
+      if (pi < p_end) {
+        const int g = (2 * pi) / W.gs;
+        if (g != gcur) load_scales(g);
+        const uint32_t wd[4] = {wb[i].x, wb[i].y, wb[i].z, wb[i].w};
+        float lo[16], hi[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const uint32_t b = (wd[j >> 2] >> (8 * (j & 3))) & 0xFFu;
+          lo[j] = (float)sign_extend4(b & 0xFu);
+          hi[j] = (float)sign_extend4(b >> 4);
+        }
+#pragma unroll
+        for (int m = 0; m < MR; ++m) {
+          if (m < M) {
+            const float x0 = xs[m * Kp + 2 * pi], x1 = xs[m * Kp + 2 * pi + 1];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              // per-pair term in the order of matvec_avx2: (lo*x0 + hi*x1) * scale
+              const float t = fmaf(hi[j], x1, lo[j] * x0);
+              acc[m][j] += t * sc[j];
+            }
+          }
+        }
+      }
+    }
+  }
+  // Reduce the slices of this warp (lanes with equal tx), then across warps.
+#pragma unroll
+  for (int off = CX; off < 32; off <<= 1)
+#pragma unroll
+    for (int m = 0; m < MR; ++m)
+#pragma unroll
+      for (int j = 0; j < 16; ++j) acc[m][j] += __shfl_xor_sync(0xffffffffu, acc[m][j], off);
+  const int warp = tid >> 5, lane = tid & 31;
+  if (lane < CX) {
+#pragma unroll
+    for (int m = 0; m < MR; ++m)
+#pragma unroll
+      for (int j = 0; j < 16; j += 4)
+        *reinterpret_cast<float4 *>(red + (warp * MR + m) * NC + 16 * lane + j) =
+            make_float4(acc[m][j], acc[m][j + 1], acc[m][j + 2], acc[m][j + 3]);
+  }
+  __syncthreads();
+  for (int i = tid; i < M * (NC / 4); i += 256) {
+    const int m = i / (NC / 4), c4 = i - m * (NC / 4);
+    const int nn = n0 + 4 * c4;
+    if (nn < N) {
+      float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+      for (int w = 0; w < 8; ++w) {
+        const float4 r = *reinterpret_cast<const float4 *>(red + (w * MR + m) * NC + 4 * c4);
+        v[0] += r.x;
+        v[1] += r.y;
+        v[2] += r.z;
+        v[3] += r.w;
+      }
+      store4(e, m, nn, v[0], v[1], v[2], v[3], false);
+    }
+  }
+}
+
+template <int MR, int CX>
+cudaError_t launch_gemv16(const float *x, int64_t ldx, int M, const Int4Weight &W, const EpiCtx &e, bool pdl,
+                          cudaStream_t stream) {
+  constexpr int NC = 16 * CX;
+  const int Kp = W.G * W.gs;
+  const size_t sm = ((((size_t)M * Kp + 3) & ~(size_t)3) + (size_t)8 * MR * NC) * sizeof(float);
+  if (sm > (size_t)kMaxDynSmem) return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((W.N + NC - 1) / NC);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = sm;
+  cfg.stream = stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, gemv16_kernel<MR, CX>, x, ldx, M, W.K, W, e);
+}
+
+template <int CX>
+cudaError_t dispatch_gemv16(const float *x, int64_t ldx, int M, const Int4Weight &W, const EpiCtx &e, bool pdl,
+                            cudaStream_t stream) {
+  if (M <= 1) return launch_gemv16<1, CX>(x, ldx, M, W, e, pdl, stream);
+  if (M <= 2) return launch_gemv16<2, CX>(x, ldx, M, W, e, pdl, stream);
+  if (M <= 4) return launch_gemv16<4, CX>(x, ldx, M, W, e, pdl, stream);
+  return launch_gemv16<8, CX>(x, ldx, M, W, e, pdl, stream);
+}
+
 __global__ void quantize_kernel(const float *__restrict__ w, int K, int N, int gs, int G, uint8_t *data,
                                 float *scales) {
   // quant.rs:63-128.  One thread per (group, column): computes the scale
@@ -391,7 +557,11 @@ __global__ void dequantize_kernel(const uint8_t *__restrict__ data, const float 
 
 cudaError_t init_matmul_kernels() {
   cudaError_t e = cudaSuccess;
-  for (const void *f : {(const void *)tile_kernel, (const void *)gemv_kernel<8>, (const void *)gemv_kernel<16>}) {
+  for (const void *f : {(const void *)tile_kernel, (const void *)gemv_kernel<8>, (const void *)gemv_kernel<16>,
+                        (const void *)gemv16_kernel<1, 2>, (const void *)gemv16_kernel<2, 2>,
+                        (const void *)gemv16_kernel<4, 2>, (const void *)gemv16_kernel<8, 2>,
+                        (const void *)gemv16_kernel<1, 4>, (const void *)gemv16_kernel<2, 4>,
+                        (const void *)gemv16_kernel<4, 4>, (const void *)gemv16_kernel<8, 4>}) {
     cudaError_t r = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
     if (r != cudaSuccess) e = r;
   }
@@ -399,7 +569,7 @@ cudaError_t init_matmul_kernels() {
 }
 
 cudaError_t int4_matmul(const float *x, int64_t ldx, int M, const Int4Weight &W, const MatmulOut &o,
-                        cudaStream_t stream) {
+                        cudaStream_t stream, bool pdl) {
   if (M <= 0 || W.N <= 0) return cudaSuccess;
   if (W.gs <= 0 || W.G <= 0 || (W.gs & 1)) return cudaErrorInvalidValue;
   if (W.w2 && ((W.N & 1) || !W.s2)) return cudaErrorInvalidValue;
@@ -410,6 +580,12 @@ cudaError_t int4_matmul(const float *x, int64_t ldx, int M, const Int4Weight &W,
   if (o.epi == EPI_ACT && (W.N & 1)) return cudaErrorInvalidValue;
   EpiCtx e{o, W.N};
   const int Kp = W.G * W.gs;
+  if (M <= 8 && !W.w2 && o.epi != EPI_KNORM && (W.N % 16) == 0 && ((uintptr_t)W.w % 16) == 0 &&
+      ((uintptr_t)W.s % 16) == 0) {
+    // 128 or more CTAs where the width allows, else 32-column CTAs
+    if (W.N / 64 >= 96) return dispatch_gemv16<4>(x, ldx, M, W, e, pdl, stream);
+    return dispatch_gemv16<2>(x, ldx, M, W, e, pdl, stream);
+  }
   if (M <= 8) {
     if (o.epi == EPI_KNORM || W.N > 1024) {
       size_t sm = ((size_t)M * Kp + (size_t)16 * M * 64) * sizeof(float);

@@ -75,7 +75,7 @@ struct MatmulOut {
 
 // Y[M, N] (epilogue) X[M, K] @ W.  x row stride ldx (floats).
 cudaError_t int4_matmul(const float *x, int64_t ldx, int M, const Int4Weight &W, const MatmulOut &o,
-                        cudaStream_t stream);
+                        cudaStream_t stream, bool pdl = false);
 
 // ── tensor-core path (tc_gemm.cu) ──
 // A pair of bf16 planes (hi, lo) of a [rows][Kp] K-contiguous operand, with

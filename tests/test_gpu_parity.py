@@ -83,6 +83,49 @@ def test_int4_matmul_vs_oracle(M, N, K):
     assert close_act(got, ref), max_excess(got, ref, True)
 
 
+@pytest.mark.parametrize("M", [1, 2, 5, 8])
+def test_int4_matmul_overlap_chain(M):
+    """Launches with programmatic dependent launch, each reading the previous
+    launch's output as its x: the weight prefetch overlaps, the x read waits."""
+    d, steps = 512, 6
+    cases = [wl.int4_case(M, d, d, seed=100 + i) for i in range(steps)]
+    x0 = cases[0][0]
+    bufs = [dev(x0)] + [torch.full((M, d), float("nan"), device="cuda") for _ in range(steps)]
+    ws = [(dev(c[1]), dev(c[2])) for c in cases]
+    for i in range(steps):
+        nb.int4_matmul(bufs[i].data_ptr(), M, d, ws[i][0].data_ptr(), ws[i][1].data_ptr(), d, cases[i][2].shape[0],
+                       bufs[i + 1].data_ptr(), overlap=True)
+    torch.cuda.synchronize()
+    for i in range(steps):
+        xin = bufs[i].cpu().numpy()
+        ref = orc.matmul(cases[i][1], cases[i][2], d, d, xin, path=1)
+        got = bufs[i + 1].cpu().numpy()
+        assert not np.isnan(got).any(), i
+        assert close_act(got, ref), (i, max_excess(got, ref, True))
+
+
+@pytest.mark.parametrize("M", [1, 8, 127, 128, 200, 512])
+def test_int4_plan_vs_oracle(M):
+    N, K = 2048, 512
+    x, packed, scales = wl.int4_case(M, N, K, seed=3 * M + 1)
+    ref = orc.matmul(packed, scales, K, N, x, path=1)
+    wd, sd = dev(packed), dev(scales)
+    plan = nb.Int4Plan(wd.data_ptr(), sd.data_ptr(), K, N, scales.shape[0], max_m=512)
+    try:
+        xd = dev(x)
+        for rep in range(2):  # the workspace is reused across calls
+            y = torch.full((M, N), float("nan"), device="cuda")
+            plan.matmul(xd.data_ptr(), M, y.data_ptr(), overlap=(rep == 1))
+            plan.status()
+            got = y.cpu().numpy()
+            assert not np.isnan(got).any()
+            assert close_act(got, ref), max_excess(got, ref, True)
+        with pytest.raises(nb.NeedleError):
+            plan.matmul(xd.data_ptr(), 513, y.data_ptr())
+    finally:
+        plan.close()
+
+
 @pytest.mark.parametrize("K,N", [(512, 2048), (33, 8), (65, 16), (16, 8), (4, 4), (2048, 24), (96, 40)])
 def test_int4_quantize_bit_exact(K, N):
     rng = np.random.default_rng(K * N)

@@ -593,18 +593,31 @@ bool Batch::prepare(const BatchSpec &spec, std::string &err) {
     chunks_.push_back(ch);
     r = ch.r1;
   }
-  // tensor-core encoder attention: head dim 64, work items (request, 128-row
-  // query tile, Q head) per chunk
+  // tensor-core encoder attention: head dim 64.  A work item pairs two
+  // (Q head, 128-row query tile) slots of one request that read the same KV
+  // head (the GQA heads of a KV head at one tile; an odd slot left over runs
+  // alone): {request, qtile_a | qtile_b << 16, head_a | head_b << 16, kv head},
+  // head_b = 0xFFFF for an empty slot b.
   tc_attn_ = hd == 64 && (c.num_heads % c.num_kv_heads) == 0;
   if (tc_attn_) {
+    const int rep = c.num_heads / c.num_kv_heads;
     std::vector<int32_t> it;
     std::vector<size_t> start;
+    std::vector<std::pair<int, int>> slots;  // (qtile, head)
     for (auto &ch : chunks_) {
       start.push_back(it.size() / 4);
       for (int r = ch.r0; r < ch.r1; ++r) {
         int T = (int)(off_h_[r + 1] - off_h_[r]);
-        for (int qt = 0; qt < (T + 127) / 128; ++qt)
-          for (int h = 0; h < c.num_heads; ++h) it.insert(it.end(), {r - ch.r0, qt, h, 0});
+        for (int g = 0; g < c.num_kv_heads; ++g) {
+          slots.clear();
+          for (int qt = 0; qt < (T + 127) / 128; ++qt)
+            for (int h = g * rep; h < (g + 1) * rep; ++h) slots.push_back({qt, h});
+          for (size_t i = 0; i < slots.size(); i += 2) {
+            const bool two = i + 1 < slots.size();
+            const int qb = two ? slots[i + 1].first : 0, hb = two ? slots[i + 1].second : 0xFFFF;
+            it.insert(it.end(), {r - ch.r0, slots[i].first | (qb << 16), slots[i].second | (hb << 16), g});
+          }
+        }
       }
     }
     int32_t *dit = alloc<int32_t>(it.size(), err);

@@ -9,27 +9,34 @@
 // applied in f32 first: Q [H][rows][64], K and V [KVH][rows][64], each as a
 // hi/lo pair (hi = bf16(v), lo = bf16(v - hi)).
 //
-// Kernel.  Persistent; a work item is (request, 128-query tile, Q head).
-// 320 threads: warp 0 TMA (Q tile once, then K/V tiles of 128 keys through a
-// 2-stage ring), warp 1 TMEM allocation + MMA issue, warps 2-9 softmax in two
-// warpgroups: thread = one query row and one half (64 keys) of each S tile;
-// the halves exchange row maxima through shared memory and split the 64
-// output columns.  Per key tile j:
-//   S_j = Q K_j^T                       tcgen05.mma M128 N128 K16, A and B
-//                                       K-major, f32 in TMEM (2 buffers, so
-//                                       S_{j+1} runs during softmax_j)
-//   p = exp(S*scale - m) (hardware exp2), online max/sum per row in registers
-//   P_j -> TMEM as bf16 hi/lo over its own S buffer (tcgen05.st)
-//   O_j = P_j V_j                       M128 N64 K16, A = P from TMEM, V read
-//                                       MN-major straight from its [key][dim]
-//                                       tile, into one of two O buffers
-//   O = O * exp(m_old - m_new) + O_j    in registers, one tile behind, so PV_j
-//                                       runs during the softmax of tile j+1
-// Each product is the 3-term split hi*hi + hi*lo + lo*hi (about 1e-6
-// relative), so the f32 reference is matched within the logit tolerance.
-// Keys past the request's end get probability 0; query rows past it are
-// computed on neighbouring rows and never stored.  TMA loads never use
-// cluster multicast; every wait is bounded (error flag, then unwind).
+// Kernel.  Persistent.  A work item is two (Q head, 128-query tile) slots
+// of one request that read the same KV head (the GQA heads of a KV head), so
+// each K/V tile is loaded once for both.  384 threads in three warpgroups:
+// warp 0 issues the TMA loads (the item's Q tiles, then K/V tiles of 128
+// keys through a 2-stage ring), warp 1 allocates TMEM and issues the MMAs
+// (warps 2-3 idle), and warpgroups 1 / 2 run the softmax of slot a / slot b
+// (thread = one query row, all 128 keys of a tile held in registers; the
+// producer warpgroup hands its registers to them with setmaxnreg).  TMEM: S_a and S_b (128 columns each; P is written back over its own
+// S), O_a and O_b (64 columns each).  Per key tile j and slot x:
+//   S_x = Q_x K_j^T      tcgen05.mma M128 N128 K16, A and B K-major in smem
+//   p = 2^(s*c - m)      c = hd^-0.5 * log2(e); m is raised only when a row's
+//                        maximum passes it by more than 8, so p <= 256; p and
+//                        the row sum share m, so their quotient is the
+//                        reference's exp(s - max) / sum
+//   P_x -> TMEM          bf16 hi/lo over S_x (tcgen05.st): keys 32c..32c+31
+//                        in columns 32c..32c+15 (hi) and 32c+16..32c+31 (lo),
+//                        the columns their own S values came from
+//   O_x (+)= P_x V_j     M128 N64 K16, A = P from TMEM, V read MN-major from
+//                        its [key][dim] tile; O stays in TMEM and the softmax
+//                        warps rescale it there when m moves
+// The MMA warp issues S_a(0), S_b(0), then per tile PV_a(j), S_a(j+1),
+// PV_b(j), S_b(j+1): while one slot's warps run the softmax, the tensor core
+// works on the other slot.  Each product is the 3-term split hi*hi + hi*lo +
+// lo*hi (about 1e-6 relative), so the f32 reference is matched within the
+// logit tolerance.  Keys past the request's end get probability 0; query
+// rows past it are computed on neighbouring rows and never stored.  Every TMA
+// load fills only its own CTA's shared memory; every wait is bounded (error
+// flag, then unwind).
 #include <cuda.h>
 #include <cuda_bf16.h>
 
@@ -42,14 +49,20 @@ namespace {
 
 using namespace tc;
 
-constexpr int AT_BM = 128, AT_BN = 128, AT_HD = 64, AT_THREADS = 320;
-constexpr int AT_TILE = AT_BM * AT_HD * 2;              // one 128 x 64 bf16 plane tile: 16 KB
-constexpr int AT_Q = 0;                                  // Q hi, Q lo
-constexpr int AT_KV = 2 * AT_TILE;                       // 2 stages x (K hi, K lo, V hi, V lo)
+constexpr int AT_BM = 128, AT_BN = 128, AT_HD = 64, AT_THREADS = 384;
+// Registers a thread: launched at 168 (65,536 / 384, rounded down to 8),
+// then the producer warpgroup drops to 56 and the two softmax warpgroups
+// rise to 224: 128 x 56 + 256 x 224 = 384 x 168 = 64,512.
+constexpr int AT_REG_LAUNCH = 168, AT_REG_PRODUCER = 56, AT_REG_SOFTMAX = 224;
+static_assert(128 * AT_REG_PRODUCER + 256 * AT_REG_SOFTMAX == AT_THREADS * AT_REG_LAUNCH,
+              "the register split must add up to the launch's registers");
+constexpr int AT_TILE = AT_BM * AT_HD * 2;  // one 128 x 64 bf16 plane tile: 16 KB
+constexpr int AT_Q = 0;                      // slot a hi, lo; slot b hi, lo
+constexpr int AT_KV = 4 * AT_TILE;           // 2 stages x (K hi, K lo, V hi, V lo)
 constexpr int AT_STAGE = 4 * AT_TILE;
-constexpr int AT_XCH = AT_KV + 2 * AT_STAGE;             // row-max / row-sum exchange [2][128] f32
-constexpr int AT_BAR = AT_XCH + 2 * 128 * 4;
+constexpr int AT_BAR = AT_KV + 2 * AT_STAGE;
 constexpr size_t AT_SMEM = 1024 + AT_BAR + 256;
+constexpr float AT_RESCALE = 8.0f;  // log2 headroom before a row's reference point m is raised
 static_assert(AT_SMEM <= 232448, "exceeds the 227 KB of dynamic shared memory per block");
 
 __device__ __forceinline__ void norm_rope64(float &x0, float &x1, const float *__restrict__ nsc,
@@ -139,16 +152,8 @@ __device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, u
       "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc));
 }
 
-// Rendezvous of the 256 softmax threads on an mbarrier (a bounded wait, so a
-// warpgroup that unwinds on an error can never strand the other).
-__device__ __forceinline__ bool xsync(uint64_t *bar, uint32_t &uses, int *err) {
-  mbar_arrive(bar);
-  return mbar_wait(bar, (uses++) & 1, err);
-}
-
-// Two x32 TMEM loads (64 consecutive columns) with a single wait.
-__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float *v) {
-  uint32_t r[64];
+// 32 x 32-bit TMEM columns of this thread's lane into r (no wait).
+__device__ __forceinline__ void tmem_ld32_raw(uint32_t taddr, uint32_t *r) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
       "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
@@ -158,18 +163,80 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float *v) {
         "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
         "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
+}
+
+// 16 x 32-bit TMEM columns of this thread's lane (tcgen05.st 32x32b.x16).
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t *r) {
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
-        "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
-        "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
-        "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
-      : "r"(taddr + 32));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
+// 2^x with the approximate base-2 exponential instruction of the PTX ISA
+// (a few ulp; subnormal results flush to zero, p < 2^-126 contributes
+// nothing at f32 precision).
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// bf16 hi/lo split of two probabilities, packed as two bf16 per word (the
+// lower key in the low half, as the TS-form MMA reads K).
+__device__ __forceinline__ void split2(float p0, float p1, uint32_t &hi, uint32_t &lo) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(p0, p1);
+  float2 hf = __bfloat1622float2(h);
+  __nv_bfloat162 l2 = __floats2bfloat162_rn(p0 - hf.x, p1 - hf.y);
+  hi = *reinterpret_cast<uint32_t *>(&h);
+  lo = *reinterpret_cast<uint32_t *>(&l2);
+}
+
+// P = 2^(s*c - m) for this thread's row of a 128-key tile held in sr,
+// written over the row's S columns 32 keys at a time (hi in a chunk's first
+// 16 columns, lo in the last 16).  Returns the row sum.  MASK: keys at kvalid
+// and beyond get probability 0.
+template <bool MASK>
+__device__ __forceinline__ float p_row(const uint32_t *sr, float c, float m, int kvalid, uint32_t tS) {
+  float ps0 = 0.0f, ps1 = 0.0f;
 #pragma unroll
-  for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+  for (int ch = 0; ch < 4; ++ch) {
+    uint32_t hw[16], lw[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int k0 = ch * 32 + 2 * i;
+      float p0 = ex2(fmaf(__uint_as_float(sr[k0]), c, -m));
+      float p1 = ex2(fmaf(__uint_as_float(sr[k0 + 1]), c, -m));
+      if (MASK) {
+        p0 = k0 < kvalid ? p0 : 0.0f;
+        p1 = k0 + 1 < kvalid ? p1 : 0.0f;
+      }
+      ps0 += p0;
+      ps1 += p1;
+      split2(p0, p1, hw[i], lw[i]);
+    }
+    tmem_st16(tS + 32 * ch, hw);
+    tmem_st16(tS + 32 * ch + 16, lw);
+  }
+  return ps0 + ps1;
+}
+
+struct AttnItem {
+  int req, qt[2], head[2], g;
+  bool two;
+};
+__device__ __forceinline__ AttnItem decode_item(int4 v) {
+  AttnItem it;
+  it.req = v.x;
+  it.qt[0] = v.y & 0xFFFF;
+  it.qt[1] = (int)((unsigned)v.y >> 16);
+  it.head[0] = v.z & 0xFFFF;
+  it.head[1] = (int)((unsigned)v.z >> 16);
+  it.g = v.w;
+  it.two = it.head[1] != 0xFFFF;
+  return it;
 }
 
 __global__ void __launch_bounds__(AT_THREADS, 1)
@@ -180,20 +247,18 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                        float *out, __nv_bfloat16 *out_hi, __nv_bfloat16 *out_lo, int ldp, AttnDims a, int *err) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *sm = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint64_t *q_full = (uint64_t *)(sm + AT_BAR);
-  uint64_t *q_empty = q_full + 1;
-  uint64_t *kv_full = q_full + 2;   // [2]
-  uint64_t *kv_empty = q_full + 4;  // [2]
-  uint64_t *s_full = q_full + 6;    // [2]
-  uint64_t *s_empty = q_full + 8;   // [2]  S/P buffer free (PV of its tile done)
-  uint64_t *p_full = q_full + 10;   // [2]  P written over the S buffer
-  uint64_t *o_full = q_full + 12;   // [2]
-  uint64_t *o_empty = q_full + 14;  // [2]
-  uint64_t *xbar = q_full + 16;     // the two softmax warpgroups' exchange rendezvous
-  uint32_t *tmem_slot = (uint32_t *)(q_full + 17);
+  uint64_t *bars = (uint64_t *)(sm + AT_BAR);
+  uint64_t *q_full = bars, *q_empty = bars + 1;
+  uint64_t *kv_full = bars + 2;   // [stage]
+  uint64_t *kv_empty = bars + 4;  // [stage]
+  uint64_t *s_full = bars + 6;    // [slot] S_x computed
+  uint64_t *p_full = bars + 8;    // [slot] P_x written and O_x rescaled (128 arrivals)
+  uint64_t *pv_done = bars + 10;  // [slot] PV_x complete: S_x may be overwritten
+  uint64_t *o_done = bars + 12;   // [slot] the item's last PV_x complete
+  uint64_t *o_free = bars + 14;   // [slot] O_x read by the epilogue (128 arrivals)
+  uint32_t *tmem_slot = (uint32_t *)(bars + 16);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int rep = a.H / a.KVH;
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     mbar_init(q_empty, 1);
@@ -201,15 +266,14 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
       mbar_init(&s_full[s], 1);
-      mbar_init(&s_empty[s], 1);
-      mbar_init(&p_full[s], 256);
-      mbar_init(&o_full[s], 1);
-      mbar_init(&o_empty[s], 256);
+      mbar_init(&p_full[s], 128);
+      mbar_init(&pv_done[s], 1);
+      mbar_init(&o_done[s], 1);
+      mbar_init(&o_free[s], 128);
     }
-    mbar_init(xbar, 256);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 1) {  // S/P: 2 x 128 columns, O: 2 x 64 columns
+  if (warp == 1) {  // S_a, S_b: 2 x 128 columns; O_a, O_b: 2 x 64 columns
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(512));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -218,28 +282,30 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *(volatile uint32_t *)tmem_slot;
-  const uint32_t t_o = tmem + 256;  // O buffer b at t_o + 64 b
-
-  if (warp == 0) {
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(AT_REG_PRODUCER));
+    if (warp == 0) {
     if (lane == 0) {  // ── TMA producer ──
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
       bool ok = true;
       for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++it) {
-        const int4 item = items[w];
-        const int64_t off = seq_off[item.x];
-        const int T = (int)(seq_off[item.x + 1] - off);
-        const int nk = (T + AT_BN - 1) / AT_BN, g = item.z / rep;
+        const AttnItem item = decode_item(items[w]);
+        const int64_t off = seq_off[item.req];
+        const int T = (int)(seq_off[item.req + 1] - off);
+        const int nk = (T + AT_BN - 1) / AT_BN;
         if (!(ok = mbar_wait(q_empty, (it & 1) ^ 1, err))) break;
-        mbar_expect_tx(q_full, 2 * AT_TILE);
-        const int qrow = item.z * slab + (int)off + item.y * AT_BM;
-        tma_load_2d(sm + AT_Q, &tmQh, q_full, 0, qrow);
-        tma_load_2d(sm + AT_Q + AT_TILE, &tmQl, q_full, 0, qrow);
+        mbar_expect_tx(q_full, (item.two ? 4 : 2) * AT_TILE);
+        for (int x = 0; x < (item.two ? 2 : 1); ++x) {
+          const int qrow = item.head[x] * slab + (int)off + item.qt[x] * AT_BM;
+          tma_load_2d(sm + AT_Q + 2 * x * AT_TILE, &tmQh, q_full, 0, qrow);
+          tma_load_2d(sm + AT_Q + (2 * x + 1) * AT_TILE, &tmQl, q_full, 0, qrow);
+        }
         for (int j = 0; j < nk; ++j) {
           if (!(ok = mbar_wait(&kv_empty[stage], phase ^ 1, err))) break;
           uint8_t *st = sm + AT_KV + stage * AT_STAGE;
-          const int krow = g * slab + (int)off + j * AT_BN;
+          const int krow = item.g * slab + (int)off + j * AT_BN;
           mbar_expect_tx(&kv_full[stage], AT_STAGE);
           tma_load_2d(st, &tmKh, &kv_full[stage], 0, krow);
           tma_load_2d(st + AT_TILE, &tmKl, &kv_full[stage], 0, krow);
@@ -265,185 +331,192 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     if (lane == 0) {  // ── MMA issuer ──
       constexpr uint32_t ID_S = umma_idesc(AT_BM, AT_BN);
       constexpr uint32_t ID_PV = umma_idesc(AT_BM, AT_HD, true);
-      int stage = 0;
-      uint32_t phase = 0;
-      uint32_t jj = 0, pv = 0;
-      int it = 0;
-      bool ok = true;
-      int pv_stage = 0, pv_sb = 0;
-      // O_t = P_t V_t for the tile t whose S/P buffer is `sb` and whose K/V
-      // sit in stage `st`; O_t goes to O buffer (pv & 1).
-      auto do_pv = [&](int st, int sb) -> bool {
-        const int ob = pv & 1;
-        if (!mbar_wait(&p_full[sb], (pv >> 1) & 1, err) || !mbar_wait(&o_empty[ob], ((pv >> 1) & 1) ^ 1, err))
-          return false;
+      // per-slot phase counters (scalars: x is 0 or 1)
+      uint32_t pv_issued0 = 0, pv_issued1 = 0, pv_waited0 = 0, pv_waited1 = 0, p_seen0 = 0, p_seen1 = 0;
+      uint32_t items0 = 0, items1 = 0;
+      // S_x = Q_x K^T from stage st, once the slot's previous PV (which reads
+      // P over S_x) has completed.
+      auto issue_s = [&](int x, int st) -> bool {
+        const uint32_t waited = x ? pv_waited1 : pv_waited0;
+        if ((x ? pv_issued1 : pv_issued0) > waited) {
+          if (!mbar_wait(&pv_done[x], waited & 1, err)) return false;
+          if (x) ++pv_waited1; else ++pv_waited0;
+        }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         uint8_t *kvs = sm + AT_KV + st * AT_STAGE;
-        const uint32_t d = t_o + (uint32_t)(ob * AT_HD);
-        const uint32_t ph = tmem + (uint32_t)(sb * AT_BN), pl = ph + 64;
-#pragma unroll
-        for (int ks = 0; ks < AT_BN / 16; ++ks) {
-          const uint64_t vh = umma_desc_mn(kvs + 2 * AT_TILE + ks * 2048);
-          const uint64_t vl = umma_desc_mn(kvs + 3 * AT_TILE + ks * 2048);
-          umma_bf16_ts(d, ph + ks * 8, vh, ID_PV, ks ? 1u : 0u);
-          umma_bf16_ts(d, ph + ks * 8, vl, ID_PV, 1u);
-          umma_bf16_ts(d, pl + ks * 8, vh, ID_PV, 1u);
+        const uint32_t d = tmem + (uint32_t)(x * AT_BN);
+#pragma unroll 1
+        for (int ks = 0; ks < AT_HD / 16; ++ks) {
+          const uint64_t adv = (uint64_t)((ks * 32) >> 4);
+          const uint64_t qh = umma_desc(sm + AT_Q + 2 * x * AT_TILE) + adv;
+          const uint64_t ql = umma_desc(sm + AT_Q + (2 * x + 1) * AT_TILE) + adv;
+          const uint64_t kh = umma_desc(kvs) + adv, kl = umma_desc(kvs + AT_TILE) + adv;
+          umma_bf16(d, qh, kh, ID_S, ks ? 1u : 0u);
+          umma_bf16(d, qh, kl, ID_S, 1u);
+          umma_bf16(d, ql, kh, ID_S, 1u);
         }
-        umma_commit(&o_full[ob]);
-        umma_commit(&s_empty[sb]);   // the S/P buffer may take the tile after next
-        umma_commit(&kv_empty[st]);  // S and PV of this tile are done with its K/V
-        ++pv;
+        umma_commit(&s_full[x]);
         return true;
       };
+      // O_x (+)= P_x V from stage st, once the softmax has written P_x (and,
+      // on an item's first tile, the previous item's O_x has been read out).
+      auto issue_pv = [&](int x, int st, int j, bool last) -> bool {
+        const uint32_t seen = x ? p_seen1 : p_seen0;
+        if (!mbar_wait(&p_full[x], seen & 1, err)) return false;
+        if (x) ++p_seen1; else ++p_seen0;
+        const uint32_t items = x ? items1 : items0;
+        if (j == 0 && items > 0 && !mbar_wait(&o_free[x], (items - 1) & 1, err)) return false;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        uint8_t *kvs = sm + AT_KV + st * AT_STAGE;
+        const uint32_t d = tmem + 256u + (uint32_t)(x * AT_HD);
+        const uint32_t pbase = tmem + (uint32_t)(x * AT_BN);
+#pragma unroll 1
+        for (int ks = 0; ks < AT_BN / 16; ++ks) {
+          // keys 16ks..16ks+15: chunk ks/2, hi at 32(ks/2) + 8(ks%2), lo 16 columns on
+          const uint32_t ph = pbase + 32u * (ks >> 1) + 8u * (ks & 1), pl = ph + 16u;
+          const uint64_t vh = umma_desc_mn(kvs + 2 * AT_TILE + ks * 2048);
+          const uint64_t vl = umma_desc_mn(kvs + 3 * AT_TILE + ks * 2048);
+          umma_bf16_ts(d, ph, vh, ID_PV, (j > 0 || ks > 0) ? 1u : 0u);
+          umma_bf16_ts(d, ph, vl, ID_PV, 1u);
+          umma_bf16_ts(d, pl, vh, ID_PV, 1u);
+        }
+        umma_commit(&pv_done[x]);
+        if (x) ++pv_issued1; else ++pv_issued0;
+        if (last) umma_commit(&o_done[x]);
+        return true;
+      };
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool ok = true;
       for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++it) {
-        const int4 item = items[w];
-        const int T = (int)(seq_off[item.x + 1] - seq_off[item.x]);
+        const AttnItem item = decode_item(items[w]);
+        const int T = (int)(seq_off[item.req + 1] - seq_off[item.req]);
         const int nk = (T + AT_BN - 1) / AT_BN;
         if (!(ok = mbar_wait(q_full, it & 1, err))) break;
+        if (!(ok = mbar_wait(&kv_full[stage], phase, err))) break;
+        if (!(ok = issue_s(0, stage))) break;
+        if (item.two && !(ok = issue_s(1, stage))) break;
+        if (nk == 1) umma_commit(q_empty);  // every S of the item issued
         for (int j = 0; j < nk && ok; ++j) {
-          const int sb = jj & 1;
-          if (!(ok = mbar_wait(&kv_full[stage], phase, err))) break;
-          if (!(ok = mbar_wait(&s_empty[sb], ((jj >> 1) & 1) ^ 1, err))) break;
-          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          uint8_t *kvs = sm + AT_KV + stage * AT_STAGE;
-          const uint32_t d = tmem + (uint32_t)(sb * AT_BN);
-#pragma unroll
-          for (int ks = 0; ks < AT_HD / 16; ++ks) {
-            const uint64_t adv = (uint64_t)((ks * 32) >> 4);
-            const uint64_t qh = umma_desc(sm + AT_Q) + adv, ql = umma_desc(sm + AT_Q + AT_TILE) + adv;
-            const uint64_t kh = umma_desc(kvs) + adv, kl = umma_desc(kvs + AT_TILE) + adv;
-            umma_bf16(d, qh, kh, ID_S, ks ? 1u : 0u);
-            umma_bf16(d, qh, kl, ID_S, 1u);
-            umma_bf16(d, ql, kh, ID_S, 1u);
+          const int cur = stage;
+          const int nxt = stage ^ 1;
+          const uint32_t nph = stage == 1 ? phase ^ 1 : phase;
+          const bool more = j + 1 < nk, last = j + 1 == nk;
+          if (!(ok = issue_pv(0, cur, j, last))) break;
+          if (more) {
+            if (!(ok = mbar_wait(&kv_full[nxt], nph, err))) break;
+            if (!(ok = issue_s(0, nxt))) break;
           }
-          umma_commit(&s_full[sb]);
-          if (j == nk - 1) umma_commit(q_empty);
-          ++jj;
-          if (j > 0 && !(ok = do_pv(pv_stage, pv_sb))) break;
-          pv_stage = stage;
-          pv_sb = sb;
-          if (++stage == 2) {
-            stage = 0;
-            phase ^= 1;
+          if (item.two) {
+            if (!(ok = issue_pv(1, cur, j, last))) break;
+            if (more && !(ok = issue_s(1, nxt))) break;
           }
+          if (j + 2 == nk) umma_commit(q_empty);
+          umma_commit(&kv_empty[cur]);  // every S and PV reading K_j / V_j issued before this commit
+          stage = nxt;
+          phase = nph;
         }
-        if (ok) ok = do_pv(pv_stage, pv_sb);
+        if (ok) {
+          ++items0;
+          if (item.two) ++items1;
+        }
       }
     }
-  } else {  // ── softmax: warps 2-9, two warpgroups ──
-    const int quarter = warp & 3, wg = (warp - 2) >> 2;
+    }
+  } else {  // ── softmax: warps 4-7 slot a, warps 8-11 slot b ──
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(AT_REG_SOFTMAX));
+    const int quarter = warp & 3, x = (warp - 4) >> 2;
     const int r = quarter * 32 + lane;  // TMEM lane = query row of the tile
     const uint32_t lanes = (uint32_t)(quarter * 32) << 16;
-    float *xch = (float *)(sm + AT_XCH);  // [2 groups][128]: row maxima, then row sums
-    uint32_t jj = 0, pv = 0, xu = 0;
-    // O += O_t (computed by the MMA with the row maxima of tile t), after
-    // rescaling the running sum by corr_t = exp(m_{t-1} - m_t).
-    float o[32];
-    auto add_o = [&](float corr) -> bool {
-      const int ob = pv & 1;
-      if (!mbar_wait(&o_full[ob], (pv >> 1) & 1, err)) return false;
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      float v[32];
-      tmem_ld32(t_o + lanes + (uint32_t)(ob * AT_HD + wg * 32), v);
-      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-      mbar_arrive(&o_empty[ob]);
-#pragma unroll
-      for (int e = 0; e < 32; ++e) o[e] = o[e] * corr + v[e];
-      ++pv;
-      return true;
-    };
+    const uint32_t tS = tmem + lanes + (uint32_t)(x * AT_BN), tO = tmem + lanes + 256u + (uint32_t)(x * AT_HD);
+    const float c = a.scale * 1.4426950408889634f;  // hd^-0.5 * log2(e)
+    uint32_t s_seen = 0, o_seen = 0;
     for (int w = blockIdx.x; w < n_items; w += gridDim.x) {
-      const int4 item = items[w];
-      const int64_t off = seq_off[item.x];
-      const int T = (int)(seq_off[item.x + 1] - off);
+      const AttnItem item = decode_item(items[w]);
+      if (x == 1 && !item.two) continue;
+      const int64_t off = seq_off[item.req];
+      const int T = (int)(seq_off[item.req + 1] - off);
       const int nk = (T + AT_BN - 1) / AT_BN;
-      float m = -INFINITY, l = 0.0f, corr_prev = 0.0f;
-#pragma unroll
-      for (int e = 0; e < 32; ++e) o[e] = 0.0f;
+      float m = -INFINITY, l = 0.0f;
       bool ok = true;
       for (int j = 0; j < nk; ++j) {
-        const int sb = jj & 1;
-        if (!(ok = mbar_wait(&s_full[sb], (jj >> 1) & 1, err))) break;
+        if (!(ok = warp_wait(&s_full[x], s_seen & 1, err))) break;
+        ++s_seen;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        float v[64];
-        tmem_ld64(tmem + lanes + (uint32_t)(sb * AT_BN + wg * 64), v);
-        const int kvalid = T - j * AT_BN - wg * 64;  // keys of this half that belong to the request
-        float mx = -INFINITY;
+        const int kvalid = T - j * AT_BN;  // keys of this tile that belong to the request (>= 1)
+        uint32_t sr[128];
 #pragma unroll
-        for (int e = 0; e < 64; ++e) {
-          v[e] *= a.scale;
-          if (e < kvalid) mx = fmaxf(mx, v[e]);
-        }
-        xch[wg * 128 + r] = mx;
-        // after this rendezvous both halves hold their S in registers, so P
-        // may overwrite the S buffer
-        if (!(ok = xsync(xbar, xu, err))) break;
-        const float m_new = fmaxf(m, fmaxf(mx, xch[(wg ^ 1) * 128 + r]));
-        if (!(ok = xsync(xbar, xu, err))) break;  // both halves read before the next write
-        const float corr = expf(m - m_new);       // 0 on the first tile (m = -inf)
-        // Probabilities with the hardware exp2 intrinsic: __expf's error,
-        // 2 + |1.17 x| ulp for x = s - max <= 0, is ~1e-6 relative where p is
-        // not negligible, far inside the logit tolerance.
-        float psum = 0.0f;
-        uint32_t ph[32], pl[32];
+        for (int q = 0; q < 4; ++q) tmem_ld32_raw(tS + 32 * q, sr + 32 * q);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        if (kvalid >= AT_BN) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float p0 = (2 * i < kvalid) ? __expf(v[2 * i] - m_new) : 0.0f;
-          float p1 = (2 * i + 1 < kvalid) ? __expf(v[2 * i + 1] - m_new) : 0.0f;
-          psum += p0 + p1;
-          __nv_bfloat162 h = __floats2bfloat162_rn(p0, p1);
-          float2 hf = __bfloat1622float2(h);
-          __nv_bfloat162 lo = __floats2bfloat162_rn(p0 - hf.x, p1 - hf.y);
-          ph[i] = *reinterpret_cast<uint32_t *>(&h);
-          pl[i] = *reinterpret_cast<uint32_t *>(&lo);
+          for (int e = 0; e < 128; ++e) mx[e & 3] = fmaxf(mx[e & 3], __uint_as_float(sr[e]));
+        } else {
+#pragma unroll
+          for (int e = 0; e < 128; ++e)
+            if (e < kvalid) mx[e & 3] = fmaxf(mx[e & 3], __uint_as_float(sr[e]));
         }
-        // P over the S buffer: hi plane in columns [0, 64), lo in [64, 128),
-        // this half's 64 keys at column offset wg * 32
-        const uint32_t tp = tmem + lanes + (uint32_t)(sb * AT_BN + wg * 32);
-        tmem_st32(tp, ph);
-        tmem_st32(tp + 64, pl);
+        const float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * c;
+        float corr = 1.0f;
+        const bool resc = j == 0 || mt > m + AT_RESCALE;
+        if (resc) {
+          corr = ex2(m - mt);  // 0 on the first tile (m = -inf)
+          m = mt;
+        }
+        const float psum = kvalid >= AT_BN ? p_row<false>(sr, c, m, kvalid, tS) : p_row<true>(sr, c, m, kvalid, tS);
+        l = l * corr + psum;
+        // O_x *= corr (PV_x(j-1) completed before S_x(j) was issued).  The
+        // tcgen05 loads and stores are warp-collective, so the whole warp
+        // takes this branch when any of its rows moved m (corr = 1 elsewhere).
+        if (__any_sync(0xffffffffu, resc && j > 0)) {
+          uint32_t ov[64];
+          tmem_ld32_raw(tO, ov);
+          tmem_ld32_raw(tO + 32, ov + 32);
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+          for (int e = 0; e < 64; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * corr);
+          tmem_st32(tO, ov);
+          tmem_st32(tO + 32, ov + 32);
+        }
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-        mbar_arrive(&p_full[sb]);
-        l = l * corr + psum;
-        m = m_new;
-        ++jj;
-        if (j > 0 && !(ok = add_o(corr_prev))) break;  // O of the previous tile
-        corr_prev = corr;
+        mbar_arrive(&p_full[x]);
       }
-      if (!ok || !add_o(corr_prev)) break;
-      // combine the two halves' row sums
-      xch[wg * 128 + r] = l;
-      if (!xsync(xbar, xu, err)) break;
-      const float ltot = l + xch[(wg ^ 1) * 128 + r];
-      if (!xsync(xbar, xu, err)) break;  // the exchange area is reused by the next item
-      const int qr = item.y * AT_BM + r;
+      if (!ok) break;
+      if (!warp_wait(&o_done[x], o_seen & 1, err)) break;  // the item's last PV_x
+      ++o_seen;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      uint32_t ov[64];
+      tmem_ld32_raw(tO, ov);
+      tmem_ld32_raw(tO + 32, ov + 32);
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      mbar_arrive(&o_free[x]);  // O_x may take the next item's PV
+      const int qt = x ? item.qt[1] : item.qt[0], head = x ? item.head[1] : item.head[0];
+      const int qr = qt * AT_BM + r;
       if (qr < T) {
-        const float inv = 1.0f / ltot;
+        const float inv = 1.0f / l;
         if (out_hi) {  // bf16 hi/lo planes of the O projection's input
-          const int64_t base = (off + qr) * (int64_t)ldp + item.z * AT_HD + wg * 32;
-          uint32_t hw[16], lw[16];
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            float x0 = o[2 * e] * inv, x1 = o[2 * e + 1] * inv;
-            __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
-            float2 hf = __bfloat1622float2(h);
-            __nv_bfloat162 lo = __floats2bfloat162_rn(x0 - hf.x, x1 - hf.y);
-            hw[e] = *reinterpret_cast<uint32_t *>(&h);
-            lw[e] = *reinterpret_cast<uint32_t *>(&lo);
-          }
+          const int64_t base = (off + qr) * (int64_t)ldp + head * AT_HD;
           uint4 *dh = reinterpret_cast<uint4 *>(out_hi + base), *dl = reinterpret_cast<uint4 *>(out_lo + base);
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            dh[e] = make_uint4(hw[4 * e], hw[4 * e + 1], hw[4 * e + 2], hw[4 * e + 3]);
-            dl[e] = make_uint4(lw[4 * e], lw[4 * e + 1], lw[4 * e + 2], lw[4 * e + 3]);
+          for (int e = 0; e < 8; ++e) {
+            uint32_t hw[4], lw[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              split2(__uint_as_float(ov[8 * e + 2 * q]) * inv, __uint_as_float(ov[8 * e + 2 * q + 1]) * inv, hw[q],
+                     lw[q]);
+            dh[e] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            dl[e] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
           }
         } else {
-          float4 *dst =
-              reinterpret_cast<float4 *>(out + (off + qr) * (int64_t)(a.H * AT_HD) + item.z * AT_HD + wg * 32);
+          float4 *dst = reinterpret_cast<float4 *>(out + (off + qr) * (int64_t)(a.H * AT_HD) + head * AT_HD);
 #pragma unroll
-          for (int e = 0; e < 8; ++e)
-            dst[e] = make_float4(o[4 * e] * inv, o[4 * e + 1] * inv, o[4 * e + 2] * inv, o[4 * e + 3] * inv);
+          for (int e = 0; e < 16; ++e)
+            dst[e] = make_float4(__uint_as_float(ov[4 * e]) * inv, __uint_as_float(ov[4 * e + 1]) * inv,
+                                 __uint_as_float(ov[4 * e + 2]) * inv, __uint_as_float(ov[4 * e + 3]) * inv);
         }
       }
     }
@@ -490,6 +563,17 @@ cudaError_t encoder_attention_tc(const AttnPlanes &p, const int64_t *seq_off, co
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int grid = n_items < sms ? n_items : sms;
+  // setmaxnreg redistributes exactly the registers of a 168-register launch;
+  // any other count would leave the increase waiting for registers that
+  // never come, so such a build is refused here.
+  static int regs = -1;
+  if (regs < 0) {
+    cudaFuncAttributes fa;
+    cudaError_t e = cudaFuncGetAttributes(&fa, enc_attn_tc_kernel);
+    if (e != cudaSuccess) return e;
+    regs = fa.numRegs;
+  }
+  if (regs != AT_REG_LAUNCH) return cudaErrorInvalidKernelImage;
   auto M = [](const unsigned char *m) { return *reinterpret_cast<const CUtensorMap *>(m); };
   enc_attn_tc_kernel<<<grid, AT_THREADS, AT_SMEM, st>>>(M(p.q.hi), M(p.q.lo), M(p.k.hi), M(p.k.lo), M(p.v.hi),
                                                         M(p.v.lo), seq_off, (const int4 *)items, n_items, p.slab, out,

@@ -55,6 +55,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity, int *err
   }
 }
 
+// Bounded wait with one outcome for the whole (converged) warp, so that a
+// timeout can never split a warp ahead of a warp-collective tcgen05
+// instruction.
+__device__ __forceinline__ bool warp_wait(uint64_t *b, uint32_t parity, int *err) {
+  return __all_sync(0xffffffffu, mbar_wait(b, parity, err));
+}
+
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(

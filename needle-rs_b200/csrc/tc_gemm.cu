@@ -27,7 +27,7 @@
 //               TMEM lanes 32q..32q+31 = output rows), fused epilogue
 //               (store / gated residual / activation / per-head k-norm)
 // TMEM holds two accumulators so the epilogue of tile i overlaps the MMAs
-// of tile i+1.  TMA loads never use cluster multicast.  Every mbarrier wait
+// of tile i+1.  Every TMA load fills only its own CTA's shared memory.  Every mbarrier wait
 // is bounded: on expiry the kernel records an error flag and unwinds.
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -337,7 +337,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     int i = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
       const int buf = i & 1;
-      if (!mbar_wait(&tfull[buf], (i >> 1) & 1, err)) break;
+      if (!warp_wait(&tfull[buf], (i >> 1) & 1, err)) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const int mt = t / num_n, nt = t - mt * num_n;
       const int m = mt * TC_BM + q * 32 + lane;

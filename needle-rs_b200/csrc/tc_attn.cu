@@ -26,9 +26,14 @@
 //   P_x -> TMEM          bf16 hi/lo over S_x (tcgen05.st): keys 32c..32c+31
 //                        in columns 32c..32c+15 (hi) and 32c+16..32c+31 (lo),
 //                        the columns their own S values came from
-//   O_x (+)= P_x V_j     M128 N64 K16, A = P from TMEM, V read MN-major from
-//                        its [key][dim] tile; O stays in TMEM and the softmax
-//                        warps rescale it there when m moves
+//   O_x (+)= P_x V_j     A = P from TMEM, V read MN-major from its [key][dim]
+//                        tiles: per 16 keys one M128 N128 K16 MMA of P_hi
+//                        against [V_hi | V_lo] (the two planes as one
+//                        128-wide operand) and one M128 N64 K16 MMA of P_lo
+//                        against V_hi; O_x holds P V_hi + P_lo V_hi in its
+//                        first 64 columns and P_hi V_lo in the next 64, summed
+//                        when the row is written out.  O stays in TMEM and the
+//                        softmax warps rescale it there when m moves
 // The MMA warp issues S_a(0), S_b(0), then per tile PV_a(j), S_a(j+1),
 // PV_b(j), S_b(j+1): while one slot's warps run the softmax, the tensor core
 // works on the other slot.  Each product is the 3-term split hi*hi + hi*lo +
@@ -330,7 +335,8 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
   } else if (warp == 1) {
     if (lane == 0) {  // ── MMA issuer ──
       constexpr uint32_t ID_S = umma_idesc(AT_BM, AT_BN);
-      constexpr uint32_t ID_PV = umma_idesc(AT_BM, AT_HD, true);
+      constexpr uint32_t ID_PV2 = umma_idesc(AT_BM, 2 * AT_HD, true);  // P_hi x [V_hi | V_lo]
+      constexpr uint32_t ID_PV = umma_idesc(AT_BM, AT_HD, true);       // P_lo x V_hi
       // per-slot phase counters (scalars: x is 0 or 1)
       uint32_t pv_issued0 = 0, pv_issued1 = 0, pv_waited0 = 0, pv_waited1 = 0, p_seen0 = 0, p_seen1 = 0;
       uint32_t items0 = 0, items1 = 0;
@@ -368,16 +374,16 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         if (j == 0 && items > 0 && !mbar_wait(&o_free[x], (items - 1) & 1, err)) return false;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         uint8_t *kvs = sm + AT_KV + st * AT_STAGE;
-        const uint32_t d = tmem + 256u + (uint32_t)(x * AT_HD);
+        const uint32_t d = tmem + 256u + (uint32_t)(x * 2 * AT_HD);
         const uint32_t pbase = tmem + (uint32_t)(x * AT_BN);
 #pragma unroll 1
         for (int ks = 0; ks < AT_BN / 16; ++ks) {
           // keys 16ks..16ks+15: chunk ks/2, hi at 32(ks/2) + 8(ks%2), lo 16 columns on
           const uint32_t ph = pbase + 32u * (ks >> 1) + 8u * (ks & 1), pl = ph + 16u;
+          // V_lo sits one plane tile (AT_TILE bytes) after V_hi: the second MN atom
+          const uint64_t vhl = umma_desc_mn(kvs + 2 * AT_TILE + ks * 2048, AT_TILE);
           const uint64_t vh = umma_desc_mn(kvs + 2 * AT_TILE + ks * 2048);
-          const uint64_t vl = umma_desc_mn(kvs + 3 * AT_TILE + ks * 2048);
-          umma_bf16_ts(d, ph, vh, ID_PV, (j > 0 || ks > 0) ? 1u : 0u);
-          umma_bf16_ts(d, ph, vl, ID_PV, 1u);
+          umma_bf16_ts(d, ph, vhl, ID_PV2, (j > 0 || ks > 0) ? 1u : 0u);
           umma_bf16_ts(d, pl, vh, ID_PV, 1u);
         }
         umma_commit(&pv_done[x]);
@@ -429,7 +435,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     const int quarter = warp & 3, x = (warp - 4) >> 2;
     const int r = quarter * 32 + lane;  // TMEM lane = query row of the tile
     const uint32_t lanes = (uint32_t)(quarter * 32) << 16;
-    const uint32_t tS = tmem + lanes + (uint32_t)(x * AT_BN), tO = tmem + lanes + 256u + (uint32_t)(x * AT_HD);
+    const uint32_t tS = tmem + lanes + (uint32_t)(x * AT_BN), tO = tmem + lanes + 256u + (uint32_t)(x * 2 * AT_HD);
     const float c = a.scale * 1.4426950408889634f;  // hd^-0.5 * log2(e)
     uint32_t s_seen = 0, o_seen = 0;
     for (int w = blockIdx.x; w < n_items; w += gridDim.x) {
@@ -471,14 +477,14 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         // tcgen05 loads and stores are warp-collective, so the whole warp
         // takes this branch when any of its rows moved m (corr = 1 elsewhere).
         if (__any_sync(0xffffffffu, resc && j > 0)) {
-          uint32_t ov[64];
-          tmem_ld32_raw(tO, ov);
-          tmem_ld32_raw(tO + 32, ov + 32);
+          uint32_t ov[128];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) tmem_ld32_raw(tO + 32 * q, ov + 32 * q);
           asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-          for (int e = 0; e < 64; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * corr);
-          tmem_st32(tO, ov);
-          tmem_st32(tO + 32, ov + 32);
+          for (int e = 0; e < 128; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * corr);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) tmem_st32(tO + 32 * q, ov + 32 * q);
         }
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -488,12 +494,14 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       if (!warp_wait(&o_done[x], o_seen & 1, err)) break;  // the item's last PV_x
       ++o_seen;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      uint32_t ov[64];
-      tmem_ld32_raw(tO, ov);
-      tmem_ld32_raw(tO + 32, ov + 32);
+      uint32_t ov[128];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) tmem_ld32_raw(tO + 32 * q, ov + 32 * q);
       asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       mbar_arrive(&o_free[x]);  // O_x may take the next item's PV
+#pragma unroll
+      for (int e = 0; e < 64; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) + __uint_as_float(ov[64 + e]));
       const int qt = x ? item.qt[1] : item.qt[0], head = x ? item.head[1] : item.head[0];
       const int qr = qt * AT_BM + r;
       if (qr < T) {

@@ -93,11 +93,14 @@ __host__ __device__ constexpr uint32_t umma_idesc(int M, int N, bool b_mn = fals
 // UMMA descriptor of an MN-major operand with 128-byte swizzle whose MN
 // extent is one 64-element atom: rows of 128 bytes = 64 bf16 along MN, one
 // row per K index, 8-row (8 K) groups of 1024 bytes (SBO).
-__device__ __forceinline__ uint64_t umma_desc_mn(const void *smem) {
+// lbo: byte stride between consecutive 64-element MN atoms when the operand
+// spans more than one (N = 128 reads the atom at smem + lbo as elements
+// 64..127).
+__device__ __forceinline__ uint64_t umma_desc_mn(const void *smem, uint32_t lbo = 16) {
   uint64_t addr = smem_u32(smem);
   uint64_t d = 0;
-  d |= (addr >> 4) & 0x3FFFull;      // start address
-  d |= (uint64_t)1 << 16;            // LBO: stride between 64-element MN atoms (one atom here)
+  d |= (addr >> 4) & 0x3FFFull;                 // start address
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;  // LBO: stride between 64-element MN atoms
   d |= (uint64_t)(1024 >> 4) << 32;  // SBO: stride between 8-row K groups
   d |= (uint64_t)1 << 46;            // version
   d |= (uint64_t)2 << 61;            // SWIZZLE_128B

@@ -18,16 +18,23 @@
 // is ~100 MB).  Activations arrive as bf16 planes [M][Kp] written by the
 // producing kernel (norm, attention) or by split_rows().
 //
-// Kernel.  Persistent, one CTA per SM, 256 threads, warp-specialised:
+// Kernel.  Persistent, one CTA per SM, 384 threads, warp-specialised:
 //   warp 0      TMA producer: 128x64 A tiles and BNx64 B tiles (hi and lo),
-//               128-byte swizzle, into a 3-stage shared-memory ring
+//               128-byte swizzle, into a shared-memory ring (3 stages at
+//               BN = 128, 2 at BN = 256; B arrives as 128-row boxes)
 //   warp 1      TMEM allocation + MMA issue (one elected lane):
 //               tcgen05.mma.cta_group::1.kind::f16, M=128, N=BN, K=16
-//   warps 4-7   epilogue: tcgen05.ld of the f32 accumulator (warp 4+q owns
-//               TMEM lanes 32q..32q+31 = output rows), fused epilogue
-//               (store / gated residual / activation / per-head k-norm)
+//   warps 2-3   idle (they complete the producer warpgroup)
+//   warps 4-11  epilogue in two warpgroups, one per half of the tile's
+//               columns: tcgen05.ld of the f32 accumulator (warp w owns TMEM
+//               lanes 32(w%4).. = output rows), fused epilogue (store / gated
+//               residual / activation / per-head k-norm / q-k norm + RoPE to
+//               attention planes / masked argmax).  The producer warpgroup
+//               hands registers to them with setmaxnreg.
 // TMEM holds two accumulators so the epilogue of tile i overlaps the MMAs
-// of tile i+1.  Every TMA load fills only its own CTA's shared memory.  Every mbarrier wait
+// of tile i+1.  BN = 256 (tall matrices) halves the shared-memory operand
+// bytes each MMA reads per output; BN = 128 keeps more tiles than SMs for
+// the decode-sized ones.  Every TMA load fills only its own CTA's shared memory.  Every mbarrier wait
 // is bounded: on expiry the kernel records an error flag and unwinds.
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -42,7 +49,13 @@ namespace {
 
 using namespace tc;
 
-constexpr int TC_BM = 128, TC_BK = 64, TC_STAGES = 3, TC_THREADS = 256;
+constexpr int TC_BM = 128, TC_BK = 64, TC_THREADS = 384;
+// Registers a thread: launched at 168 (65,536 / 384, rounded down to 8); the
+// producer warpgroup drops to 56 and the two epilogue warpgroups rise to 224:
+// 128 x 56 + 256 x 224 = 384 x 168.
+constexpr int TC_REG_LAUNCH = 168, TC_REG_PRODUCER = 56, TC_REG_EPILOGUE = 224;
+static_assert(128 * TC_REG_PRODUCER + 256 * TC_REG_EPILOGUE == TC_THREADS * TC_REG_LAUNCH,
+              "the register split must add up to the launch's registers");
 struct TcEpi {
   MatmulOut o;
   int N;
@@ -219,7 +232,7 @@ __device__ __forceinline__ unsigned long long epi_argmax32(const TcEpi &e, int m
   return best;
 }
 
-template <int BN>
+template <int BN, int TC_STAGES>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
                    const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl, int M, int N,
@@ -247,7 +260,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 128);
+      mbar_init(&tempty[b], 256);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -261,6 +274,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *(volatile uint32_t *)tmem_slot;
 
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(TC_REG_PRODUCER));
   if (warp == 0) {
     // ── TMA producer ──
     if (lane == 0) {
@@ -279,8 +294,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           mbar_expect_tx(&full[stage], STAGE_BYTES);
           tma_load_2d(st, &tmAh, &full[stage], kb * TC_BK, mt * TC_BM);
           tma_load_2d(st + A_BYTES, &tmAl, &full[stage], kb * TC_BK, mt * TC_BM);
-          tma_load_2d(st + 2 * A_BYTES, &tmBh, &full[stage], kb * TC_BK, nt * BN);
-          tma_load_2d(st + 2 * A_BYTES + B_BYTES, &tmBl, &full[stage], kb * TC_BK, nt * BN);
+#pragma unroll
+          for (int h = 0; h < BN / 128; ++h) {  // 128-row boxes, contiguous in shared memory
+            tma_load_2d(st + 2 * A_BYTES + h * (B_BYTES * 128 / BN), &tmBh, &full[stage], kb * TC_BK,
+                        nt * BN + 128 * h);
+            tma_load_2d(st + 2 * A_BYTES + B_BYTES + h * (B_BYTES * 128 / BN), &tmBl, &full[stage], kb * TC_BK,
+                        nt * BN + 128 * h);
+          }
           if (++stage == TC_STAGES) {
             stage = 0;
             phase ^= 1;
@@ -331,9 +351,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (ok) umma_commit(&tfull[buf]);
       }
     }
-  } else if (warp >= 4) {
-    // ── epilogue ──
-    const int q = warp - 4;
+  }
+  } else {
+    // ── epilogue: warpgroup `half` takes columns [half * BN/2, (half + 1) * BN/2) ──
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(TC_REG_EPILOGUE));
+    const int q = warp & 3, half = (warp - 4) >> 2;
     int i = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
       const int buf = i & 1;
@@ -345,7 +367,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const bool amax = e.o.epi == EPI_ARGMAX;
       const bool wide = e.o.epi == EPI_KNORM || e.o.epi == EPI_QKV;  // whole 64-column heads
       unsigned long long best = 0ull;
-      for (int c = 0; c < BN; c += (wide ? 64 : 32)) {
+      for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += (wide ? 64 : 32)) {
         float v[64];
         tmem_ld32(base + c, v);
         if (wide) tmem_ld32(base + c + 32, v + 32);
@@ -440,9 +462,11 @@ int tc_sm_count() {
   return n[dev] > 0 ? n[dev] : 148;
 }
 
-constexpr size_t tc_smem_bytes(int BN) {
-  return 1024 + (size_t)TC_STAGES * (2 * TC_BM * TC_BK * 2 + 2 * BN * TC_BK * 2) + 256;
+constexpr size_t tc_smem_bytes(int BN, int stages) {
+  return 1024 + (size_t)stages * (2 * TC_BM * TC_BK * 2 + 2 * BN * TC_BK * 2) + 256;
 }
+static_assert(tc_smem_bytes(128, 3) <= 232448 && tc_smem_bytes(256, 2) <= 232448,
+              "exceeds the 227 KB of dynamic shared memory per block");
 
 }  // namespace
 
@@ -505,18 +529,44 @@ cudaError_t tc_matmul(const TcPlanes &A, int M, const TcPlanes &B, int N, const 
   }
   if (o.epi == EPI_ACT && (N & 1)) return cudaErrorInvalidValue;
   TcEpi e{o, N};
-  const int tiles = ((M + TC_BM - 1) / TC_BM) * ((N + 127) / 128);
-  const int grid = tiles < tc_sm_count() ? tiles : tc_sm_count();
-  tc_gemm_kernel<128><<<grid, TC_THREADS, tc_smem_bytes(128), st>>>(
-      *reinterpret_cast<const CUtensorMap *>(A.hi), *reinterpret_cast<const CUtensorMap *>(A.lo),
-      *reinterpret_cast<const CUtensorMap *>(B.hi), *reinterpret_cast<const CUtensorMap *>(B.lo), M, N, A.Kp, e, err,
-      b_lo_zero ? 1 : 0);
+  // setmaxnreg redistributes exactly the registers of a 168-register launch;
+  // any other count would leave the increase waiting for registers that
+  // never come, so such a build is refused here.
+  static int regs[2] = {-1, -1};
+  if (regs[0] < 0) {
+    cudaFuncAttributes fa;
+    cudaError_t ce = cudaFuncGetAttributes(&fa, tc_gemm_kernel<128, 3>);
+    if (ce != cudaSuccess) return ce;
+    regs[0] = fa.numRegs;
+    ce = cudaFuncGetAttributes(&fa, tc_gemm_kernel<256, 2>);
+    if (ce != cudaSuccess) return ce;
+    regs[1] = fa.numRegs;
+  }
+  if (regs[0] != TC_REG_LAUNCH || regs[1] != TC_REG_LAUNCH) return cudaErrorInvalidKernelImage;
+  const int sms = tc_sm_count(), num_m = (M + TC_BM - 1) / TC_BM;
+  const auto *ah = reinterpret_cast<const CUtensorMap *>(A.hi), *al = reinterpret_cast<const CUtensorMap *>(A.lo);
+  const auto *bh = reinterpret_cast<const CUtensorMap *>(B.hi), *bl = reinterpret_cast<const CUtensorMap *>(B.lo);
+  const int tiles256 = num_m * ((N + 255) / 256);
+  if (tiles256 >= 2 * sms) {
+    const int grid = sms;
+    tc_gemm_kernel<256, 2><<<grid, TC_THREADS, tc_smem_bytes(256, 2), st>>>(*ah, *al, *bh, *bl, M, N, A.Kp, e, err,
+                                                                           b_lo_zero ? 1 : 0);
+  } else {
+    const int tiles = num_m * ((N + 127) / 128);
+    const int grid = tiles < sms ? tiles : sms;
+    tc_gemm_kernel<128, 3><<<grid, TC_THREADS, tc_smem_bytes(128, 3), st>>>(*ah, *al, *bh, *bl, M, N, A.Kp, e, err,
+                                                                           b_lo_zero ? 1 : 0);
+  }
   return cudaGetLastError();
 }
 
 cudaError_t init_tc_kernels() {
-  return cudaFuncSetAttribute(tc_gemm_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              (int)tc_smem_bytes(128));
+  cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<128, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)tc_smem_bytes(128, 3));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(tc_gemm_kernel<256, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)tc_smem_bytes(256, 2));
+  return e;
 }
 
 }  // namespace ndl

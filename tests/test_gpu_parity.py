@@ -126,6 +126,26 @@ def test_int4_plan_vs_oracle(M):
         plan.close()
 
 
+@pytest.mark.parametrize("M,N,K", [(4800, 2176, 512), (4736, 2048, 96)])
+def test_int4_plan_wide_tiles_vs_oracle(M, N, K):
+    # Tall matrices take the 128 x 256 output tiles; N = 2176 leaves a
+    # half-empty last column tile, M = 4800 a partial last row tile.
+    x, packed, scales = wl.int4_case(M, N, K, seed=M + N)
+    rows = np.r_[0:64, M // 2 - 32:M // 2 + 32, M - 64:M]
+    ref = orc.matmul(packed, scales, K, N, x[rows], path=1)
+    wd, sd = dev(packed), dev(scales)
+    plan = nb.Int4Plan(wd.data_ptr(), sd.data_ptr(), K, N, scales.shape[0], max_m=M)
+    try:
+        y = torch.full((M, N), float("nan"), device="cuda")
+        plan.matmul(dev(x).data_ptr(), M, y.data_ptr())
+        plan.status()
+        got = y.cpu().numpy()
+        assert not np.isnan(got).any()
+        assert close_act(got[rows], ref), max_excess(got[rows], ref, True)
+    finally:
+        plan.close()
+
+
 @pytest.mark.parametrize("K,N", [(512, 2048), (33, 8), (65, 16), (16, 8), (4, 4), (2048, 24), (96, 40)])
 def test_int4_quantize_bit_exact(K, N):
     rng = np.random.default_rng(K * N)
@@ -315,6 +335,21 @@ def test_batched_decode_tensor_core_vs_oracle(full):
     tol = 2 * (ATOL + RTOL * 10.0)
     for r in (0, 1, 77, 159):
         rid, rmarg, rlg = ref.generate(prompts[r], steps, mask_bits=masks[r], want_logits=True)
+        assert tokens_match(ids[r], rid, rmarg, tol), r
+        assert close(lg[r, 0], rlg[0]), max_excess(lg[r, 0], rlg[0])
+
+
+def test_wide_prefill_tiles_vs_oracle(full):
+    # Over 9,500 prompt rows: every prefill projection (the fused QKV with its
+    # norm + RoPE epilogue included) runs with 128 x 256 output tiles.
+    eng, ref = full
+    ids_in, off = wl.random_prompts(96, 100, 128, 8192, seed=14)
+    prompts = [ids_in[off[i]:off[i + 1]] for i in range(96)]
+    steps = 3
+    ids, lens, lg = eng.run_batch_ids(prompts, steps, want_logits=True)
+    tol = 2 * (ATOL + RTOL * 10.0)
+    for r in (0, 50, 95):
+        rid, rmarg, rlg = ref.generate(prompts[r], steps, want_logits=True)
         assert tokens_match(ids[r], rid, rmarg, tol), r
         assert close(lg[r, 0], rlg[0]), max_excess(lg[r, 0], rlg[0])
 

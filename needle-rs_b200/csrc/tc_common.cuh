@@ -70,6 +70,35 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, u
       : "memory");
 }
 
+// ── CTA pairs (a cluster of two CTAs sharing one tcgen05.mma.cta_group::2) ──
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Shared-memory address of the same variable in CTA 0 of the pair (the
+// address bit that selects the peer cleared).
+__device__ __forceinline__ uint32_t pair_leader_addr(const void *p) { return smem_u32(p) & 0xFEFFFFFFu; }
+// TMA 2-D load into this CTA's own shared memory whose completed bytes are
+// counted on the pair leader's mbarrier.
+__device__ __forceinline__ void tma_load_2d_pair(void *dst, const CUtensorMap *map, uint32_t leader_bar, int x,
+                                                 int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+      "%4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(leader_bar), "r"(x), "r"(y)
+      : "memory");
+}
+// Arrive on the mbarrier at the same offset in CTA `rank` of the cluster.
+__device__ __forceinline__ void mbar_arrive_cluster(uint64_t *b, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(b)), "r"(rank));
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote) : "memory");
+}
+
 // UMMA shared-memory descriptor: K-major operand, 128-byte swizzle, 8-row
 // atoms of 1024 bytes stacked along M/N (SBO = 1024 B), version 1 (sm100).
 __device__ __forceinline__ uint64_t umma_desc(const void *smem) {
@@ -105,6 +134,27 @@ __device__ __forceinline__ uint64_t umma_desc_mn(const void *smem, uint32_t lbo 
   d |= (uint64_t)1 << 46;            // version
   d |= (uint64_t)2 << 61;            // SWIZZLE_128B
   return d;
+}
+
+// tcgen05.mma issued by the pair leader over both CTAs: A rows and B columns
+// split between the CTAs' shared memory at the same offsets, D split by rows
+// between their TMEM.
+__device__ __forceinline__ void umma_bf16_pair(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                               uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+// Arrive on the mbarrier at this offset in both CTAs of the pair once the
+// pair's earlier MMAs complete.
+__device__ __forceinline__ void umma_commit_pair(uint64_t *bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"((uint16_t)3)
+      : "memory");
 }
 
 __device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {

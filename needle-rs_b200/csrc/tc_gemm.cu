@@ -232,6 +232,34 @@ __device__ __forceinline__ unsigned long long epi_argmax32(const TcEpi &e, int m
   return best;
 }
 
+// Epilogue of accumulator columns [c0, c1) for this thread's output row m
+// (TMEM lane quarter at `base`); output column = n_base + accumulator column.
+__device__ __forceinline__ void epi_tile(const TcEpi &e, int M, int N, int m, uint32_t base, int c0, int c1,
+                                         int n_base) {
+  const bool amax = e.o.epi == EPI_ARGMAX;
+  const bool wide = e.o.epi == EPI_KNORM || e.o.epi == EPI_QKV;  // whole 64-column heads
+  unsigned long long best = 0ull;
+  for (int c = c0; c < c1; c += (wide ? 64 : 32)) {
+    float v[64];
+    tmem_ld32(base + c, v);
+    if (wide) tmem_ld32(base + c + 32, v + 32);
+    const int n0 = n_base + c;
+    if (m < M && n0 < N) {
+      if (amax) {
+        unsigned long long k = epi_argmax32(e, m, n0, v);
+        best = k > best ? k : best;
+      } else if (e.o.epi == EPI_QKV) {
+        epi_qkv64(e, m, n0, v);
+      } else if (wide) {
+        epi_row<64>(e, m, n0, v);
+      } else {
+        epi_row<32>(e, m, n0, v);
+      }
+    }
+  }
+  if (amax && m < M) atomicMax(e.o.keys + m, best);
+}
+
 template <int BN, int TC_STAGES>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
@@ -364,28 +392,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const int mt = t / num_n, nt = t - mt * num_n;
       const int m = mt * TC_BM + q * 32 + lane;
       const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
-      const bool amax = e.o.epi == EPI_ARGMAX;
-      const bool wide = e.o.epi == EPI_KNORM || e.o.epi == EPI_QKV;  // whole 64-column heads
-      unsigned long long best = 0ull;
-      for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += (wide ? 64 : 32)) {
-        float v[64];
-        tmem_ld32(base + c, v);
-        if (wide) tmem_ld32(base + c + 32, v + 32);
-        const int n0 = nt * BN + c;
-        if (m < M && n0 < N) {
-          if (amax) {
-            unsigned long long k = epi_argmax32(e, m, n0, v);
-            best = k > best ? k : best;
-          } else if (e.o.epi == EPI_QKV) {
-            epi_qkv64(e, m, n0, v);
-          } else if (wide) {
-            epi_row<64>(e, m, n0, v);
-          } else {
-            epi_row<32>(e, m, n0, v);
-          }
-        }
-      }
-      if (amax && m < M) atomicMax(e.o.keys + m, best);
+      epi_tile(e, M, N, m, base, half * (BN / 2), (half + 1) * (BN / 2), nt * BN);
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       mbar_arrive(&tempty[buf]);
     }
@@ -395,6 +402,159 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   if (warp == 1) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * BN));
+  }
+}
+
+// CTA-pair GEMM for tall matrices: a cluster of two CTAs computes 256 x 256
+// output tiles with tcgen05.mma.cta_group::2 M256 N256 K16.  Each CTA loads
+// its own 128 rows of A and its own 128 rows (output columns) of B into its
+// shared memory (64 KB per K block of 64, 3 stages); the leader CTA issues
+// the MMAs, which read both CTAs' tiles at the same offsets and leave each
+// CTA's 128 output rows in its own TMEM.  Per MMA a CTA's shared memory
+// supplies half the operand bytes of the single-CTA M128 N256 form.
+// Synchronisation: both CTAs' loads complete on the leader's `full`
+// barrier (the leader expects both CTAs' bytes); MMA completion is
+// signalled to both CTAs' `empty` and `tfull` barriers; both CTAs'
+// epilogue warps arrive on the leader's `tempty`.  Every wait is bounded.
+template <int STAGES>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
+                        const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl, int M,
+                        int N, int Kp, TcEpi e, int *err, int b_lo_zero) {
+  constexpr int HALF = 128, BN = 256;
+  constexpr int A_BYTES = HALF * TC_BK * 2, B_BYTES = HALF * TC_BK * 2;
+  constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
+  constexpr uint32_t IDESC = umma_idesc(2 * HALF, BN);
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t *full = (uint64_t *)(smem + STAGES * STAGE_BYTES);
+  uint64_t *empty = full + STAGES;
+  uint64_t *tfull = empty + STAGES;
+  uint64_t *tempty = tfull + 2;
+  uint32_t *tmem_slot = (uint32_t *)(tempty + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int num_m = (M + 2 * HALF - 1) / (2 * HALF), num_n = (N + BN - 1) / BN;
+  const int tiles = num_m * num_n, nkb = Kp / TC_BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 16);  // 8 epilogue warps in each CTA
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {  // two 256-column f32 accumulators in each CTA's TMEM
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(2 * BN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers initialised before any remote arrive
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *(volatile uint32_t *)tmem_slot;
+
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(TC_REG_PRODUCER));
+    if (warp == 0 && lane == 0) {
+      // ── TMA producer (both CTAs) ──
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&tmAh) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&tmAl) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&tmBh) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&tmBl) : "memory");
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = pair; t < tiles && ok; t += npairs) {
+        const int mt = t / num_n, nt = t - mt * num_n;
+        const int arow = mt * 2 * HALF + (int)rank * HALF, brow = nt * BN + (int)rank * HALF;
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!(ok = mbar_wait(&empty[stage], phase ^ 1, err))) break;
+          if (rank == 0) mbar_expect_tx(&full[stage], 2 * STAGE_BYTES);  // both CTAs' bytes
+          const uint32_t fb = pair_leader_addr(&full[stage]);
+          uint8_t *st = smem + stage * STAGE_BYTES;
+          tma_load_2d_pair(st, &tmAh, fb, kb * TC_BK, arow);
+          tma_load_2d_pair(st + A_BYTES, &tmAl, fb, kb * TC_BK, arow);
+          tma_load_2d_pair(st + 2 * A_BYTES, &tmBh, fb, kb * TC_BK, brow);
+          tma_load_2d_pair(st + 2 * A_BYTES + B_BYTES, &tmBl, fb, kb * TC_BK, brow);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // Drain: every issued stage consumed before the CTA exits.
+      for (int s = 0; s < STAGES && ok; ++s) {
+        ok = mbar_wait(&empty[stage], phase ^ 1, err);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    } else if (warp == 1 && lane == 0 && rank == 0) {
+      // ── MMA issuer (leader CTA) ──
+      int stage = 0;
+      uint32_t phase = 0;
+      int i = 0;
+      bool ok = true;
+      for (int t = pair; t < tiles && ok; t += npairs, ++i) {
+        const int buf = i & 1;
+        if (!(ok = mbar_wait(&tempty[buf], ((i >> 1) & 1) ^ 1, err))) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t d = tmem + (uint32_t)(buf * BN);
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!(ok = mbar_wait(&full[stage], phase, err))) break;
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          uint8_t *st = smem + stage * STAGE_BYTES;
+          const uint64_t ah = umma_desc(st), al = umma_desc(st + A_BYTES);
+          const uint64_t bh = umma_desc(st + 2 * A_BYTES), bl = umma_desc(st + 2 * A_BYTES + B_BYTES);
+#pragma unroll
+          for (int k = 0; k < TC_BK / 16; ++k) {
+            const uint64_t adv = (uint64_t)((k * 32) >> 4);  // 16 bf16 = 32 bytes along K
+            umma_bf16_pair(d, ah + adv, bh + adv, IDESC, (kb | k) ? 1u : 0u);
+            if (!b_lo_zero) umma_bf16_pair(d, ah + adv, bl + adv, IDESC, 1u);
+            umma_bf16_pair(d, al + adv, bh + adv, IDESC, 1u);
+          }
+          umma_commit_pair(&empty[stage]);  // both CTAs' stage is free once these MMAs complete
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (ok) umma_commit_pair(&tfull[buf]);
+      }
+    }
+  } else {
+    // ── epilogue (both CTAs): warpgroup `half` takes 128 of the 256 columns ──
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(TC_REG_EPILOGUE));
+    const int q = warp & 3, half = (warp - 4) >> 2;
+    int i = 0;
+    for (int t = pair; t < tiles; t += npairs, ++i) {
+      const int buf = i & 1;
+      if (!warp_wait(&tfull[buf], (i >> 1) & 1, err)) break;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const int mt = t / num_n, nt = t - mt * num_n;
+      const int m = mt * 2 * HALF + (int)rank * HALF + q * 32 + lane;
+      const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
+      epi_tile(e, M, N, m, base, half * (BN / 2), (half + 1) * (BN / 2), nt * BN);
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(&tempty[buf], 0);  // the leader's barrier
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  cluster_sync();  // no remote arrive or MMA targets a CTA that has left
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * BN));
   }
 }
 
@@ -467,6 +627,9 @@ constexpr size_t tc_smem_bytes(int BN, int stages) {
 }
 static_assert(tc_smem_bytes(128, 3) <= 232448 && tc_smem_bytes(256, 2) <= 232448,
               "exceeds the 227 KB of dynamic shared memory per block");
+constexpr int TC_PAIR_STAGES = 3;
+constexpr size_t tc_smem_pair_bytes() { return 1024 + (size_t)TC_PAIR_STAGES * (4 * 128 * TC_BK * 2) + 256; }
+static_assert(tc_smem_pair_bytes() <= 232448, "exceeds the 227 KB of dynamic shared memory per block");
 
 }  // namespace
 
@@ -543,10 +706,35 @@ cudaError_t tc_matmul(const TcPlanes &A, int M, const TcPlanes &B, int N, const 
     regs[1] = fa.numRegs;
   }
   if (regs[0] != TC_REG_LAUNCH || regs[1] != TC_REG_LAUNCH) return cudaErrorInvalidKernelImage;
+  static int pair_regs = -1;
+  if (pair_regs < 0) {
+    cudaFuncAttributes fa;
+    cudaError_t ce = cudaFuncGetAttributes(&fa, tc_gemm_pair_kernel<TC_PAIR_STAGES>);
+    if (ce != cudaSuccess) return ce;
+    pair_regs = fa.numRegs;
+  }
   const int sms = tc_sm_count(), num_m = (M + TC_BM - 1) / TC_BM;
   const auto *ah = reinterpret_cast<const CUtensorMap *>(A.hi), *al = reinterpret_cast<const CUtensorMap *>(A.lo);
   const auto *bh = reinterpret_cast<const CUtensorMap *>(B.hi), *bl = reinterpret_cast<const CUtensorMap *>(B.lo);
   const int tiles256 = num_m * ((N + 255) / 256);
+  const int tiles_pair = ((M + 255) / 256) * ((N + 255) / 256);
+  if (tiles_pair >= sms && pair_regs == TC_REG_LAUNCH) {  // at least two 256 x 256 tiles per CTA pair
+    const int npairs = tiles_pair < sms / 2 ? tiles_pair : sms / 2;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * npairs);
+    cfg.blockDim = dim3(TC_THREADS);
+    cfg.dynamicSmemBytes = tc_smem_pair_bytes();
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<TC_PAIR_STAGES>, *ah, *al, *bh, *bl, M, N, A.Kp, e, err,
+                              b_lo_zero ? 1 : 0);
+  }
   if (tiles256 >= 2 * sms) {
     const int grid = sms;
     tc_gemm_kernel<256, 2><<<grid, TC_THREADS, tc_smem_bytes(256, 2), st>>>(*ah, *al, *bh, *bl, M, N, A.Kp, e, err,
@@ -566,6 +754,9 @@ cudaError_t init_tc_kernels() {
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(tc_gemm_kernel<256, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)tc_smem_bytes(256, 2));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(tc_gemm_pair_kernel<TC_PAIR_STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)tc_smem_pair_bytes());
   return e;
 }
 

@@ -70,6 +70,16 @@ NeedleBatch *needle_batch_prepare(NeedleHandle *handle, const uint32_t *prompt_i
 int needle_batch_run(NeedleBatch *batch);
 int needle_batch_sync(NeedleBatch *batch);
 int needle_batch_results(NeedleBatch *batch, uint32_t *out_ids, uint32_t *out_lens);
+/* Step-wise decoding for callers that build each step's vocabulary mask from
+ * the tokens so far (the loop of engine.rs:286-322 with their own grammar):
+ * needle_batch_begin runs the prefill; needle_batch_set_step_mask replaces
+ * the mask rows [n_req][ceil(V/64)] of one step (the batch must have been
+ * prepared with mask_bits); needle_batch_step runs the next decode step and
+ * returns its token per request with lens / done (any may be NULL; the token
+ * of a request that is done, at EOS or earlier, is unspecified). */
+int needle_batch_begin(NeedleBatch *batch);
+int needle_batch_set_step_mask(NeedleBatch *batch, uint32_t step, const uint64_t *rows);
+int needle_batch_step(NeedleBatch *batch, uint32_t *tokens, uint32_t *lens, uint8_t *done);
 /* The cudaStream_t the batch runs on (as void *), for the caller's events. */
 void *needle_batch_stream(NeedleBatch *batch);
 /* Kernels the last needle_batch_run launched. */
@@ -105,6 +115,58 @@ int needle_debug_forward(NeedleHandle *handle, const uint32_t *enc_ids, size_t n
 int needle_run_batch_ids_logits(NeedleHandle *handle, const uint32_t *prompt_ids, const uint64_t *prompt_offsets,
                                 size_t n_req, uint32_t max_new, const uint64_t *mask_bits, uint32_t flags,
                                 uint32_t *out_ids, uint32_t *out_lens, float *logits);
+
+/* ── text front end (needle_run's tokenizer, tool JSON, constrained decoding) ─ */
+
+/* NeedleEngine::run_batch (crates/needle-infer/src/engine.rs:142-144): run n
+ * (query, tools_json) requests, each as needle_run would, decoded together
+ * on the GPU with one constrained-decoding state per request.  out_texts[i]
+ * receives a string to free with needle_free_str.  0 on success, -1 on
+ * failure (no strings left allocated). */
+int needle_run_batch(NeedleHandle *handle, const char *const *queries, const char *const *tools_json, size_t n,
+                     char **out_texts);
+
+/* The SentencePiece vocabulary of crates/needle-infer/src/tokenizer.rs:31-246
+ * (one "piece\tscore" per line, line index = id; BPE by score, greedy
+ * longest match for a file without scores). */
+typedef struct NeedleVocab NeedleVocab;
+/* Parse vocabulary text; NULL (error set) if it is not UTF-8.  Free with
+ * needle_vocab_free. */
+NeedleVocab *needle_vocab_parse(const char *text, size_t len);
+/* The vocabulary a handle loaded (owned by the handle). */
+const NeedleVocab *needle_handle_vocab(NeedleHandle *handle);
+size_t needle_vocab_size(const NeedleVocab *vocab);
+/* Vocabulary::encode: token ids of text (trimmed, SentencePiece-normalised);
+ * writes min(count, cap) ids and returns the count; (size_t)-1 if text is not
+ * UTF-8. */
+size_t needle_vocab_encode(const NeedleVocab *vocab, const char *text, uint32_t *out, size_t cap);
+/* Vocabulary::decode_ids (free the result with needle_free_str). */
+char *needle_vocab_decode(const NeedleVocab *vocab, const uint32_t *ids, size_t n);
+void needle_vocab_free(NeedleVocab *vocab);
+/* to_snake_case of tokenizer.rs:248-292 (free with needle_free_str). */
+char *needle_snake_case(const char *name);
+/* The tools JSON as the encoder sees it: tool names in snake_case, whitespace
+ * outside strings removed (engine.rs:233-239, 354-471). */
+char *needle_tools_encoder_text(const char *tools_json);
+/* Output with the tools' snake_case names replaced by the original names
+ * (restore_tool_names, engine.rs:473-546). */
+char *needle_tools_restore_names(const char *tools_json, const char *output);
+
+/* ConstrainedDecoder (crates/needle-infer/src/constrained.rs:300-375): JSON
+ * state machine + name / argument-key tries over a tools JSON. */
+typedef struct NeedleConstraint NeedleConstraint;
+NeedleConstraint *needle_constraint_new(const char *tools_json, const NeedleVocab *vocab);
+/* Advance past an emitted token / raw output bytes. */
+int needle_constraint_update(NeedleConstraint *c, uint32_t token);
+int needle_constraint_feed(NeedleConstraint *c, const char *bytes, size_t len);
+/* Allowed-token bitmap for the next step into bits[ceil(vocab_size/64)]
+ * (bit set = allowed, the mask_bits format of needle_run_batch_ids): returns
+ * 1 when the step is constrained, 0 when every token is allowed (bits all
+ * set), -1 on bad arguments. */
+int needle_constraint_mask(NeedleConstraint *c, size_t vocab_size, uint64_t *bits);
+/* 0 free, 1 inside a tool name, 2 inside an argument key. */
+int needle_constraint_state(const NeedleConstraint *c);
+void needle_constraint_free(NeedleConstraint *c);
 
 /* ── INT4 kernels on device pointers (reference layout, quant.rs:45-58) ──── */
 /* w_data: [(G*gs/2)][N] bytes, low nibble = row 2p, high = row 2p+1;

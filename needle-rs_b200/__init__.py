@@ -72,6 +72,9 @@ def lib():
             "needle_batch_time_kernel": (I, [P, I]),
             "needle_batch_kernel_timing": (I, [P, P, P, P, P]),
             "needle_batch_free": (None, [P]),
+            "needle_batch_begin": (I, [P]),
+            "needle_batch_set_step_mask": (I, [P, U32, P]),
+            "needle_batch_step": (I, [P, P, P, P]),
             "needle_shard_requests": (I, [P, S, I, P]),
             "needle_debug_forward": (I, [P, P, S, P, S, P, P]),
             "needle_int4_matmul": (I, [P, S, S, P, P, S, S, P, P]),
@@ -82,6 +85,22 @@ def lib():
             "needle_int4_plan_free": (None, [P]),
             "needle_int4_quantize": (I, [P, S, S, P, P, P]),
             "needle_int4_dequantize": (I, [P, P, S, S, S, P, P]),
+            "needle_run_batch": (I, [P, P, P, S, P]),
+            "needle_vocab_parse": (P, [C.c_char_p, S]),
+            "needle_handle_vocab": (P, [P]),
+            "needle_vocab_size": (S, [P]),
+            "needle_vocab_encode": (S, [P, C.c_char_p, P, S]),
+            "needle_vocab_decode": (P, [P, P, S]),
+            "needle_vocab_free": (None, [P]),
+            "needle_snake_case": (P, [C.c_char_p]),
+            "needle_tools_encoder_text": (P, [C.c_char_p]),
+            "needle_tools_restore_names": (P, [C.c_char_p, C.c_char_p]),
+            "needle_constraint_new": (P, [C.c_char_p, P]),
+            "needle_constraint_update": (I, [P, U32]),
+            "needle_constraint_feed": (I, [P, C.c_char_p, S]),
+            "needle_constraint_mask": (I, [P, S, P]),
+            "needle_constraint_state": (I, [P]),
+            "needle_constraint_free": (None, [P]),
             "needle_ffn_forward": (I, [P, S, S, S, P, P, P, P, P, P, I, P, P]),
             "needle_ffn_forward_noalloc": (I, [P, S, S, S, P, P, P, P, P, P, I, P, P]),
         }
@@ -177,6 +196,25 @@ class NeedleEngine:
         lib().needle_free_str(r)
         return s
 
+    def run_batch(self, queries, tools_jsons):
+        """NeedleEngine::run_batch: one output string per (query, tools) pair."""
+        n = len(queries)
+        if len(tools_jsons) != n:
+            raise ValueError("queries and tools_jsons differ in length")
+        qa = (C.c_char_p * max(n, 1))(*[q.encode() for q in queries])
+        ta = (C.c_char_p * max(n, 1))(*[t.encode() for t in tools_jsons])
+        out = (C.c_void_p * max(n, 1))()
+        _check(lib().needle_run_batch(self._h, qa, ta, n, out))
+        res = []
+        for i in range(n):
+            res.append(C.string_at(out[i]).decode())
+            lib().needle_free_str(out[i])
+        return res
+
+    def vocab(self):
+        """The handle's vocabulary (valid while the engine is open)."""
+        return Vocab(_handle=lib().needle_handle_vocab(self._h), _owner=self)
+
     def run_stream(self, query, tools_json, on_token):
         CB = C.CFUNCTYPE(None, C.c_uint32, C.c_char_p, C.c_void_p)
         cb = CB(lambda tid, piece, ud: on_token(int(tid), piece.decode()))
@@ -242,6 +280,22 @@ class Batch:
 
     def sync(self):
         _check(lib().needle_batch_sync(self._b))
+
+    def begin(self):
+        """Prefill; decode steps then run one at a time with step()."""
+        _check(lib().needle_batch_begin(self._b))
+
+    def set_step_mask(self, step, rows):
+        r = np.ascontiguousarray(rows, np.uint64)
+        _check(lib().needle_batch_set_step_mask(self._b, int(step), _p(r)))
+
+    def step(self):
+        """-> (tokens [n], lens [n], done [n]) of the decode step just run."""
+        t = np.zeros(self.n, np.uint32)
+        ln = np.zeros(self.n, np.uint32)
+        d = np.zeros(self.n, np.uint8)
+        _check(lib().needle_batch_step(self._b, _p(t), _p(ln), _p(d)))
+        return t, ln, d
 
     def results(self):
         out = np.zeros((self.n, self.max_new), np.uint32)
@@ -350,3 +404,109 @@ def ffn_forward_noalloc(x_ptr, T, d, ff, g, u, dn, act, out_ptr, stream=None):
     array (no allocation; T * d_ff <= 1,048,576; overlapping calls race)."""
     _check(lib().needle_ffn_forward_noalloc(x_ptr, T, d, ff, g[0], g[1], u[0], u[1], dn[0], dn[1], act, out_ptr,
                                             stream))
+
+
+# ── text front end (tokenizer, tool JSON, constrained decoding) ─────────────
+
+def _take_str(r):
+    if not r:
+        raise NeedleError(last_error() or "needle call failed")
+    s = C.string_at(r).decode()
+    lib().needle_free_str(r)
+    return s
+
+
+class Vocab:
+    """SentencePiece vocabulary (Vocabulary of tokenizer.rs)."""
+
+    def __init__(self, text=None, _handle=None, _owner=None):
+        self._own = _handle is None
+        self._owner = _owner
+        if _handle is None:
+            b = text.encode() if isinstance(text, str) else bytes(text)
+            _handle = lib().needle_vocab_parse(b, len(b))
+            if not _handle:
+                raise NeedleError(last_error() or "needle_vocab_parse failed")
+        self._h = _handle
+
+    def __len__(self):
+        return lib().needle_vocab_size(self._h)
+
+    def encode(self, text):
+        b = text.encode()
+        n = lib().needle_vocab_encode(self._h, b, None, 0)
+        if n == C.c_size_t(-1).value:
+            raise NeedleError("invalid text")
+        out = np.zeros(max(n, 1), np.uint32)
+        lib().needle_vocab_encode(self._h, b, _p(out), n)
+        return out[:n].tolist()
+
+    def decode(self, ids):
+        a = np.ascontiguousarray(ids, np.uint32)
+        return _take_str(lib().needle_vocab_decode(self._h, _p(a) if a.size else None, a.size))
+
+    def close(self):
+        if self._own and getattr(self, "_h", None):
+            lib().needle_vocab_free(self._h)
+        self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def snake_case(name):
+    return _take_str(lib().needle_snake_case(name.encode()))
+
+
+def tools_encoder_text(tools_json):
+    """The tools JSON as the encoder sees it (snake_case names, compact)."""
+    return _take_str(lib().needle_tools_encoder_text(tools_json.encode()))
+
+
+def restore_tool_names(tools_json, output):
+    return _take_str(lib().needle_tools_restore_names(tools_json.encode(), output.encode()))
+
+
+class Constraint:
+    """ConstrainedDecoder of constrained.rs over a tools JSON."""
+
+    FREE, IN_NAME, IN_ARG_KEY = 0, 1, 2
+
+    def __init__(self, tools_json, vocab):
+        self._vocab = vocab
+        self._h = lib().needle_constraint_new(tools_json.encode(), vocab._h)
+        if not self._h:
+            raise NeedleError(last_error() or "needle_constraint_new failed")
+
+    def update(self, token):
+        _check(lib().needle_constraint_update(self._h, int(token)))
+
+    def feed(self, data):
+        b = data.encode() if isinstance(data, str) else bytes(data)
+        _check(lib().needle_constraint_feed(self._h, b, len(b)))
+
+    def mask(self, vocab_size):
+        """-> (uint64 bitmap [ceil(V/64)], constrained?)"""
+        bits = np.zeros((vocab_size + 63) // 64, np.uint64)
+        rc = lib().needle_constraint_mask(self._h, vocab_size, _p(bits))
+        if rc < 0:
+            raise NeedleError("needle_constraint_mask failed")
+        return bits, rc == 1
+
+    @property
+    def state(self):
+        return lib().needle_constraint_state(self._h)
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().needle_constraint_free(self._h)
+        self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

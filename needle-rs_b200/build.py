@@ -16,7 +16,7 @@ NVCC = os.environ.get("NVCC", "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 CU = ["int4_matmul.cu", "attention.cu", "head.cu", "tc_gemm.cu", "tc_attn.cu", "ffn_noalloc.cu"]
-CPP = ["safetensors.cpp", "engine.cpp", "capi.cpp"]
+CPP = ["safetensors.cpp", "frontend.cpp", "engine.cpp", "capi.cpp"]
 
 
 def sources():

@@ -17,12 +17,23 @@
 #include "../../include/needle_b200.h"
 #include "capi_internal.h"
 #include "engine.h"
+#include "frontend.h"
 
 using namespace ndl;
+
+struct NeedleVocab {
+  text::Vocab v;
+};
+
+struct NeedleConstraint {
+  std::unique_ptr<text::ConstrainedDecoder> d;
+  std::vector<uint64_t> bits;
+};
 
 struct NeedleHandle {
   std::unique_ptr<DevModel> model;
   std::string vocab_text;
+  NeedleVocab vocab;  // parsed once at load; read-only afterwards
 };
 
 struct NeedleBatch {
@@ -31,6 +42,7 @@ struct NeedleBatch {
   BatchSpec spec;
   std::vector<uint64_t> offsets;
   int timed_cls = 0;
+  int next_step = -1;  // step-wise decoding: next step to run (-1 before needle_batch_begin)
 };
 
 namespace {
@@ -84,6 +96,7 @@ NeedleHandle *load_impl(std::vector<uint8_t> weights, const std::string &vocab_t
   auto *h = new NeedleHandle();
   h->model = std::move(model);
   h->vocab_text = vocab_text;
+  h->vocab.v.parse(vocab_text);
   return h;
 }
 
@@ -173,18 +186,287 @@ NeedleHandle *needle_load_bytes_on_device(const uint8_t *wd, size_t wl, const ui
   return load_bytes(wd, wl, vd, vl, device);
 }
 
+// NeedleEngine::run_impl (crates/needle-infer/src/engine.rs:226-322) on the
+// GPU engine, for n requests at once (run_batch, engine.rs:142-144): per
+// request the tools JSON is normalised and compacted, the encoder input is
+// query ++ [TOOLS] ++ tools (truncated to max_enc_len as the reference
+// truncates), and greedy decoding runs from EOS one step at a time so that
+// each request's constrained-decoding mask for step s+1 follows its token of
+// step s; a request stops at EOS (not emitted); the output has the
+// <tool_call> prefix stripped and the original tool names restored.  cb (n =
+// 1 only) fires per emitted token in order.
+static bool run_text_batch(NeedleHandle *h, const std::vector<std::string> &queries,
+                           const std::vector<std::string> &tools, NeedleStreamCallback cb, void *ud,
+                           std::vector<std::string> &outs) {
+  const Config &c = h->model->cfg;
+  const size_t n = queries.size();
+  outs.assign(n, std::string());
+  std::vector<std::vector<text::ToolDef>> defs(n);
+  std::vector<uint32_t> ids;
+  std::vector<uint64_t> off(1, 0);
+  std::vector<size_t> slot;  // request index of each batch row
+  for (size_t r = 0; r < n; ++r) {
+    defs[r] = text::parse_tools_json(tools[r]);
+    const std::string compact = text::compact_json(text::normalize_tools_json(tools[r], defs[r]));
+    const std::vector<uint32_t> q = h->vocab.v.encode(queries[r]), t = h->vocab.v.encode(compact);
+    const size_t max_enc = (size_t)c.max_enc_len;
+    if ((q.empty() && t.empty()) || max_enc == 0) continue;  // empty result, no decoding
+    const size_t q_len = std::min(q.size(), max_enc >= 2 ? max_enc - 2 : 0);
+    const size_t rem = max_enc >= q_len + 1 ? max_enc - (q_len + 1) : 0;
+    const size_t t_len = std::min(t.size(), rem);
+    ids.insert(ids.end(), q.begin(), q.begin() + q_len);
+    ids.push_back(text::kToolsId);
+    ids.insert(ids.end(), t.begin(), t.begin() + t_len);
+    off.push_back(ids.size());
+    slot.push_back(r);
+  }
+  for (uint32_t id : ids)
+    if (id >= (uint32_t)c.vocab_size) {
+      set_err("the vocabulary has token ids beyond the model's vocab_size");
+      return false;
+    }
+  const int B = (int)slot.size(), steps = c.max_dec_len;
+  std::vector<std::vector<uint32_t>> gen(B);
+  if (B > 0 && steps > 0) {
+    const size_t W = ((size_t)c.vocab_size + 63) / 64;
+    std::vector<uint64_t> init((size_t)B * steps * W, ~0ull);  // every step starts unconstrained
+    BatchSpec s;
+    s.ids = ids.data();
+    s.offsets = off.data();
+    s.n_req = B;
+    s.max_new = steps;
+    s.mask = init.data();
+    s.flags = BATCH_STOP_ON_EOS;
+    Batch b(h->model.get());
+    std::string err;
+    std::vector<text::ConstrainedDecoder> dec;
+    dec.reserve(B);
+    for (int i = 0; i < B; ++i) dec.emplace_back(defs[slot[i]], h->vocab.v);
+    if (!b.prepare(s, err) || !b.begin(err)) {
+      set_err(err);
+      return false;
+    }
+    std::vector<uint64_t> rows((size_t)B * W), bits;
+    std::vector<uint32_t> tok(B), lens(B);
+    std::vector<uint8_t> done(B), finished(B, 0);
+    int active = B;
+    for (int step = 0; step < steps && active > 0; ++step) {
+      bool any = false;
+      for (int i = 0; i < B; ++i) {
+        uint64_t *row = rows.data() + (size_t)i * W;
+        if (!finished[i] && dec[i].mask((size_t)c.vocab_size, bits)) {
+          std::copy(bits.begin(), bits.end(), row);
+          any = true;
+        } else {
+          std::fill(row, row + W, ~0ull);
+        }
+      }
+      if (any && !b.set_mask_step(step, rows.data(), err)) {
+        set_err(err);
+        return false;
+      }
+      if (!b.step(err) || !b.peek_step(step, tok.data(), lens.data(), done.data(), err)) {
+        set_err(err);
+        return false;
+      }
+      for (int i = 0; i < B; ++i) {
+        if (finished[i]) continue;
+        if (done[i] || lens[i] <= (uint32_t)step) {  // EOS
+          finished[i] = 1;
+          --active;
+          continue;
+        }
+        if (cb) {
+          const std::string piece = h->vocab.v.piece_text(tok[i]);
+          if (piece.find('\0') == std::string::npos) cb(tok[i], piece.c_str(), ud);
+        }
+        gen[i].push_back(tok[i]);
+        dec[i].update(tok[i]);
+      }
+    }
+  }
+  const std::string tc = h->vocab.v.size() > text::kToolCallId ? h->vocab.v.piece_text(text::kToolCallId) : std::string();
+  for (int i = 0; i < B; ++i) {
+    std::string raw = h->vocab.v.decode_ids(gen[i]);
+    if (!tc.empty() && raw.compare(0, tc.size(), tc) == 0) raw.erase(0, tc.size());
+    outs[slot[i]] = text::restore_tool_names(raw, defs[slot[i]]);
+  }
+  return true;
+}
+
+static char *dup_text(const std::string &out) {
+  if (out.find('\0') != std::string::npos) {
+    set_err("output contained null byte");
+    return nullptr;
+  }
+  char *r = (char *)std::malloc(out.size() + 1);
+  if (!r) {
+    set_err("out of host memory");
+    return nullptr;
+  }
+  std::memcpy(r, out.c_str(), out.size() + 1);
+  return r;
+}
+
 static char *run_text(NeedleHandle *h, const char *query, const char *tools_json, NeedleStreamCallback cb,
                       void *ud) {
-  (void)cb;
-  (void)ud;
   if (!h) return nullptr;
   if (!query || !tools_json) return nullptr;
   if (!valid_utf8((const uint8_t *)query, std::strlen(query)) ||
       !valid_utf8((const uint8_t *)tools_json, std::strlen(tools_json)))
     return nullptr;
   clear_err();
-  set_err("needle_run: the text front end is not part of this build; use needle_run_batch_ids");
-  return nullptr;
+  std::vector<std::string> outs;
+  if (!run_text_batch(h, {query}, {tools_json}, cb, ud, outs)) return nullptr;
+  return dup_text(outs[0]);
+}
+
+NeedleVocab *needle_vocab_parse(const char *text, size_t len) {
+  clear_err();
+  if (!text && len) {
+    set_err("null vocabulary text");
+    return nullptr;
+  }
+  std::string s(text ? text : "", len);
+  if (!text::utf8_valid(s)) {
+    set_err("vocab is not valid UTF-8");
+    return nullptr;
+  }
+  auto *v = new NeedleVocab();
+  v->v.parse(s);
+  return v;
+}
+
+const NeedleVocab *needle_handle_vocab(NeedleHandle *h) { return h ? &h->vocab : nullptr; }
+
+size_t needle_vocab_size(const NeedleVocab *v) { return v ? v->v.size() : 0; }
+
+size_t needle_vocab_encode(const NeedleVocab *v, const char *text, uint32_t *out, size_t cap) {
+  if (!v || !text || !text::utf8_valid(text)) return (size_t)-1;
+  const std::vector<uint32_t> ids = v->v.encode(text);
+  if (out)
+    for (size_t i = 0; i < ids.size() && i < cap; ++i) out[i] = ids[i];
+  return ids.size();
+}
+
+char *needle_vocab_decode(const NeedleVocab *v, const uint32_t *ids, size_t n) {
+  clear_err();
+  if (!v || (!ids && n)) {
+    set_err("invalid decode arguments");
+    return nullptr;
+  }
+  return dup_text(v->v.decode_ids(std::vector<uint32_t>(ids, ids + n)));
+}
+
+void needle_vocab_free(NeedleVocab *v) { delete v; }
+
+char *needle_snake_case(const char *name) {
+  clear_err();
+  if (!name || !text::utf8_valid(name)) {
+    set_err("null or invalid UTF-8 name");
+    return nullptr;
+  }
+  return dup_text(text::to_snake_case(name));
+}
+
+char *needle_tools_encoder_text(const char *tools_json) {
+  clear_err();
+  if (!tools_json || !text::utf8_valid(tools_json)) {
+    set_err("null or invalid UTF-8 tools JSON");
+    return nullptr;
+  }
+  const auto defs = text::parse_tools_json(tools_json);
+  return dup_text(text::compact_json(text::normalize_tools_json(tools_json, defs)));
+}
+
+char *needle_tools_restore_names(const char *tools_json, const char *output) {
+  clear_err();
+  if (!tools_json || !output || !text::utf8_valid(tools_json) || !text::utf8_valid(output)) {
+    set_err("null or invalid UTF-8 argument");
+    return nullptr;
+  }
+  return dup_text(text::restore_tool_names(output, text::parse_tools_json(tools_json)));
+}
+
+NeedleConstraint *needle_constraint_new(const char *tools_json, const NeedleVocab *v) {
+  clear_err();
+  if (!tools_json || !v || !text::utf8_valid(tools_json)) {
+    set_err("null vocabulary or null / invalid UTF-8 tools JSON");
+    return nullptr;
+  }
+  auto *c = new NeedleConstraint();
+  c->d = std::make_unique<text::ConstrainedDecoder>(text::parse_tools_json(tools_json), v->v);
+  return c;
+}
+
+int needle_constraint_update(NeedleConstraint *c, uint32_t token) {
+  if (!c) return -1;
+  c->d->update(token);
+  return 0;
+}
+
+int needle_constraint_feed(NeedleConstraint *c, const char *bytes, size_t len) {
+  if (!c || (!bytes && len)) return -1;
+  c->d->feed_bytes(std::string(bytes ? bytes : "", len));
+  return 0;
+}
+
+int needle_constraint_mask(NeedleConstraint *c, size_t vocab_size, uint64_t *bits) {
+  if (!c || !bits || vocab_size == 0) return -1;
+  const size_t W = (vocab_size + 63) / 64;
+  if (c->d->mask(vocab_size, c->bits)) {
+    std::copy(c->bits.begin(), c->bits.begin() + W, bits);
+    return 1;
+  }
+  std::fill(bits, bits + W, ~0ull);
+  return 0;
+}
+
+int needle_constraint_state(const NeedleConstraint *c) {
+  if (!c) return -1;
+  switch (c->d->state_machine().state) {
+    case text::JsonState::InName:
+      return 1;
+    case text::JsonState::InArgKey:
+      return 2;
+    default:
+      return 0;
+  }
+}
+
+void needle_constraint_free(NeedleConstraint *c) { delete c; }
+
+int needle_run_batch(NeedleHandle *h, const char *const *queries, const char *const *tools_json, size_t n,
+                     char **out_texts) {
+  if (!h) return -1;
+  clear_err();
+  if (!queries || !tools_json || !out_texts || n > (size_t)INT32_MAX) {
+    set_err("invalid batch arguments");
+    return -1;
+  }
+  std::vector<std::string> q(n), t(n);
+  for (size_t i = 0; i < n; ++i) {
+    out_texts[i] = nullptr;
+    if (!queries[i] || !tools_json[i] || !valid_utf8((const uint8_t *)queries[i], std::strlen(queries[i])) ||
+        !valid_utf8((const uint8_t *)tools_json[i], std::strlen(tools_json[i]))) {
+      set_err("request " + std::to_string(i) + ": null or invalid UTF-8 query or tools");
+      return -1;
+    }
+    q[i] = queries[i];
+    t[i] = tools_json[i];
+  }
+  std::vector<std::string> outs;
+  if (!run_text_batch(h, q, t, nullptr, nullptr, outs)) return -1;
+  for (size_t i = 0; i < n; ++i) {
+    if (!(out_texts[i] = dup_text(outs[i]))) {
+      for (size_t k = 0; k < i; ++k) {
+        std::free(out_texts[k]);
+        out_texts[k] = nullptr;
+      }
+      return -1;
+    }
+  }
+  return 0;
 }
 
 char *needle_run(NeedleHandle *h, const char *query, const char *tools_json) {
@@ -299,6 +581,51 @@ int needle_batch_results(NeedleBatch *nb, uint32_t *out_ids, uint32_t *out_lens)
     set_err(err);
     return -1;
   }
+  return 0;
+}
+
+int needle_batch_begin(NeedleBatch *nb) {
+  if (!nb) return -1;
+  clear_err();
+  std::string err;
+  nb->batch->set_timed_class(nb->timed_cls);
+  if (!nb->batch->begin(err)) {
+    set_err(err);
+    return -1;
+  }
+  nb->next_step = 0;
+  return 0;
+}
+
+int needle_batch_set_step_mask(NeedleBatch *nb, uint32_t step, const uint64_t *rows) {
+  if (!nb || !rows) return -1;
+  clear_err();
+  std::string err;
+  if (!nb->batch->set_mask_step((int)step, rows, err)) {
+    set_err(err);
+    return -1;
+  }
+  return 0;
+}
+
+int needle_batch_step(NeedleBatch *nb, uint32_t *tokens, uint32_t *lens, uint8_t *done) {
+  if (!nb) return -1;
+  clear_err();
+  if (nb->next_step < 0) {
+    set_err("needle_batch_begin must run first");
+    return -1;
+  }
+  std::string err;
+  const int step = nb->next_step;
+  std::vector<uint32_t> tk(tokens ? 0 : nb->spec.n_req), ln(lens ? 0 : nb->spec.n_req);
+  std::vector<uint8_t> dn(done ? 0 : nb->spec.n_req);
+  if (!nb->batch->step(err) ||
+      !nb->batch->peek_step(step, tokens ? tokens : tk.data(), lens ? lens : ln.data(), done ? done : dn.data(),
+                            err)) {
+    set_err(err);
+    return -1;
+  }
+  ++nb->next_step;
   return 0;
 }
 

@@ -1058,6 +1058,43 @@ bool Batch::peek(uint32_t *lens, uint8_t *done, uint32_t *ids, std::string &err)
   return true;
 }
 
+bool Batch::set_mask_row(int req, int step, const uint64_t *bits, std::string &err) {
+  if (!mask_ || req < 0 || req >= spec_.n_req || step < 0 || step >= spec_.max_new) {
+    err = "set_mask_row: no such mask row";
+    return false;
+  }
+  uint64_t *dst = mask_ + ((size_t)req * spec_.max_new + step) * W_;
+  NDL_CK(cudaMemcpyAsync(dst, bits, (size_t)W_ * sizeof(uint64_t), cudaMemcpyHostToDevice, st_));
+  return true;
+}
+
+bool Batch::set_mask_step(int step, const uint64_t *rows, std::string &err) {
+  if (!mask_ || step < 0 || step >= spec_.max_new) {
+    err = "set_mask_step: no such mask step";
+    return false;
+  }
+  const size_t row = (size_t)W_ * sizeof(uint64_t);
+  NDL_CK(cudaMemcpy2DAsync(mask_ + (size_t)step * W_, (size_t)spec_.max_new * row, rows, row, row,
+                           (size_t)spec_.n_req, cudaMemcpyHostToDevice, st_));
+  return true;
+}
+
+bool Batch::peek_step(int step, uint32_t *tokens, uint32_t *lens, uint8_t *done, std::string &err) {
+  if (step < 0 || step >= spec_.max_new) {
+    err = "peek_step: no such step";
+    return false;
+  }
+  cudaStream_t st = st_;
+  const int B = spec_.n_req;
+  if (tokens)
+    NDL_CK(cudaMemcpy2DAsync(tokens, sizeof(uint32_t), out_ids_ + step, (size_t)spec_.max_new * sizeof(uint32_t),
+                             sizeof(uint32_t), (size_t)B, cudaMemcpyDeviceToHost, st));
+  if (lens) NDL_CK(cudaMemcpyAsync(lens, lens_, (size_t)B * 4, cudaMemcpyDeviceToHost, st));
+  if (done) NDL_CK(cudaMemcpyAsync(done, done_, (size_t)B, cudaMemcpyDeviceToHost, st));
+  NDL_CK(cudaStreamSynchronize(st));
+  return true;
+}
+
 bool Batch::run(std::string &err) {
   if (!begin(err)) return false;
   const int steps = spec_.max_new;

@@ -141,6 +141,15 @@ class Batch {
   bool begin(std::string &err);
   bool step(std::string &err);
   bool peek(uint32_t *lens, uint8_t *done, uint32_t *ids, std::string &err);
+  // Overwrite the vocabulary bitmap a request uses at one decode step
+  // (ceil(V/64) words, host memory), ordered before later steps on the
+  // batch's stream.  The batch must have been prepared with a mask.
+  bool set_mask_row(int req, int step, const uint64_t *bits, std::string &err);
+  // The same for every request at once: rows [n_req][ceil(V/64)] (one
+  // strided copy).
+  bool set_mask_step(int step, const uint64_t *rows, std::string &err);
+  // Synchronise and read one step's tokens [n_req] plus lens / done.
+  bool peek_step(int step, uint32_t *tokens, uint32_t *lens, uint8_t *done, std::string &err);
   bool download(uint32_t *out_ids, uint32_t *out_lens, float *logits, float *enc_out, std::string &err);
   cudaStream_t stream() const { return st_; }
   // Number of kernels one run() launches (reported by the benchmark).

@@ -159,3 +159,52 @@ def int4_case(M, N, K, seed=0):
     x = rng.standard_normal((M, K)).astype(np.float32)
     packed, scales = random_int4(rng, K, N)
     return x, packed, scales
+
+
+SPECIAL_PIECES = ["<pad>", "</s>", "<s>", "<unk>", "<tool_call>", "<tools>"]
+
+
+def random_vocab(size=8192, seed=0):
+    """A SentencePiece-style vocabulary text ("piece\\tscore" per line) of
+    `size` pieces, in the layout of the shipped vocab: the six special tokens
+    (ids 0-5), the 256 byte-fallback pieces <0xXX>, the base characters
+    (U+2581, printable ASCII, a few non-ASCII letters), then merged pieces
+    drawn from words and JSON fragments with scores -(merge rank)."""
+    rng = np.random.default_rng(seed)
+    pieces = list(SPECIAL_PIECES) + ["<0x%02X>" % b for b in range(256)]
+    base = ["\u2581"] + [chr(c) for c in range(0x21, 0x7F)] + list("éàüßñ")
+    pieces += base
+    scores = [0.0] * len(pieces)
+    words = ["name", "arguments", "get", "weather", "location", "unit", "city", "search", "query", "time",
+             "set", "alarm", "send", "message", "email", "book", "flight", "from", "to", "date", "the", "what",
+             "is", "of", "for", "and", "please", "new", "york", "paris", "celsius", "call", "tool", "value"]
+    letters = "abcdefghijklmnopqrstuvwxyz"
+    for _ in range(600):
+        words.append("".join(rng.choice(list(letters), int(rng.integers(2, 9)))))
+    frags = ['{"', '":"', '","', '":{', '"}', '}}', '}]', '[{"', '":', ',"', '":"get', '_', '":[']
+    cand = []
+    seen = set(pieces)
+    for w in words:
+        for form in (w, "\u2581" + w, w.capitalize(), "\u2581" + w.capitalize(), "_" + w):
+            for L in range(2, min(len(form), 9) + 1):
+                for i in range(0, len(form) - L + 1):
+                    cand.append(form[i:i + L])
+    cand += frags
+    rng.shuffle(cand)
+    # shorter pieces first so that longer ones are reachable through merges
+    cand.sort(key=len)
+    rank = 1
+    for c in cand:
+        if len(pieces) >= size:
+            break
+        if c in seen:
+            continue
+        seen.add(c)
+        pieces.append(c)
+        scores.append(-float(rank))
+        rank += 1
+    while len(pieces) < size:  # pad with unused pieces
+        pieces.append("<extra_%d>" % len(pieces))
+        scores.append(-float(rank))
+        rank += 1
+    return "".join("%s\t%s\n" % (p, repr(sc) if sc != int(sc) else "%d" % int(sc)) for p, sc in zip(pieces, scores))

@@ -211,6 +211,29 @@ class NeedleEngine:
             lib().needle_free_str(out[i])
         return res
 
+    @property
+    def contrastive_dim(self):
+        return lib().needle_contrastive_dim(self._h)
+
+    def encode_contrastive(self, text):
+        """L2-normalised contrastive embedding, or None without a head."""
+        c = self.contrastive_dim
+        if not c:
+            return None
+        out = np.zeros(c, np.float32)
+        if not lib().needle_encode_contrastive(self._h, text.encode(), _p(out), c):
+            raise NeedleError(last_error() or "needle_encode_contrastive failed")
+        return out
+
+    def retrieve_tools(self, query, tool_descriptions, top_k):
+        """[(index, score)] by descending contrastive similarity (retrieve_tools)."""
+        n = len(tool_descriptions)
+        descs = (C.c_char_p * max(n, 1))(*[t.encode() for t in tool_descriptions])
+        idx = np.zeros(max(top_k, 1), np.uint64)
+        sc = np.zeros(max(top_k, 1), np.float32)
+        m = lib().needle_retrieve_tools(self._h, query.encode(), descs, n, top_k, _p(idx), _p(sc))
+        return [(int(idx[i]), float(sc[i])) for i in range(m)]
+
     def vocab(self):
         """The handle's vocabulary (valid while the engine is open)."""
         return Vocab(_handle=lib().needle_handle_vocab(self._h), _owner=self)

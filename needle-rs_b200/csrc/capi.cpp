@@ -12,6 +12,7 @@
 #include <memory>
 #include <mutex>
 #include <string>
+#include <algorithm>
 #include <vector>
 
 #include "../../include/needle_b200.h"
@@ -478,26 +479,106 @@ char *needle_run_stream(NeedleHandle *h, const char *query, const char *tools_js
   return run_text(h, query, tools_json, cb, ud);
 }
 
-size_t needle_contrastive_dim(NeedleHandle *h) {
-  (void)h;
-  return 0;  // random-init / shipped checkpoints without contrastive tensors
+static bool dev_check(cudaError_t e);
+
+// encode_contrastive (engine.rs:153-181) for several texts in one
+// prefill-only batch: emb [n][c_dim] (zeros for a text without tokens).
+static bool contrastive_batch(NeedleHandle *h, const std::vector<std::string> &texts, std::vector<float> &emb) {
+  const DevModel &m = *h->model;
+  const int c = m.c_dim, d = m.cfg.d_model;
+  emb.assign(texts.size() * (size_t)c, 0.0f);
+  std::vector<uint32_t> ids;
+  std::vector<uint64_t> off(1, 0);
+  std::vector<size_t> slot;
+  for (size_t i = 0; i < texts.size(); ++i) {
+    const std::vector<uint32_t> t = h->vocab.v.encode(texts[i]);
+    if (t.empty()) continue;
+    if (t.size() > (size_t)m.cfg.max_enc_len) {
+      set_err("text " + std::to_string(i) + " has " + std::to_string(t.size()) + " tokens, more than max_enc_len");
+      return false;
+    }
+    for (uint32_t id : t)
+      if (id >= (uint32_t)m.cfg.vocab_size) {
+        set_err("the vocabulary has token ids beyond the model's vocab_size");
+        return false;
+      }
+    ids.insert(ids.end(), t.begin(), t.end());
+    off.push_back(ids.size());
+    slot.push_back(i);
+  }
+  if (slot.empty()) return true;
+  const int B = (int)slot.size();
+  BatchSpec s;
+  s.ids = ids.data();
+  s.offsets = off.data();
+  s.n_req = B;
+  s.max_new = 0;
+  s.want_enc_out = true;
+  Batch b(h->model.get());
+  std::string err;
+  if (!b.prepare(s, err) || !b.run(err)) {
+    set_err(err);
+    return false;
+  }
+  cudaStream_t st = b.stream();
+  float *dout = nullptr;
+  std::vector<float> host((size_t)B * c);
+  bool ok = dev_check(cudaMallocAsync(&dout, host.size() * sizeof(float), st)) &&
+            dev_check(contrastive_embed(b.enc_out_dev(), b.seq_off_dev(), B, d, m.c_hk, m.c_hb, m.c_hidden, m.c_pk,
+                                        c, dout, st)) &&
+            dev_check(cudaMemcpyAsync(host.data(), dout, host.size() * sizeof(float), cudaMemcpyDeviceToHost, st));
+  if (dout) cudaFreeAsync(dout, st);
+  if (!ok || !dev_check(cudaStreamSynchronize(st))) return false;
+  for (int i = 0; i < B; ++i) std::copy(&host[(size_t)i * c], &host[(size_t)(i + 1) * c], &emb[slot[i] * c]);
+  return true;
 }
+
+size_t needle_contrastive_dim(NeedleHandle *h) { return h ? (size_t)h->model->c_dim : 0; }
 
 bool needle_encode_contrastive(NeedleHandle *h, const char *text, float *out, size_t dim) {
-  (void)text;
-  (void)dim;
-  if (!h || !out) return false;
-  return false;
+  if (!h || !out || !text || !valid_utf8((const uint8_t *)text, std::strlen(text))) return false;
+  if (!h->model->c_dim) return false;
+  std::vector<float> emb;
+  if (!contrastive_batch(h, {text}, emb) || emb.size() != dim) return false;
+  std::copy(emb.begin(), emb.end(), out);
+  return true;
 }
 
+// retrieve_tools (engine.rs:189-217): query and descriptions embedded in one
+// batch, dot-product scores (sequential f32 sums), a stable sort by
+// descending score in f32::total_cmp order, the first top_k written.
 size_t needle_retrieve_tools(NeedleHandle *h, const char *query, const char **descs, size_t n, size_t k,
                              size_t *idx, float *scores) {
-  (void)query;
-  (void)descs;
-  (void)idx;
-  (void)scores;
-  if (!h || n == 0 || k == 0) return 0;
-  return 0;
+  if (!h || !query || !descs || !idx || !scores || n == 0 || k == 0) return 0;
+  if (!valid_utf8((const uint8_t *)query, std::strlen(query))) return 0;
+  std::vector<std::string> texts{query};
+  for (size_t i = 0; i < n; ++i) {
+    if (!descs[i] || !valid_utf8((const uint8_t *)descs[i], std::strlen(descs[i]))) return 0;
+    texts.push_back(descs[i]);
+  }
+  const size_t c = (size_t)h->model->c_dim;
+  if (!c) return 0;
+  std::vector<float> emb;
+  if (!contrastive_batch(h, texts, emb)) return 0;
+  std::vector<std::pair<size_t, float>> res(n);
+  for (size_t i = 0; i < n; ++i) {
+    float sc = 0.0f;
+    for (size_t j = 0; j < c; ++j) sc += emb[j] * emb[(i + 1) * c + j];
+    res[i] = {i, sc};
+  }
+  auto key = [](float x) {  // f32::total_cmp as a signed integer order
+    int32_t b;
+    std::memcpy(&b, &x, 4);
+    return b ^ (int32_t)((uint32_t)(b >> 31) >> 1);
+  };
+  std::stable_sort(res.begin(), res.end(),
+                   [&](const auto &a, const auto &b) { return key(a.second) > key(b.second); });
+  const size_t m = std::min(k, n);
+  for (size_t i = 0; i < m; ++i) {
+    idx[i] = res[i].first;
+    scores[i] = res[i].second;
+  }
+  return m;
 }
 
 void needle_free_str(char *s) { std::free(s); }

@@ -418,6 +418,22 @@ std::unique_ptr<DevModel> load_model(std::vector<uint8_t> raw, int device, std::
   }
   if (!L.vec("encoder_final_norm", d, m->enc_final_norm) || !L.vec("decoder_final_norm", d, m->dec_final_norm))
     return nullptr;
+  {  // load_contrastive_head (engine.rs:548-573): all three tensors with
+     // consistent shapes, else no head
+    std::vector<float> pk, hk, hb;
+    if (st.get_f32("contrastive_proj_kernel", pk) && st.get_f32("contrastive_hidden_kernel", hk) &&
+        st.get_f32("contrastive_hidden_bias", hb)) {
+      const size_t h = hb.size();
+      if (h != 0 && hk.size() == (size_t)d * h && pk.size() % h == 0 && h <= (size_t)INT32_MAX &&
+          pk.size() / h <= (size_t)INT32_MAX) {
+        if (!L.upload(m->c_hk, hk.data(), hk.size()) || !L.upload(m->c_hb, hb.data(), hb.size()) ||
+            !L.upload(m->c_pk, pk.data(), pk.size()))
+          return nullptr;
+        m->c_hidden = (int)h;
+        m->c_dim = (int)(pk.size() / h);
+      }
+    }
+  }
   // RoPE table (rope.rs:20-41, model.rs:52-56), computed on the host with the
   // reference's formula and uploaded.
   m->rope_len = std::max(c.max_enc_len, c.max_dec_len);

@@ -85,6 +85,9 @@ struct DevModel {
   std::vector<void *> allocs;
   size_t weight_bytes = 0;
   int *kerr = nullptr;  // device flag: a bounded in-kernel wait expired
+  // contrastive head (engine.rs:28-34, 548-573), when the file has it
+  int c_hidden = 0, c_dim = 0;
+  float *c_hk = nullptr, *c_hb = nullptr, *c_pk = nullptr;  // [d][h], [h], [h][c]
 
   ~DevModel();
 };
@@ -152,6 +155,10 @@ class Batch {
   bool peek_step(int step, uint32_t *tokens, uint32_t *lens, uint8_t *done, std::string &err);
   bool download(uint32_t *out_ids, uint32_t *out_lens, float *logits, float *enc_out, std::string &err);
   cudaStream_t stream() const { return st_; }
+  // Encoder output rows [ttot][d] (prepared with want_enc_out) and the
+  // requests' row offsets [n_req + 1], on the device.
+  const float *enc_out_dev() const { return enc_out_; }
+  const int64_t *seq_off_dev() const { return seq_off_; }
   // Number of kernels one run() launches (reported by the benchmark).
   int64_t kernels_launched() const { return launches_; }
   // Optional timing of one kernel class: CUDA events around each of its

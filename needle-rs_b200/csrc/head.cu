@@ -273,4 +273,59 @@ cudaError_t finish_step(unsigned long long *keys, int B, int max_new, int stop_o
   return cudaGetLastError();
 }
 
+
+namespace {
+// Sequential f32 sums with separate multiply and add roundings, as the
+// reference computes them.
+__global__ void contrastive_kernel(const float *__restrict__ enc, const int64_t *__restrict__ off, int d,
+                                   const float *__restrict__ hk, const float *__restrict__ hb, int h,
+                                   const float *__restrict__ pk, int c, float *out) {
+  extern __shared__ float cs[];
+  float *pooled = cs, *hidden = cs + d, *proj = hidden + h;
+  const int r = blockIdx.x;
+  const int64_t o = off[r];
+  const int T = (int)(off[r + 1] - o);
+  const float inv_n = __fdiv_rn(1.0f, (float)T);
+  for (int j = threadIdx.x; j < d; j += blockDim.x) {
+    float acc = 0.0f;
+    for (int t = 0; t < T; ++t) acc = __fadd_rn(acc, enc[(o + t) * d + j]);
+    pooled[j] = __fmul_rn(acc, inv_n);
+  }
+  __syncthreads();
+  for (int j = threadIdx.x; j < h; j += blockDim.x) {
+    float acc = hb[j];
+    for (int i = 0; i < d; ++i) acc = __fadd_rn(acc, __fmul_rn(pooled[i], hk[(int64_t)i * h + j]));
+    hidden[j] = fmaxf(acc, 0.0f);
+  }
+  __syncthreads();
+  for (int j = threadIdx.x; j < c; j += blockDim.x) {
+    float acc = 0.0f;
+    for (int i = 0; i < h; ++i) acc = __fadd_rn(acc, __fmul_rn(hidden[i], pk[(int64_t)i * c + j]));
+    proj[j] = acc;
+  }
+  __syncthreads();
+  __shared__ float norm;
+  if (threadIdx.x == 0) {
+    float sq = 0.0f;
+    for (int j = 0; j < c; ++j) sq = __fadd_rn(sq, __fmul_rn(proj[j], proj[j]));
+    norm = __fsqrt_rn(__fadd_rn(sq, 1e-12f));
+  }
+  __syncthreads();
+  for (int j = threadIdx.x; j < c; j += blockDim.x) out[(int64_t)r * c + j] = __fdiv_rn(proj[j], norm);
+}
+}  // namespace
+
+cudaError_t contrastive_embed(const float *enc, const int64_t *off, int n_req, int d, const float *hk,
+                              const float *hb, int h, const float *pk, int c, float *out, cudaStream_t st) {
+  if (n_req <= 0) return cudaSuccess;
+  const size_t sm = ((size_t)d + h + c) * sizeof(float);
+  if (sm > (size_t)kMaxDynSmem) return cudaErrorInvalidValue;
+  if (sm > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(contrastive_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    if (e != cudaSuccess) return e;
+  }
+  contrastive_kernel<<<n_req, 256, sm, st>>>(enc, off, d, hk, hb, h, pk, c, out);
+  return cudaGetLastError();
+}
+
 }  // namespace ndl

@@ -103,6 +103,13 @@ cudaError_t tc_matmul(const TcPlanes &A, int M, const TcPlanes &B, int N, const 
                       cudaStream_t st, bool b_lo_zero = false);
 cudaError_t init_tc_kernels();
 
+// ContrastiveHead::encode (engine.rs:37-69) after the mean pool of
+// encode_contrastive (engine.rs:163-179), one CTA per request: out[r][c] from
+// the encoder rows [off[r], off[r+1]) of enc [.][d], in the reference's
+// sequential f32 order (no fused multiply-add).
+cudaError_t contrastive_embed(const float *enc, const int64_t *off, int n_req, int d, const float *hk,
+                              const float *hb, int h, const float *pk, int c, float *out, cudaStream_t st);
+
 // ── tensor-core encoder attention (tc_attn.cu) ──
 // Per-head bf16 hi/lo planes of the normed + RoPE'd Q, K and the V of one
 // prefill chunk: Q [H][slab][64], K and V [KVH][slab][64] (buf: qh ql kh kl

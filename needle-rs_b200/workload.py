@@ -61,8 +61,11 @@ def to_bf16_bytes(a):
     return (np.asarray(a, np.float32).view(np.uint32) >> 16).astype(np.uint16).tobytes()
 
 
-def random_model(seed=0, path=None, **overrides):
-    """SafeTensors bytes of a random-init model (config overrides allowed)."""
+def random_model(seed=0, path=None, contrastive=None, **overrides):
+    """SafeTensors bytes of a random-init model (config overrides allowed).
+    contrastive=(hidden_dim, contrastive_dim) adds the contrastive head's F32
+    tensors (contrastive_hidden_kernel [d, h], contrastive_hidden_bias [h],
+    contrastive_proj_kernel [h, c]), drawn after every other tensor."""
     cfg = dict(DEFAULT_CFG)
     cfg.update(overrides)
     rng = np.random.default_rng(seed)
@@ -117,6 +120,11 @@ def random_model(seed=0, path=None, **overrides):
         attn(p + ".cross_attn")
         if not nf:
             ffn(p)
+    if contrastive is not None:
+        h, c = contrastive
+        f32("contrastive_hidden_kernel", rng.standard_normal((d, h)) / np.sqrt(d))
+        f32("contrastive_hidden_bias", rng.uniform(-0.1, 0.1, h))
+        f32("contrastive_proj_kernel", rng.standard_normal((h, c)) / np.sqrt(h))
     return write_safetensors(T, path, metadata=cfg)
 
 

@@ -372,6 +372,9 @@ struct Model {
   std::vector<float> enc_final_norm, dec_final_norm;
   Rope rope;
   float embed_scale = 0;
+  // contrastive head (engine.rs:28-34), present when the file has its tensors
+  std::vector<float> c_hk, c_hb, c_pk;  // [d][h], [h], [h][c]
+  size_t c_hidden = 0, c_dim = 0;
 };
 
 // ffn.rs:19-56
@@ -1118,6 +1121,22 @@ Model *load_model(std::vector<uint8_t> raw, std::string &err) {
   m->rope.sin.assign(m->rope.max_len * m->rope.half_dim, 0.0f);
   rope_table(m->rope.max_len, hd, c.rope_theta, m->rope.cos.data(), m->rope.sin.data());
   m->embed_scale = std::sqrt((float)d);
+  // load_contrastive_head (engine.rs:548-573): all three tensors, shapes
+  // consistent with d_model, else no head
+  {
+    std::vector<float> pk, hk, hb;
+    if (st.get_f32("contrastive_proj_kernel", pk) && st.get_f32("contrastive_hidden_kernel", hk) &&
+        st.get_f32("contrastive_hidden_bias", hb)) {
+      size_t h = hb.size();
+      if (h != 0 && hk.size() == d * h && pk.size() % h == 0) {
+        m->c_hk = std::move(hk);
+        m->c_hb = std::move(hb);
+        m->c_pk = std::move(pk);
+        m->c_hidden = h;
+        m->c_dim = m->c_pk.size() / h;
+      }
+    }
+  }
   return m;
 }
 
@@ -1257,6 +1276,46 @@ int orc_forward(const void *mp, const uint32_t *enc_ids, size_t n_enc, const uin
   }
   return 0;
 }
+
+// encode_contrastive (engine.rs:153-181) + ContrastiveHead::encode
+// (engine.rs:37-69): encoder output mean-pooled over positions (sequential
+// sums, then * 1/T), relu(pooled @ hidden_kernel + bias) @ proj_kernel, L2
+// normalised with eps 1e-12.  Returns the embedding length (0: no head);
+// an empty id list gives the zero vector.
+size_t orc_encode_contrastive(const void *mp, const uint32_t *ids, size_t n, float *out) {
+  const Model &m = *(const Model *)mp;
+  if (!m.c_dim) return 0;
+  const size_t d = m.cfg.d_model, h = m.c_hidden, c = m.c_dim;
+  if (n == 0) {
+    std::fill(out, out + c, 0.0f);
+    return c;
+  }
+  if (!ids_valid(m, ids, n)) return 0;
+  auto enc_kv = make_enc_kv(m, n);
+  auto x = encode(m, ids, n, enc_kv);
+  std::vector<float> pooled(d, 0.0f), hidden(h), proj(c);
+  for (size_t t = 0; t < n; ++t)
+    for (size_t j = 0; j < d; ++j) pooled[j] += x[t * d + j];
+  const float inv_n = 1.0f / (float)n;
+  for (auto &v : pooled) v *= inv_n;
+  for (size_t j = 0; j < h; ++j) {
+    float acc = m.c_hb[j];
+    for (size_t i = 0; i < d; ++i) acc += pooled[i] * m.c_hk[i * h + j];
+    hidden[j] = std::max(acc, 0.0f);
+  }
+  for (size_t j = 0; j < c; ++j) {
+    float acc = 0.0f;
+    for (size_t i = 0; i < h; ++i) acc += hidden[i] * m.c_pk[i * c + j];
+    proj[j] = acc;
+  }
+  float sq = 0.0f;
+  for (float v : proj) sq += v * v;
+  const float norm = std::sqrt(sq + 1e-12f);
+  for (size_t j = 0; j < c; ++j) out[j] = proj[j] / norm;
+  return c;
+}
+
+size_t orc_contrastive_dim(const void *mp) { return ((const Model *)mp)->c_dim; }
 
 size_t orc_generate(const void *mp, const uint32_t *enc_ids, size_t n_enc, size_t max_new,
                     const uint64_t *mask_bits, int stop_on_eos, uint32_t *out_ids, float *margins,

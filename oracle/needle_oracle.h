@@ -104,6 +104,10 @@ int orc_run_batch(const void *model, const uint32_t *ids,
 /* KV-cache saturation semantics (attn.rs:53-67): pushes n_push rows into a
  * cache of max_len rows; returns the final len. */
 size_t orc_kv_cache_push_count(size_t max_len, size_t n_push);
+/* encode_contrastive (engine.rs:153-181): embedding length written to out
+ * (0: the model has no contrastive head); no ids -> zero vector. */
+size_t orc_encode_contrastive(const void *model, const uint32_t *ids, size_t n, float *out);
+size_t orc_contrastive_dim(const void *model);
 
 #ifdef __cplusplus
 }

@@ -49,6 +49,8 @@ def lib():
             "orc_generate": (S, [P, P, S, S, P, I, P, P, P]),
             "orc_run_batch": (I, [P, P, P, S, S, P, I, P, P, P, I]),
             "orc_kv_cache_push_count": (S, [S, S]),
+            "orc_encode_contrastive": (S, [P, P, S, P]),
+            "orc_contrastive_dim": (S, [P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -166,6 +168,22 @@ class Model:
         if rc != 0:
             raise ValueError("invalid token ids")
         return enc, lg
+
+    @property
+    def contrastive_dim(self):
+        return lib().orc_contrastive_dim(self.h)
+
+    def encode_contrastive(self, ids):
+        """encode_contrastive (engine.rs:153-181) on token ids, or None
+        without a contrastive head."""
+        c = self.contrastive_dim
+        if not c:
+            return None
+        e = np.ascontiguousarray(ids, np.uint32)
+        out = np.zeros(c, np.float32)
+        if lib().orc_encode_contrastive(self.h, _p(e) if e.size else None, e.size, _p(out)) != c:
+            raise ValueError("invalid token ids")
+        return out
 
     def generate(self, enc_ids, max_new, mask_bits=None, stop_on_eos=False, want_logits=False):
         e = np.ascontiguousarray(enc_ids, np.uint32)

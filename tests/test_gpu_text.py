@@ -42,7 +42,7 @@ CASES = [
 def models():
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
-    blob = wl.random_model(seed=21, max_dec_len=STEPS)
+    blob = wl.random_model(seed=21, max_dec_len=STEPS, contrastive=(256, 128))
     return nb.NeedleEngine.from_bytes(blob, VOCAB), orc.Model(data=blob), to.Vocab(VOCAB)
 
 
@@ -133,3 +133,46 @@ def test_step_masks_match_upfront_masks(models):
         assert np.array_equal(lens, ref_lens)
     finally:
         b.close()
+
+
+# ── contrastive head (engine.rs:24-217) ───────────────────────────────────
+
+DESCS = ["Get the current weather for a city", "Send an email message", "Book a flight between two cities",
+         "", "Search the web", "Set an alarm for a time", "naïve café 中文"]
+
+
+def test_encode_contrastive_matches_reference(models):
+    eng, model, vocab = models
+    assert eng.contrastive_dim == model.contrastive_dim == 128
+    for text in ["What's the weather in Paris?"] + DESCS:
+        got = eng.encode_contrastive(text)
+        ref = model.encode_contrastive(vocab.encode(text))
+        assert np.all(np.abs(got - ref) <= ATOL + RTOL * np.abs(ref)), (text, float(np.max(np.abs(got - ref))))
+    assert not np.any(eng.encode_contrastive("   "))  # no tokens: the zero vector
+
+
+def test_retrieve_tools_matches_reference(models):
+    eng, model, vocab = models
+    query = "What's the weather in Paris?"
+    got = eng.retrieve_tools(query, DESCS, 4)
+    q = model.encode_contrastive(vocab.encode(query))
+    ref = [float(np.dot(q, model.encode_contrastive(vocab.encode(t)))) for t in DESCS]
+    order = sorted(range(len(DESCS)), key=lambda i: -ref[i])  # stable: ties keep index order
+    assert len(got) == 4
+    for r, (i, sc) in enumerate(got):
+        assert abs(sc - ref[i]) <= 1e-4
+        if r + 1 < len(DESCS) and abs(ref[order[r]] - ref[order[r + 1]]) > 1e-3:
+            assert i == order[r]
+    assert eng.retrieve_tools(query, DESCS, 100)[-1][0] in range(len(DESCS))
+    assert eng.retrieve_tools(query, [], 3) == []
+
+
+def test_no_contrastive_head():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    eng = nb.NeedleEngine.from_bytes(wl.random_model(seed=22, num_encoder_layers=1, num_decoder_layers=1), VOCAB)
+    try:
+        assert eng.contrastive_dim == 0 and eng.encode_contrastive("x") is None
+        assert eng.retrieve_tools("x", ["a", "b"], 2) == []
+    finally:
+        eng.close()

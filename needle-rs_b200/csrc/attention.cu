@@ -377,6 +377,14 @@ __global__ void __launch_bounds__(256) dec_self_attn_kernel(const float *__restr
 }
 
 // ── decoder attention over a K/V row range, head dim 64 ────────────────────
+// One value as the bf16 pair (hi, lo) of a tensor-core operand plane:
+// hi = bf16(v), lo = bf16(v - hi).
+__device__ __forceinline__ void store_split(__nv_bfloat16 *hi, __nv_bfloat16 *lo, float v) {
+  __nv_bfloat16 h = __float2bfloat16_rn(v);
+  *hi = h;
+  *lo = __float2bfloat16_rn(v - __bfloat162float(h));
+}
+
 // Shared by cross-attention (attn.rs:281-337; rows = the request's encoder
 // K/V) and decoder self-attention (attn.rs:100-183; rows = the request's
 // cache).  The REP query heads of one KV head (GQA) share every K and V row
@@ -386,7 +394,8 @@ __global__ void __launch_bounds__(256) dec_self_attn_kernel(const float *__restr
 template <int REP, int NT>
 __device__ __forceinline__ void attend_hd64(const float *qs, const float *__restrict__ kb,
                                             const float *__restrict__ vb, int kvd, int T, float scale, float *sc,
-                                            float *red, float *out_row) {
+                                            float *red, float *out_row, __nv_bfloat16 *hi_row = nullptr,
+                                            __nv_bfloat16 *lo_row = nullptr) {
   constexpr int HD = 64, NHW = NT / 16, NW = NT / 32, UNR = 4, SPAN = NHW * UNR;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int hw = tid >> 4, hl = tid & 15;
@@ -495,7 +504,10 @@ __device__ __forceinline__ void attend_hd64(const float *qs, const float *__rest
     int j = i / HD, d = i - j * HD;
     float sum = 0.0f;
     for (int w = 0; w < NHW; ++w) sum += red[(w * REP + j) * HD + d];
-    out_row[j * HD + d] = sum;
+    if (hi_row)
+      store_split(hi_row + j * HD + d, lo_row + j * HD + d, sum);
+    else
+      out_row[j * HD + d] = sum;
   }
 }
 
@@ -507,6 +519,7 @@ __global__ void __launch_bounds__(256) cross_attn_kernel(const float *__restrict
                                                          const float *__restrict__ kplane,
                                                          const float *__restrict__ vplane,
                                                          const int64_t *__restrict__ seq_off, float *out,
+                                                         __nv_bfloat16 *hi, __nv_bfloat16 *lo, int64_t ldp,
                                                          AttnDims a) {
   constexpr int HD = 64;
   extern __shared__ __align__(16) float sm[];
@@ -528,57 +541,197 @@ __global__ void __launch_bounds__(256) cross_attn_kernel(const float *__restrict
   }
   __syncthreads();
   attend_hd64<REP, 256>(qs, kplane + off * kvd + g * HD, vplane + off * kvd + g * HD, kvd, T, a.scale, sc, red,
-                        out + (int64_t)b * qd + g * REP * HD);
+                        out + (int64_t)b * qd + g * REP * HD, hi ? hi + (int64_t)b * ldp + g * REP * HD : nullptr,
+                        hi ? lo + (int64_t)b * ldp + g * REP * HD : nullptr);
 }
 
-// Decoder self-attention, head dim 64 (attn.rs:100-183).  CTA = (request, KV
-// head), 128 threads: warps 0..REP-1 ZCRMSNorm + RoPE (position pos[b]) the
-// group's query heads, warp REP does the same to the key and appends k, v to
-// the cache row pos[b] (push_kv saturates at cap, attn.rs:53-61), then the
-// group attends over the cache.
-template <int REP>
-__global__ void __launch_bounds__(128) self_attn_hd64_kernel(const float *__restrict__ qkv,
-                                                             const int32_t *__restrict__ step,
-                                                             const float *__restrict__ qn,
-                                                             const float *__restrict__ kn,
-                                                             const float *__restrict__ rc,
-                                                             const float *__restrict__ rs, float *kc, float *vc,
-                                                             int cap, float *out, AttnDims a) {
-  constexpr int HD = 64;
-  extern __shared__ __align__(16) float sm[];
+// 16-byte global -> shared copy that completes asynchronously (no register
+// holds the data in flight); cp_async_wait makes the executing thread's own
+// copies visible to it.
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)),
+               "l"(gmem)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+
+// Decoder self-attention for one new token per request, head dim 64, two
+// query heads per KV head (attn.rs:100-183).  CTA = (request, KV head), 128
+// threads, the context in passes of 64 cache rows:
+//   * every thread first starts asynchronous 16-byte copies of the pass's
+//     K and V rows into shared memory (K rows padded to 68 floats, so a
+//     thread reading a whole row meets no bank conflict);
+//   * PREP: while they are in flight, warps 0-1 apply ZCRMSNorm + RoPE
+//     (position pos) to the two query heads and warp 2 does the same to the
+//     new key and appends k, v at row pos (push_kv saturates at cap,
+//     attn.rs:53-61; the appended row is then read from shared memory).
+//     Without PREP the QKV projection's epilogue has done all of that
+//     already: q is read normed from qkv and row pos is in the cache;
+//   * scores: thread (head tid/64, row tid%64) forms one full 64-term dot;
+//   * softmax across passes with a running maximum and sum (ops.rs:5-36 up
+//     to the order of the sums);
+//   * P·V: thread (row group tid/16, dimensions 4·(tid%16)..+3) accumulates
+//     both heads over the rows of its group; the eight groups are summed at
+//     the end.
+// The result goes to out [B, H*64] f32, or, when hi is set, straight to the
+// bf16 hi/lo operand planes (row stride ldp) of the output projection.
+template <bool PREP>
+__global__ void __launch_bounds__(128) self_attn_step_kernel(
+    const float *__restrict__ qkv, const int32_t *__restrict__ step, const float *__restrict__ qn,
+    const float *__restrict__ kn, const float *__restrict__ rc, const float *__restrict__ rs, float *kc, float *vc,
+    int cap, float *out, __nv_bfloat16 *hi, __nv_bfloat16 *lo, int64_t ldp, AttnDims a) {
+  constexpr int HD = 64, REP = 2, CH = 64, KP = HD + 4;
+  __shared__ __align__(16) float ks[CH][KP];
+  __shared__ __align__(16) float vs[CH][HD];
+  __shared__ __align__(16) float qs[REP][HD];
+  __shared__ __align__(16) float knew[HD], vnew[HD];
+  __shared__ __align__(8) float2 ps[CH];  // (head 0, head 1) weights of a row
+  __shared__ float wmax[4], wsum[4];
+  float(*part)[REP][HD] = reinterpret_cast<float(*)[REP][HD]>(&vs[0][0]);  // after the last pass
   const int b = blockIdx.y, g = blockIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int qd = a.H * HD, kvd = a.KVH * HD, ld = qd + 2 * kvd;
-  float *qs = sm;                  // [REP][64]
-  float *red = sm + REP * HD;      // [8][REP][64]
-  float *sc = red + 8 * REP * HD;  // [REP][cap]
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int pos = step[b];
   const bool append = pos < cap;
+  // rows copied from the cache: with PREP the new row is not there yet
+  const int cached = PREP ? (append ? pos : cap) : (append ? pos + 1 : cap);
+  const int total = append ? pos + 1 : cap;  // rows attended over
+  const float *kcb = kc + (int64_t)b * cap * kvd + g * HD;
+  const float *vcb = vc + (int64_t)b * cap * kvd + g * HD;
   const float *row = qkv + (int64_t)b * ld;
-  float *kcb = kc + (int64_t)b * cap * kvd + g * HD;
-  float *vcb = vc + (int64_t)b * cap * kvd + g * HD;
-  const float *cr = rc + (int64_t)pos * (HD / 2), *sr = rs + (int64_t)pos * (HD / 2);
-  if (warp < REP) {
-    float *v = qs + warp * HD;
-    const float *src = row + (g * REP + warp) * HD;
-    v[lane] = src[lane];
-    v[lane + 32] = src[lane + 32];
-    __syncwarp();
-    norm_rope_head(v, HD, qn, cr, sr, true, lane);
-  } else if (warp == REP && append) {
-    float *kd = kcb + (int64_t)pos * kvd;
-    const float *ks = row + qd + g * HD, *vs = row + qd + kvd + g * HD;
-    kd[lane] = ks[lane];
-    kd[lane + 32] = ks[lane + 32];
-    __syncwarp();
-    norm_rope_head(kd, HD, kn, cr, sr, true, lane);
-    float *vd = vcb + (int64_t)pos * kvd;
-    vd[lane] = vs[lane];
-    vd[lane + 32] = vs[lane + 32];
+  auto fetch = [&](int c0) {
+    const int c = tid & 15;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int r = (tid >> 4) + 8 * u, t = c0 + r;
+      if (t < cached) {
+        cp_async16(&ks[r][4 * c], kcb + (int64_t)t * kvd + 4 * c);
+        cp_async16(&vs[r][4 * c], vcb + (int64_t)t * kvd + 4 * c);
+      }
+    }
+  };
+  fetch(0);
+  if constexpr (PREP) {
+    const float *cr = rc + (int64_t)pos * (HD / 2), *sr = rs + (int64_t)pos * (HD / 2);
+    if (warp < REP) {
+      float *v = qs[warp];
+      const float *src = row + (g * REP + warp) * HD;
+      v[lane] = src[lane];
+      v[lane + 32] = src[lane + 32];
+      __syncwarp();
+      norm_rope_head(v, HD, qn, cr, sr, true, lane);
+    } else if (warp == REP) {
+      const float *kr = row + qd + g * HD, *vr = row + qd + kvd + g * HD;
+      knew[lane] = kr[lane];
+      knew[lane + 32] = kr[lane + 32];
+      vnew[lane] = vr[lane];
+      vnew[lane + 32] = vr[lane + 32];
+      __syncwarp();
+      norm_rope_head(knew, HD, kn, cr, sr, true, lane);
+      __syncwarp();
+      if (append) {
+        float *kd = kc + ((int64_t)b * cap + pos) * kvd + g * HD;
+        float *vd = vc + ((int64_t)b * cap + pos) * kvd + g * HD;
+        kd[lane] = knew[lane];
+        kd[lane + 32] = knew[lane + 32];
+        vd[lane] = vnew[lane];
+        vd[lane + 32] = vnew[lane + 32];
+      }
+    }
+  } else {
+    if (tid < 2 * 16) cp_async16(&qs[tid >> 4][4 * (tid & 15)], row + (g * REP + (tid >> 4)) * HD + 4 * (tid & 15));
   }
-  __syncthreads();  // the appended row is visible to the whole block
-  attend_hd64<REP, 128>(qs, kcb, vcb, kvd, append ? pos + 1 : cap, a.scale, sc, red,
-                        out + (int64_t)b * qd + g * REP * HD);
+  const int sj = tid >> 6, sr_ = tid & 63;  // scores: (head, row)
+  const int rg = tid >> 4, dq = tid & 15;   // P·V: (row group, 4 dimensions)
+  float m[REP], l[REP], acc[REP][4];
+#pragma unroll
+  for (int j = 0; j < REP; ++j) {
+    m[j] = -INFINITY;
+    l[j] = 0.0f;
+    acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
+  }
+  for (int c0 = 0; c0 < total; c0 += CH) {
+    if (c0 > 0) fetch(c0);
+    cp_async_wait();
+    __syncthreads();  // every thread's copies (and q, the new row) visible
+    float sc = -INFINITY;
+    {
+      const int t = c0 + sr_;
+      if (t < total) {
+        const float *kp = (PREP && append && t == pos) ? knew : ks[sr_];
+        const float *q = qs[sj];
+        float d = 0.0f;
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          const float4 k4 = *reinterpret_cast<const float4 *>(kp + 4 * c);
+          const float4 q4 = *reinterpret_cast<const float4 *>(q + 4 * c);
+          d = fmaf(q4.x, k4.x, d);
+          d = fmaf(q4.y, k4.y, d);
+          d = fmaf(q4.z, k4.z, d);
+          d = fmaf(q4.w, k4.w, d);
+        }
+        sc = d * a.scale;
+      }
+    }
+    const float wm = warp_max(sc);
+    if (lane == 0) wmax[warp] = wm;
+    __syncthreads();
+    float corr[REP];
+#pragma unroll
+    for (int j = 0; j < REP; ++j) {
+      const float mn = fmaxf(m[j], fmaxf(wmax[2 * j], wmax[2 * j + 1]));
+      corr[j] = expf(m[j] - mn);  // 0 on the first pass (m = -inf)
+      m[j] = mn;
+    }
+    const float p = c0 + sr_ < total ? expf(sc - (sj ? m[1] : m[0])) : 0.0f;
+    reinterpret_cast<float *>(&ps[sr_])[sj] = p;
+    const float wsm = warp_sum(p);
+    if (lane == 0) wsum[warp] = wsm;
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < REP; ++j) {
+      l[j] = l[j] * corr[j] + (wsum[2 * j] + wsum[2 * j + 1]);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[j][e] *= corr[j];
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int r = rg + 8 * u, t = c0 + r;
+      if (t >= total) break;
+      const float4 v4 = (PREP && append && t == pos) ? *reinterpret_cast<const float4 *>(&vnew[4 * dq])
+                                                     : *reinterpret_cast<const float4 *>(&vs[r][4 * dq]);
+      const float2 pj = ps[r];
+      acc[0][0] = fmaf(pj.x, v4.x, acc[0][0]);
+      acc[0][1] = fmaf(pj.x, v4.y, acc[0][1]);
+      acc[0][2] = fmaf(pj.x, v4.z, acc[0][2]);
+      acc[0][3] = fmaf(pj.x, v4.w, acc[0][3]);
+      acc[1][0] = fmaf(pj.y, v4.x, acc[1][0]);
+      acc[1][1] = fmaf(pj.y, v4.y, acc[1][1]);
+      acc[1][2] = fmaf(pj.y, v4.z, acc[1][2]);
+      acc[1][3] = fmaf(pj.y, v4.w, acc[1][3]);
+    }
+    __syncthreads();  // shared tiles free for the next pass
+  }
+  // the two row groups of a warp, then the four warps
+#pragma unroll
+  for (int j = 0; j < REP; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[j][e] += __shfl_xor_sync(0xffffffffu, acc[j][e], 16);
+  if (lane < 16)
+#pragma unroll
+    for (int j = 0; j < REP; ++j)
+      *reinterpret_cast<float4 *>(&part[warp][j][4 * dq]) = make_float4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]);
+  __syncthreads();
+  {
+    const int j = tid >> 6, d = tid & 63;
+    const float o = (part[0][j][d] + part[1][j][d] + part[2][j][d] + part[3][j][d]) * (1.0f / (j ? l[1] : l[0]));
+    const int64_t col = (int64_t)(g * REP + j) * HD + d;
+    if (hi)
+      store_split(hi + (int64_t)b * ldp + col, lo + (int64_t)b * ldp + col, o);
+    else
+      out[(int64_t)b * qd + col] = o;
+  }
 }
 
 // Generic cross-attention for head dims other than 64 (small test models).
@@ -647,8 +800,7 @@ cudaError_t init_attention_kernels() {
   set((const void *)encoder_attn_kernel);
   set((const void *)dec_self_attn_kernel);
   set((const void *)cross_attn_kernel<2>);
-  set((const void *)self_attn_hd64_kernel<2>);
-  set((const void *)cross_attn_generic_kernel);
+    set((const void *)cross_attn_generic_kernel);
   return e;
 }
 
@@ -709,16 +861,21 @@ cudaError_t encoder_attention(const float *qkv, const int64_t *seq_off, int n_re
 
 cudaError_t decoder_self_attention(const float *qkv, const int32_t *step, const float *q_norm,
                                    const float *k_norm, const float *rope_cos, const float *rope_sin, float *kc,
-                                   float *vc, int cap, int B, float *out, AttnDims a, cudaStream_t st) {
+                                   float *vc, int cap, int B, float *out, AttnDims a, cudaStream_t st, void *hi_,
+                                   void *lo_, int64_t ldp, bool prepared) {
+  __nv_bfloat16 *hi = static_cast<__nv_bfloat16 *>(hi_), *lo = static_cast<__nv_bfloat16 *>(lo_);
   if (B <= 0) return cudaSuccess;
   if (a.HD > 128 || (a.HD & 1) || cap <= 0) return cudaErrorInvalidValue;
   if (a.HD == 64 && a.H == 2 * a.KVH) {
-    size_t sm = ((size_t)2 * 64 + (size_t)8 * 2 * 64 + (size_t)2 * cap) * sizeof(float);
-    if (sm > kMaxDynSmem) return cudaErrorInvalidValue;
-    self_attn_hd64_kernel<2><<<dim3(a.KVH, B), 128, sm, st>>>(qkv, step, q_norm, k_norm, rope_cos, rope_sin, kc,
-                                                               vc, cap, out, a);
+    if (prepared)
+      self_attn_step_kernel<false><<<dim3(a.KVH, B), 128, 0, st>>>(qkv, step, q_norm, k_norm, rope_cos, rope_sin,
+                                                                   kc, vc, cap, out, hi, lo, ldp, a);
+    else
+      self_attn_step_kernel<true><<<dim3(a.KVH, B), 128, 0, st>>>(qkv, step, q_norm, k_norm, rope_cos, rope_sin, kc,
+                                                                  vc, cap, out, hi, lo, ldp, a);
     return cudaGetLastError();
   }
+  if (hi || prepared) return cudaErrorInvalidValue;
   size_t sm = ((size_t)a.H * a.HD + (size_t)a.H * cap) * sizeof(float);
   if (sm > kMaxDynSmem) return cudaErrorInvalidValue;
   dec_self_attn_kernel<<<B, 256, sm, st>>>(qkv, step, q_norm, k_norm, rope_cos, rope_sin, kc, vc, cap, out, a);
@@ -727,15 +884,17 @@ cudaError_t decoder_self_attention(const float *qkv, const int32_t *step, const 
 
 cudaError_t decoder_cross_attention(const float *q, const float *q_norm, const float *kplane,
                                     const float *vplane, const int64_t *seq_off, int B, float *out, AttnDims a,
-                                    cudaStream_t st, int max_len) {
+                                    cudaStream_t st, int max_len, void *hi_, void *lo_, int64_t ldp) {
+  __nv_bfloat16 *hi = static_cast<__nv_bfloat16 *>(hi_), *lo = static_cast<__nv_bfloat16 *>(lo_);
   if (B <= 0) return cudaSuccess;
   int rep = a.H / a.KVH;
   if (a.HD == 64 && rep == 2) {
     size_t sm = ((size_t)rep * 64 + (size_t)16 * rep * 64 + (size_t)rep * max_len) * sizeof(float);
     if (sm > kMaxDynSmem) return cudaErrorInvalidValue;
-    cross_attn_kernel<2><<<dim3(a.KVH, B), 256, sm, st>>>(q, q_norm, kplane, vplane, seq_off, out, a);
+    cross_attn_kernel<2><<<dim3(a.KVH, B), 256, sm, st>>>(q, q_norm, kplane, vplane, seq_off, out, hi, lo, ldp, a);
     return cudaGetLastError();
   }
+  if (hi) return cudaErrorInvalidValue;
   if (a.HD > 128 || (a.HD & 1)) return cudaErrorInvalidValue;
   size_t sm = ((size_t)a.H * a.HD + (size_t)a.H * max_len) * sizeof(float);
   if (sm > kMaxDynSmem) return cudaErrorInvalidValue;

@@ -924,6 +924,10 @@ bool Batch::decode_step(std::string &err, bool capture) {
   const int qkvd = qd + 2 * kvd;
   cudaStream_t st = st_;
   const TcPlanes *pd = (B >= kTcMinRows && d == 512) ? tc_map(tc_padded_k(d), B) : nullptr;
+  // attention outputs written straight as the output projections' operand planes
+  const TcPlanes *pa = (B >= kTcMinRows && hd == 64 && c.num_heads == 2 * c.num_kv_heads && qd == tc_padded_k(qd))
+                           ? tc_map(tc_padded_k(qd), B)
+                           : nullptr;
   auto norm = [&](const float *scale, float *f32_out) -> bool {
     if (pd) {
       NDL_TK(TIME_ELEMENTWISE, capture, rms_norm_planes(x_, d, tc_hi_, tc_lo_, pd->Kp, f32_out, d, scale, B, d, st));
@@ -934,20 +938,41 @@ bool Batch::decode_step(std::string &err, bool capture) {
   };
   for (size_t l = 0; l < m.dec.size(); ++l) {  // layers.rs:100-149
     const DecLayerDev &D = m.dec[l];
+    const TcPlanes *pal = (pa && D.sa_o.tc_ready && D.ca_o.tc_ready && D.sa_o.tc.Kp == pa->Kp && D.ca_o.tc.Kp == pa->Kp)
+                              ? pa
+                              : nullptr;
+    void *ahi = pal ? tc_hi_ : nullptr, *alo = pal ? tc_lo_ : nullptr;
+    const int64_t aldp = pal ? pal->Kp : 0;
     if (!norm(D.sa_norm, nullptr)) return false;
+    const size_t coff = l * (size_t)B * cap_ * kvd;
+    // tensor-core path: q/k norm, RoPE and the cache append run in the QKV
+    // projection's epilogue
+    const bool prep = pd && D.sa_qkv.tc_ready && hd == 64 && c.num_heads == 2 * c.num_kv_heads;
     MatmulOut o;
     o.y = qkv_;
     o.ldy = qkvd;
+    if (prep) {
+      o.epi = EPI_QKV_DEC;
+      o.pos = pos_;
+      o.q_norm = D.sa_qn;
+      o.k_norm = D.sa_kn;
+      o.rope_cos = m.rope_cos;
+      o.rope_sin = m.rope_sin;
+      o.heads_q = c.num_heads;
+      o.heads_kv = c.num_kv_heads;
+      o.kcache = self_k_ + coff;
+      o.vcache = self_v_ + coff;
+      o.cache_cap = cap_;
+    }
     if (!mm_in(TIME_DECODE_MATMUL, capture, pd, xn_, d, B, D.sa_qkv, o, err)) return false;
-    size_t coff = l * (size_t)B * cap_ * kvd;
     NDL_TK(TIME_SELF_ATTENTION, capture, decoder_self_attention(qkv_, pos_, D.sa_qn, D.sa_kn, m.rope_cos, m.rope_sin, self_k_ + coff,
-                                  self_v_ + coff, cap_, B, att_, m.ad, st));
+                                  self_v_ + coff, cap_, B, att_, m.ad, st, ahi, alo, aldp, prep));
     MatmulOut r;
     r.y = x_;
     r.ldy = d;
     r.epi = EPI_RESID;
     r.gate = D.sa_gate;
-    if (!mm(TIME_DECODE_MATMUL, capture, att_, qd, B, D.sa_o, r, err)) return false;
+    if (!mm_in(TIME_DECODE_MATMUL, capture, pal, att_, qd, B, D.sa_o, r, err)) return false;
     if (!norm(D.ca_norm, nullptr)) return false;
     MatmulOut qo;
     qo.y = q_;
@@ -956,7 +981,7 @@ bool Batch::decode_step(std::string &err, bool capture) {
     const float *kp = kv_planes_ + (size_t)2 * l * ttot_ * kvd, *vp = kp + (size_t)ttot_ * kvd;
     cudaEvent_t ev;
     if (!tbegin(TIME_CROSS_ATTENTION, capture, ev, err)) return false;
-    NDL_LK(decoder_cross_attention(q_, D.ca_qn, kp, vp, seq_off_, B, att_, m.ad, st, tmax_));
+    NDL_LK(decoder_cross_attention(q_, D.ca_qn, kp, vp, seq_off_, B, att_, m.ad, st, tmax_, ahi, alo, aldp));
     // algorithmic bytes: the encoder K and V rows once, q in, attention out
     if (!tend(ev, 4.0 * (double)ttot_ * kvd * c.num_heads / c.num_kv_heads,
               (double)ttot_ * kvd * 8 + (double)B * qd * 8, err))
@@ -966,7 +991,7 @@ bool Batch::decode_step(std::string &err, bool capture) {
     r2.ldy = d;
     r2.epi = EPI_RESID;
     r2.gate = D.ca_gate;
-    if (!mm(TIME_DECODE_MATMUL, capture, att_, qd, B, D.ca_o, r2, err)) return false;
+    if (!mm_in(TIME_DECODE_MATMUL, capture, pal, att_, qd, B, D.ca_o, r2, err)) return false;
     if (D.ffn) {
       if (!norm(D.ffn_norm, nullptr)) return false;
       MatmulOut a;

@@ -576,6 +576,7 @@ cudaError_t int4_matmul(const float *x, int64_t ldx, int M, const Int4Weight &W,
   // Output groups of 4 columns never straddle a column block; the fused
   // k-norm needs whole 64-column heads.
   if (o.col_block && (o.col_block % 4)) return cudaErrorInvalidValue;
+  if (o.epi == EPI_QKV || o.epi == EPI_QKV_DEC || o.epi == EPI_ARGMAX) return cudaErrorInvalidValue;  // tensor-core only
   if (o.epi == EPI_KNORM && (!o.col_block || (o.col_block % 64) || !o.vec)) return cudaErrorInvalidValue;
   if (o.epi == EPI_ACT && (W.N & 1)) return cudaErrorInvalidValue;
   EpiCtx e{o, W.N};

@@ -45,6 +45,11 @@ enum Epilogue : int {
   EPI_QKV = 5,    // fused Q|K|V projection of the encoder: per 64-column head,
                   // ZCRMSNorm + RoPE (Q, K) then bf16 hi/lo into the attention
                   // planes (tensor-core path only)
+  EPI_QKV_DEC = 6,  // fused Q|K|V projection of one decoder step: per 64-column
+                    // head, ZCRMSNorm + RoPE at position pos[m] (Q, K); Q f32 to
+                    // y, K and V appended to the self-attention caches at row
+                    // pos[m] when pos[m] < cache_cap (attn.rs:100-140, push_kv
+                    // saturating as attn.rs:53-61; tensor-core path only)
 };
 
 enum Activation : int { ACT_DRELU = 0, ACT_SWIGLU = 1, ACT_GELU = 2 };
@@ -71,6 +76,9 @@ struct MatmulOut {
   const float *q_norm = nullptr, *k_norm = nullptr, *rope_cos = nullptr, *rope_sin = nullptr;
   void *planes[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
   int slab = 0, heads_q = 0, heads_kv = 0;
+  // EPI_QKV_DEC: caches [M][cache_cap][heads_kv*64] f32
+  float *kcache = nullptr, *vcache = nullptr;
+  int cache_cap = 0;
 };
 
 // Y[M, N] (epilogue) X[M, K] @ W.  x row stride ldx (floats).
@@ -177,17 +185,24 @@ cudaError_t encoder_attention(const float *qkv, const int64_t *seq_off, int n_re
 // Decoder self-attention for one new token per request (attn.rs:100-183):
 // q|k|v from qkv rows [B, (H+2*KVH)*HD]; ZCRMSNorm + RoPE at position
 // step[b], append k, v to the caches (saturating at cap), attend over the
-// cache.  kc/vc: [B, cap, KVH*HD].  out: [B, H*HD].
+// cache.  kc/vc: [B, cap, KVH*HD].  out: [B, H*HD] f32, or, when hi is set
+// (head dim 64, two query heads per KV head), the bf16 hi/lo operand planes
+// of the next tensor-core matmul, row stride ldp elements.  `prepared`
+// (same head layout): the QKV projection ran with EPI_QKV_DEC, so q in qkv is
+// already normed and rotated and k, v are already in the caches.
 cudaError_t decoder_self_attention(const float *qkv, const int32_t *step, const float *q_norm,
                                    const float *k_norm, const float *rope_cos, const float *rope_sin, float *kc,
-                                   float *vc, int cap, int B, float *out, AttnDims a, cudaStream_t st);
+                                   float *vc, int cap, int B, float *out, AttnDims a, cudaStream_t st,
+                                   void *hi = nullptr, void *lo = nullptr, int64_t ldp = 0, bool prepared = false);
 
 // Decoder cross-attention (attn.rs:281-337): q [B, H*HD] (q_norm applied
 // here), K/V of request b at rows seq_off[b].. of kplane / vplane
-// [*, KVH*HD].  out: [B, H*HD].
+// [*, KVH*HD].  out: [B, H*HD] f32, or the bf16 hi/lo planes as for
+// decoder_self_attention.
 cudaError_t decoder_cross_attention(const float *q, const float *q_norm, const float *kplane,
                                     const float *vplane, const int64_t *seq_off, int B, float *out, AttnDims a,
-                                    cudaStream_t st, int max_len);
+                                    cudaStream_t st, int max_len, void *hi = nullptr, void *lo = nullptr,
+                                    int64_t ldp = 0);
 
 // Output head (model.rs:89-149) + additive mask (engine.rs:294-297) + argmax
 // (engine.rs:299-304), fused.  h: [B, d]; emb: [V, d].  Request b is at step

@@ -141,13 +141,16 @@ __device__ __forceinline__ void epi_row(const TcEpi &e, int m, int n0, float *v)
   }
 }
 
-// EPI_QKV on the 64 columns (one head) n0.. of row m: ZCRMSNorm + RoPE for
-// Q and K heads (attn.rs:218-235), then bf16 hi/lo into the attention planes.
+// EPI_QKV / EPI_QKV_DEC on the 64 columns (one head) n0.. of row m:
+// ZCRMSNorm + RoPE for Q and K heads (attn.rs:218-235, 120-140), then either
+// bf16 hi/lo into the encoder attention planes or, for a decoder step, Q as
+// f32 and K, V appended to the self-attention caches.
 __device__ __forceinline__ void epi_qkv64(const TcEpi &e, int m, int n0, float *v) {
   const MatmulOut &o = e.o;
   const int hh = n0 >> 6, H = o.heads_q, KVH = o.heads_kv;
   int plane;
   int64_t base;
+  const bool dec = o.epi == EPI_QKV_DEC;
   if (hh < H + KVH) {
     const float4 *sc = reinterpret_cast<const float4 *>(hh < H ? o.q_norm : o.k_norm);
     float ss = 0.0f;
@@ -184,6 +187,21 @@ __device__ __forceinline__ void epi_qkv64(const TcEpi &e, int m, int n0, float *
   } else {
     plane = 4;
     base = ((int64_t)(hh - H - KVH) * o.slab + m) * 64;
+  }
+  if (dec) {
+    float *dst;
+    if (hh < H) {
+      dst = o.y + (int64_t)m * o.ldy + hh * 64;
+    } else {
+      const int p = o.pos[m];
+      if (p >= o.cache_cap) return;  // cache full: nothing appended
+      dst = (hh < H + KVH ? o.kcache : o.vcache) + ((int64_t)m * o.cache_cap + p) * (KVH * 64) +
+            (hh < H + KVH ? hh - H : hh - H - KVH) * 64;
+    }
+    float4 *d4 = reinterpret_cast<float4 *>(dst);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) d4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    return;
   }
   uint4 *dh = reinterpret_cast<uint4 *>((__nv_bfloat16 *)o.planes[plane] + base);
   uint4 *dl = reinterpret_cast<uint4 *>((__nv_bfloat16 *)o.planes[plane + 1] + base);
@@ -237,7 +255,8 @@ __device__ __forceinline__ unsigned long long epi_argmax32(const TcEpi &e, int m
 __device__ __forceinline__ void epi_tile(const TcEpi &e, int M, int N, int m, uint32_t base, int c0, int c1,
                                          int n_base) {
   const bool amax = e.o.epi == EPI_ARGMAX;
-  const bool wide = e.o.epi == EPI_KNORM || e.o.epi == EPI_QKV;  // whole 64-column heads
+  const bool qkv = e.o.epi == EPI_QKV || e.o.epi == EPI_QKV_DEC;
+  const bool wide = e.o.epi == EPI_KNORM || qkv;  // whole 64-column heads
   unsigned long long best = 0ull;
   for (int c = c0; c < c1; c += (wide ? 64 : 32)) {
     float v[64];
@@ -248,7 +267,7 @@ __device__ __forceinline__ void epi_tile(const TcEpi &e, int M, int N, int m, ui
       if (amax) {
         unsigned long long k = epi_argmax32(e, m, n0, v);
         best = k > best ? k : best;
-      } else if (e.o.epi == EPI_QKV) {
+      } else if (qkv) {
         epi_qkv64(e, m, n0, v);
       } else if (wide) {
         epi_row<64>(e, m, n0, v);
@@ -687,6 +706,11 @@ cudaError_t tc_matmul(const TcPlanes &A, int M, const TcPlanes &B, int N, const 
       return cudaErrorInvalidValue;
     for (int i = 0; i < 6; ++i)
       if (!o.planes[i] || ((uintptr_t)o.planes[i] % 16)) return cudaErrorInvalidValue;
+  } else if (o.epi == EPI_QKV_DEC) {
+    if (N != (o.heads_q + 2 * o.heads_kv) * 64 || !o.pos || !o.q_norm || !o.k_norm || !o.rope_cos || !o.rope_sin ||
+        !o.kcache || !o.vcache || o.cache_cap <= 0 || (o.ldy % 4) || ((uintptr_t)o.y % 16) ||
+        ((uintptr_t)o.kcache % 16) || ((uintptr_t)o.vcache % 16))
+      return cudaErrorInvalidValue;
   } else if ((o.ldy % 4) || ((uintptr_t)o.y % 16) || (o.col_block && (o.block_stride % 4))) {
     return cudaErrorInvalidValue;
   }

@@ -339,6 +339,26 @@ def test_batched_decode_tensor_core_vs_oracle(full):
         assert close(lg[r, 0], rlg[0]), max_excess(lg[r, 0], rlg[0])
 
 
+def test_long_decode_vs_oracle(full):
+    # 72 greedy steps: the decoder self-attention passes over more than 64
+    # cached positions, on the 136-request path (attention output written as
+    # the output projection's operand planes) and on the single-request path.
+    eng, ref = full
+    ids_in, off = wl.random_prompts(136, 8, 40, 8192, seed=15)
+    prompts = [ids_in[off[i]:off[i + 1]] for i in range(136)]
+    steps = 72
+    ids, lens, lg = eng.run_batch_ids(prompts, steps, want_logits=True)
+    one, _, lg1 = eng.run_batch_ids([prompts[3]], steps, want_logits=True)
+    tol = 2 * (ATOL + RTOL * 10.0)
+    for r, got, glg in ((0, ids[0], lg[0]), (3, ids[3], lg[3]), (135, ids[135], lg[135]), (3, one[0], lg1[0])):
+        rid, rmarg, rlg = ref.generate(prompts[r], steps, want_logits=True)
+        assert tokens_match(got, rid, rmarg, tol), r
+        for s in range(steps):
+            if got[:s].tolist() != rid[:s].tolist():
+                break
+            assert close(glg[s], rlg[s]), (r, s, max_excess(glg[s], rlg[s]))
+
+
 def test_wide_prefill_tiles_vs_oracle(full):
     # Over 9,500 prompt rows: every prefill projection (the fused QKV with its
     # norm + RoPE epilogue included) runs with 128 x 256 output tiles.

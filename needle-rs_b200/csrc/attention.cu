@@ -558,7 +558,9 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_al
 
 // Decoder self-attention for one new token per request, head dim 64, two
 // query heads per KV head (attn.rs:100-183).  CTA = (request, KV head), 128
-// threads, the context in passes of 64 cache rows:
+// threads, the context in passes of CH (16, 32 or 64) cache rows; the host
+// picks the smallest CH that holds the step's context, so the shared memory
+// a CTA holds, and with it the CTAs resident per SM, follows the context:
 //   * every thread first starts asynchronous 16-byte copies of the pass's
 //     K and V rows into shared memory (K rows padded to 68 floats, so a
 //     thread reading a whole row meets no bank conflict);
@@ -576,12 +578,13 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_al
 //     the end.
 // The result goes to out [B, H*64] f32, or, when hi is set, straight to the
 // bf16 hi/lo operand planes (row stride ldp) of the output projection.
-template <bool PREP>
-__global__ void __launch_bounds__(128) self_attn_step_kernel(
+template <bool PREP, int CH>
+__global__ void __launch_bounds__(128, CH == 16 ? 12 : CH == 32 ? 10 : 6) self_attn_step_kernel(
     const float *__restrict__ qkv, const int32_t *__restrict__ step, const float *__restrict__ qn,
     const float *__restrict__ kn, const float *__restrict__ rc, const float *__restrict__ rs, float *kc, float *vc,
     int cap, float *out, __nv_bfloat16 *hi, __nv_bfloat16 *lo, int64_t ldp, AttnDims a) {
-  constexpr int HD = 64, REP = 2, CH = 64, KP = HD + 4;
+  constexpr int HD = 64, REP = 2, KP = HD + 4;
+  static_assert(CH == 16 || CH == 32 || CH == 64, "pass size");
   __shared__ __align__(16) float ks[CH][KP];
   __shared__ __align__(16) float vs[CH][HD];
   __shared__ __align__(16) float qs[REP][HD];
@@ -603,7 +606,7 @@ __global__ void __launch_bounds__(128) self_attn_step_kernel(
   auto fetch = [&](int c0) {
     const int c = tid & 15;
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
+    for (int u = 0; u < CH / 8; ++u) {
       const int r = (tid >> 4) + 8 * u, t = c0 + r;
       if (t < cached) {
         cp_async16(&ks[r][4 * c], kcb + (int64_t)t * kvd + 4 * c);
@@ -658,7 +661,7 @@ __global__ void __launch_bounds__(128) self_attn_step_kernel(
     float sc = -INFINITY;
     {
       const int t = c0 + sr_;
-      if (t < total) {
+      if (sr_ < CH && t < total) {
         const float *kp = (PREP && append && t == pos) ? knew : ks[sr_];
         const float *q = qs[sj];
         float d = 0.0f;
@@ -684,8 +687,8 @@ __global__ void __launch_bounds__(128) self_attn_step_kernel(
       corr[j] = expf(m[j] - mn);  // 0 on the first pass (m = -inf)
       m[j] = mn;
     }
-    const float p = c0 + sr_ < total ? expf(sc - (sj ? m[1] : m[0])) : 0.0f;
-    reinterpret_cast<float *>(&ps[sr_])[sj] = p;
+    const float p = sr_ < CH && c0 + sr_ < total ? expf(sc - (sj ? m[1] : m[0])) : 0.0f;
+    if (sr_ < CH) reinterpret_cast<float *>(&ps[sr_])[sj] = p;
     const float wsm = warp_sum(p);
     if (lane == 0) wsum[warp] = wsm;
     __syncthreads();
@@ -696,7 +699,7 @@ __global__ void __launch_bounds__(128) self_attn_step_kernel(
       for (int e = 0; e < 4; ++e) acc[j][e] *= corr[j];
     }
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
+    for (int u = 0; u < CH / 8; ++u) {
       const int r = rg + 8 * u, t = c0 + r;
       if (t >= total) break;
       const float4 v4 = (PREP && append && t == pos) ? *reinterpret_cast<const float4 *>(&vnew[4 * dq])
@@ -862,17 +865,25 @@ cudaError_t encoder_attention(const float *qkv, const int64_t *seq_off, int n_re
 cudaError_t decoder_self_attention(const float *qkv, const int32_t *step, const float *q_norm,
                                    const float *k_norm, const float *rope_cos, const float *rope_sin, float *kc,
                                    float *vc, int cap, int B, float *out, AttnDims a, cudaStream_t st, void *hi_,
-                                   void *lo_, int64_t ldp, bool prepared) {
+                                   void *lo_, int64_t ldp, bool prepared, int max_rows) {
   __nv_bfloat16 *hi = static_cast<__nv_bfloat16 *>(hi_), *lo = static_cast<__nv_bfloat16 *>(lo_);
   if (B <= 0) return cudaSuccess;
   if (a.HD > 128 || (a.HD & 1) || cap <= 0) return cudaErrorInvalidValue;
   if (a.HD == 64 && a.H == 2 * a.KVH) {
-    if (prepared)
-      self_attn_step_kernel<false><<<dim3(a.KVH, B), 128, 0, st>>>(qkv, step, q_norm, k_norm, rope_cos, rope_sin,
-                                                                   kc, vc, cap, out, hi, lo, ldp, a);
+    const dim3 grid(a.KVH, B);
+    const int rows = max_rows > 0 && max_rows < cap ? max_rows : cap;
+    if (prepared && rows <= 16)
+      self_attn_step_kernel<false, 16><<<grid, 128, 0, st>>>(qkv, step, q_norm, k_norm, rope_cos, rope_sin, kc, vc,
+                                                              cap, out, hi, lo, ldp, a);
+    else if (prepared && rows <= 32)
+      self_attn_step_kernel<false, 32><<<grid, 128, 0, st>>>(qkv, step, q_norm, k_norm, rope_cos, rope_sin, kc, vc,
+                                                              cap, out, hi, lo, ldp, a);
+    else if (prepared)
+      self_attn_step_kernel<false, 64><<<grid, 128, 0, st>>>(qkv, step, q_norm, k_norm, rope_cos, rope_sin, kc, vc,
+                                                              cap, out, hi, lo, ldp, a);
     else
-      self_attn_step_kernel<true><<<dim3(a.KVH, B), 128, 0, st>>>(qkv, step, q_norm, k_norm, rope_cos, rope_sin, kc,
-                                                                  vc, cap, out, hi, lo, ldp, a);
+      self_attn_step_kernel<true, 64><<<grid, 128, 0, st>>>(qkv, step, q_norm, k_norm, rope_cos, rope_sin, kc, vc,
+                                                             cap, out, hi, lo, ldp, a);
     return cudaGetLastError();
   }
   if (hi || prepared) return cudaErrorInvalidValue;

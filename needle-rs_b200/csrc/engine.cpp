@@ -486,7 +486,8 @@ Batch::~Batch() {
   int prev = 0;
   cudaGetDevice(&prev);
   cudaSetDevice(m_->device);
-  if (graph_) cudaGraphExecDestroy(graph_);
+  for (auto &g : graphs_)
+    if (g) cudaGraphExecDestroy(g);
   if (st_) cudaStreamSynchronize(st_);
   for (auto &e : timed_) {
     cudaEventDestroy(e.a);
@@ -917,7 +918,7 @@ bool Batch::prefill(std::string &err) {
   return true;
 }
 
-bool Batch::decode_step(std::string &err, bool capture) {
+bool Batch::decode_step(std::string &err, bool capture, int att_rows) {
   const DevModel &m = *m_;
   const Config &c = m.cfg;
   const int B = spec_.n_req, d = c.d_model, hd = c.head_dim(), qd = c.num_heads * hd, kvd = c.num_kv_heads * hd;
@@ -966,7 +967,7 @@ bool Batch::decode_step(std::string &err, bool capture) {
     }
     if (!mm_in(TIME_DECODE_MATMUL, capture, pd, xn_, d, B, D.sa_qkv, o, err)) return false;
     NDL_TK(TIME_SELF_ATTENTION, capture, decoder_self_attention(qkv_, pos_, D.sa_qn, D.sa_kn, m.rope_cos, m.rope_sin, self_k_ + coff,
-                                  self_v_ + coff, cap_, B, att_, m.ad, st, ahi, alo, aldp, prep));
+                                  self_v_ + coff, cap_, B, att_, m.ad, st, ahi, alo, aldp, prep, att_rows));
     MatmulOut r;
     r.y = x_;
     r.ldy = d;
@@ -1049,12 +1050,16 @@ bool Batch::begin(std::string &err) {
   timed_.clear();
   if (!reset_decoder(err) || !prefill(err)) return false;
   use_graph_ = !(spec_.flags & BATCH_NO_GRAPH) && !timed_cls_ && spec_.max_new > 0;
-  if (use_graph_ && !graph_) {
+  // one graph per self-attention row bound the steps of this batch reach
+  for (int s = 0; use_graph_ && s < spec_.max_new; ++s) {
+    const int rows = att_rows(s);
+    cudaGraphExec_t &ge = graphs_[att_slot(rows)];
+    if (ge) continue;
     cudaStream_t st = st_;
     int64_t before = launches_;
     NDL_CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
     std::string cerr;
-    bool ok = decode_step(cerr, true);
+    bool ok = decode_step(cerr, true, rows);
     cudaGraph_t g = nullptr;
     cudaError_t ce = cudaStreamEndCapture(st, &g);
     if (!ok || ce != cudaSuccess) {
@@ -1062,9 +1067,10 @@ bool Batch::begin(std::string &err) {
       err = ok ? std::string("graph capture failed: ") + cudaGetErrorString(ce) : cerr;
       return false;
     }
-    cudaError_t ie = cudaGraphInstantiate(&graph_, g, 0);
+    cudaError_t ie = cudaGraphInstantiate(&ge, g, 0);
     cudaGraphDestroy(g);
     if (ie != cudaSuccess) {
+      ge = nullptr;
       err = std::string("graph instantiate failed: ") + cudaGetErrorString(ie);
       return false;
     }
@@ -1080,9 +1086,9 @@ bool Batch::step(std::string &err) {
     return false;
   }
   if (use_graph_) {
-    NDL_CK(cudaGraphLaunch(graph_, st_));
+    NDL_CK(cudaGraphLaunch(graphs_[att_slot(att_rows(steps_done_))], st_));
     launches_ += step_launches_;
-  } else if (!decode_step(err, false)) {
+  } else if (!decode_step(err, false, att_rows(steps_done_))) {
     return false;
   }
   ++steps_done_;

@@ -174,7 +174,17 @@ class Batch {
  private:
   bool prefill(std::string &err);
   bool reset_decoder(std::string &err);
-  bool decode_step(std::string &err, bool capture);
+  // One decode step.  att_rows: no request attends over more self-attention
+  // rows in this step (sizes the self-attention kernel's pass).
+  bool decode_step(std::string &err, bool capture, int att_rows);
+  // Self-attention row bound of decode step `step` and its graph slot: every
+  // request is at most at position `step`, so it attends over at most
+  // min(step + 1, cap) rows; the bound is rounded up to 16, 32 or cap.
+  int att_rows(int step) const {
+    const int r = step + 1 < cap_ ? step + 1 : cap_;
+    return r <= 16 ? 16 : r <= 32 ? 32 : cap_;
+  }
+  static int att_slot(int rows) { return rows <= 16 ? 0 : rows <= 32 ? 1 : 2; }
   bool mm(int cls, bool capture, const float *x, int64_t ldx, int M, const Lin &w, const MatmulOut &o,
           std::string &err);
   bool mm_in(int cls, bool capture, const TcPlanes *planes, const float *x, int64_t ldx, int M, const Lin &w,
@@ -226,7 +236,7 @@ class Batch {
   uint8_t *done_ = nullptr;
   unsigned int *n_done_ = nullptr;
   float *logits_ = nullptr;
-  cudaGraphExec_t graph_ = nullptr;
+  cudaGraphExec_t graphs_[3] = {nullptr, nullptr, nullptr};  // decode step, by att_slot
   bool use_graph_ = false;
   uint32_t *first_ids_ = nullptr;
   int steps_done_ = 0;

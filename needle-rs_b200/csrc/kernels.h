@@ -190,10 +190,13 @@ cudaError_t encoder_attention(const float *qkv, const int64_t *seq_off, int n_re
 // of the next tensor-core matmul, row stride ldp elements.  `prepared`
 // (same head layout): the QKV projection ran with EPI_QKV_DEC, so q in qkv is
 // already normed and rotated and k, v are already in the caches.
+// max_rows > 0: no request attends over more rows than that (step[b] + 1 <=
+// max_rows); it sizes the kernel's pass.
 cudaError_t decoder_self_attention(const float *qkv, const int32_t *step, const float *q_norm,
                                    const float *k_norm, const float *rope_cos, const float *rope_sin, float *kc,
                                    float *vc, int cap, int B, float *out, AttnDims a, cudaStream_t st,
-                                   void *hi = nullptr, void *lo = nullptr, int64_t ldp = 0, bool prepared = false);
+                                   void *hi = nullptr, void *lo = nullptr, int64_t ldp = 0, bool prepared = false,
+                                   int max_rows = 0);
 
 // Decoder cross-attention (attn.rs:281-337): q [B, H*HD] (q_norm applied
 // here), K/V of request b at rows seq_off[b].. of kplane / vplane

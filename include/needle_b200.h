@@ -44,6 +44,8 @@ int needle_handle_device(NeedleHandle *handle);
 #define NEEDLE_STOP_ON_EOS 1u     /* end a request at EOS, as run_impl does (engine.rs:306-308) */
 #define NEEDLE_DEVICE_POINTERS 2u /* prompt_ids / mask_bits / outputs are device pointers */
 #define NEEDLE_NO_GRAPH 4u        /* launch decode steps one kernel at a time (no CUDA graph) */
+#define NEEDLE_NO_PDL 8u          /* decode kernels wait for their predecessor to finish before they launch
+                                     (no programmatic dependent launch); results are the same either way */
 
 /* Greedy generation for n_req independent requests (run_batch,
  * engine.rs:142-144, with the decode loop of engine.rs:286-322 on IDs):

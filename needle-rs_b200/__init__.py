@@ -20,6 +20,7 @@ LIB_PATH = os.path.join(HERE, "libneedle_c.so")
 STOP_ON_EOS = 1
 DEVICE_POINTERS = 2
 NO_GRAPH = 4
+NO_PDL = 8
 
 _lib = None
 
@@ -249,7 +250,8 @@ class NeedleEngine:
         return s
 
     # ── token-ID level ──
-    def run_batch_ids(self, prompts, max_new, mask_bits=None, stop_on_eos=False, want_logits=False, graph=True):
+    def run_batch_ids(self, prompts, max_new, mask_bits=None, stop_on_eos=False, want_logits=False, graph=True,
+                      pdl=True):
         """Greedy generation for a list of prompts (lists of token ids).
 
         mask_bits: None or uint64 [n_req, max_new, ceil(V/64)].  Returns
@@ -259,7 +261,7 @@ class NeedleEngine:
         out = np.zeros((n, max_new), np.uint32)
         lens = np.zeros(n, np.uint32)
         mb = None if mask_bits is None else np.ascontiguousarray(mask_bits, np.uint64)
-        flags = (STOP_ON_EOS if stop_on_eos else 0) | (0 if graph else NO_GRAPH)
+        flags = (STOP_ON_EOS if stop_on_eos else 0) | (0 if graph else NO_GRAPH) | (0 if pdl else NO_PDL)
         if want_logits:
             lg = np.zeros((n, max_new, self.cfg["vocab_size"]), np.float32)
             _check(lib().needle_run_batch_ids_logits(self._h, _p(ids), _p(off), n, max_new, _p(mb), flags,

@@ -10,6 +10,13 @@
 #include "kernels.h"
 
 namespace ndl {
+
+namespace {
+thread_local bool g_pdl = false;
+}
+void set_pdl(bool on) { g_pdl = on; }
+bool pdl_on() { return g_pdl; }
+
 namespace {
 
 // ── ZCRMSNorm rows (norm.rs:23-30) ─────────────────────────────────────────
@@ -58,6 +65,8 @@ __global__ void rms_norm_kernel(const float *__restrict__ x, int64_t ldx, float 
 __global__ void rms_norm_planes_kernel(const float *__restrict__ x, int64_t ldx, __nv_bfloat16 *hi, __nv_bfloat16 *lo,
                                        int64_t ldp, float *out, int64_t ldo, const float *__restrict__ scale,
                                        int rows) {
+  pdl_trigger();
+  pdl_wait();
   int row = (int)(((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
   if (row >= rows) return;
   const float *xr = x + (int64_t)row * ldx;
@@ -523,6 +532,8 @@ __global__ void __launch_bounds__(256) cross_attn_kernel(const float *__restrict
                                                          AttnDims a) {
   constexpr int HD = 64;
   extern __shared__ __align__(16) float sm[];
+  pdl_trigger();
+  pdl_wait();
   const int b = blockIdx.y, g = blockIdx.x;
   const int64_t off = seq_off[b];
   const int T = (int)(seq_off[b + 1] - off);
@@ -592,6 +603,8 @@ __global__ void __launch_bounds__(128, CH == 16 ? 12 : CH == 32 ? 10 : 6) self_a
   __shared__ __align__(8) float2 ps[CH];  // (head 0, head 1) weights of a row
   __shared__ float wmax[4], wsum[4];
   float(*part)[REP][HD] = reinterpret_cast<float(*)[REP][HD]>(&vs[0][0]);  // after the last pass
+  pdl_trigger();
+  pdl_wait();
   const int b = blockIdx.y, g = blockIdx.x;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int qd = a.H * HD, kvd = a.KVH * HD, ld = qd + 2 * kvd;
@@ -829,9 +842,8 @@ cudaError_t rms_norm_planes(const float *x, int64_t ldx, void *hi, void *lo, int
   if (rows <= 0) return cudaSuccess;
   if (d != 512 || (ldx & 3) || (ldp & 3) || (out && (ldo & 3))) return cudaErrorInvalidValue;
   int64_t threads = (int64_t)rows * 32;
-  rms_norm_planes_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(
-      x, ldx, (__nv_bfloat16 *)hi, (__nv_bfloat16 *)lo, ldp, out, ldo, scale, rows);
-  return cudaGetLastError();
+  return launch(rms_norm_planes_kernel, dim3((unsigned)((threads + 255) / 256)), dim3(256), 0, st, x, ldx,
+                (__nv_bfloat16 *)hi, (__nv_bfloat16 *)lo, ldp, out, ldo, scale, rows);
 }
 
 cudaError_t embed_rows(const uint32_t *ids, const float *emb, float *x, int rows, int d, float es,
@@ -872,19 +884,12 @@ cudaError_t decoder_self_attention(const float *qkv, const int32_t *step, const 
   if (a.HD == 64 && a.H == 2 * a.KVH) {
     const dim3 grid(a.KVH, B);
     const int rows = max_rows > 0 && max_rows < cap ? max_rows : cap;
-    if (prepared && rows <= 16)
-      self_attn_step_kernel<false, 16><<<grid, 128, 0, st>>>(qkv, step, q_norm, k_norm, rope_cos, rope_sin, kc, vc,
-                                                              cap, out, hi, lo, ldp, a);
-    else if (prepared && rows <= 32)
-      self_attn_step_kernel<false, 32><<<grid, 128, 0, st>>>(qkv, step, q_norm, k_norm, rope_cos, rope_sin, kc, vc,
-                                                              cap, out, hi, lo, ldp, a);
-    else if (prepared)
-      self_attn_step_kernel<false, 64><<<grid, 128, 0, st>>>(qkv, step, q_norm, k_norm, rope_cos, rope_sin, kc, vc,
-                                                              cap, out, hi, lo, ldp, a);
-    else
-      self_attn_step_kernel<true, 64><<<grid, 128, 0, st>>>(qkv, step, q_norm, k_norm, rope_cos, rope_sin, kc, vc,
-                                                             cap, out, hi, lo, ldp, a);
-    return cudaGetLastError();
+    auto k = prepared ? (rows <= 16   ? self_attn_step_kernel<false, 16>
+                         : rows <= 32 ? self_attn_step_kernel<false, 32>
+                                      : self_attn_step_kernel<false, 64>)
+                      : self_attn_step_kernel<true, 64>;
+    return launch(k, grid, dim3(128), 0, st, qkv, step, q_norm, k_norm, rope_cos, rope_sin, kc, vc, cap, out, hi, lo,
+                  ldp, a);
   }
   if (hi || prepared) return cudaErrorInvalidValue;
   size_t sm = ((size_t)a.H * a.HD + (size_t)a.H * cap) * sizeof(float);
@@ -902,8 +907,8 @@ cudaError_t decoder_cross_attention(const float *q, const float *q_norm, const f
   if (a.HD == 64 && rep == 2) {
     size_t sm = ((size_t)rep * 64 + (size_t)16 * rep * 64 + (size_t)rep * max_len) * sizeof(float);
     if (sm > kMaxDynSmem) return cudaErrorInvalidValue;
-    cross_attn_kernel<2><<<dim3(a.KVH, B), 256, sm, st>>>(q, q_norm, kplane, vplane, seq_off, out, hi, lo, ldp, a);
-    return cudaGetLastError();
+    return launch(cross_attn_kernel<2>, dim3(a.KVH, B), dim3(256), sm, st, q, q_norm, kplane, vplane, seq_off, out, hi,
+                  lo, ldp, a);
   }
   if (hi) return cudaErrorInvalidValue;
   if (a.HD > 128 || (a.HD & 1)) return cudaErrorInvalidValue;

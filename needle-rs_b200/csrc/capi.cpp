@@ -144,6 +144,7 @@ bool make_spec(NeedleHandle *h, const uint32_t *ids, const uint64_t *off, size_t
   if (flags & NEEDLE_STOP_ON_EOS) f |= BATCH_STOP_ON_EOS;
   if (flags & NEEDLE_DEVICE_POINTERS) f |= BATCH_DEVICE_INPUTS;
   if (flags & NEEDLE_NO_GRAPH) f |= BATCH_NO_GRAPH;
+  if (flags & NEEDLE_NO_PDL) f |= BATCH_NO_PDL;
   s.flags = f;
   return true;
 }

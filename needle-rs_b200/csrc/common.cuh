@@ -35,4 +35,36 @@ __device__ __forceinline__ int sign_extend4(uint32_t nib) {
   return (int)(nib << 28) >> 28;
 }
 
+// Programmatic dependent launch.  pdl_trigger lets the next kernel of the
+// stream start its CTAs; pdl_wait blocks until the previous kernel of the
+// stream has completed and its writes are visible.  Both are no-ops in a
+// kernel launched without the programmatic-serialization attribute.  A kernel
+// launched with it calls pdl_wait before its first global-memory access.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Whether launches from this host thread currently use programmatic
+// dependent launch (set_pdl in kernels.h).
+bool pdl_on();
+
+// <<<grid, block, smem, st>>> launch, with the programmatic-serialization
+// attribute while pdl_on().
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                          Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  if (pdl_on()) {
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+  }
+  return cudaLaunchKernelEx(&cfg, k, static_cast<Args &&>(args)...);
+}
+
 }  // namespace ndl

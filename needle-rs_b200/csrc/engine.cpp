@@ -919,6 +919,12 @@ bool Batch::prefill(std::string &err) {
 }
 
 bool Batch::decode_step(std::string &err, bool capture, int att_rows) {
+  // the step's kernels start during their predecessor's tail (each waits for
+  // it before touching global memory)
+  struct PdlScope {
+    explicit PdlScope(bool on) { set_pdl(on); }
+    ~PdlScope() { set_pdl(false); }
+  } pdl_scope(!(spec_.flags & BATCH_NO_PDL));
   const DevModel &m = *m_;
   const Config &c = m.cfg;
   const int B = spec_.n_req, d = c.d_model, hd = c.head_dim(), qd = c.num_heads * hd, kvd = c.num_kv_heads * hd;

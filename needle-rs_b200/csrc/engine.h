@@ -113,6 +113,7 @@ enum BatchFlags : uint32_t {
   BATCH_STOP_ON_EOS = 1u,     // engine.rs:306-308: stop a request at EOS
   BATCH_DEVICE_INPUTS = 2u,   // prompt ids / masks are device pointers
   BATCH_NO_GRAPH = 4u,        // launch each decode step eagerly
+  BATCH_NO_PDL = 8u,          // no programmatic dependent launch in the decode step
 };
 
 struct BatchSpec {

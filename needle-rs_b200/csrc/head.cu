@@ -197,6 +197,8 @@ __global__ void finish_step_kernel(unsigned long long *keys, int B, int max_new,
                                    uint32_t *out_ids, uint32_t *lens, uint8_t *done, int32_t *pos,
                                    unsigned int *n_done, const uint32_t *__restrict__ teacher,
                                    const float *__restrict__ emb, float *x, int d, float es) {
+  pdl_trigger();
+  pdl_wait();
   int b = (int)(((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
   if (b >= B) return;
   unsigned long long k = keys[b];
@@ -268,9 +270,8 @@ cudaError_t finish_step(unsigned long long *keys, int B, int max_new, int stop_o
                         const float *emb, float *x, int d, float embed_scale, cudaStream_t st) {
   if (B <= 0) return cudaSuccess;
   int64_t threads = (int64_t)B * 32;
-  finish_step_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(
-      keys, B, max_new, stop_on_eos, out_ids, lens, done, pos, n_done, teacher, emb, x, d, embed_scale);
-  return cudaGetLastError();
+  return launch(finish_step_kernel, dim3((unsigned)((threads + 255) / 256)), dim3(256), 0, st, keys, B, max_new,
+                stop_on_eos, out_ids, lens, done, pos, n_done, teacher, emb, x, d, embed_scale);
 }
 
 

@@ -164,6 +164,12 @@ cudaError_t embed_rows(const uint32_t *ids, const float *emb, float *x, int rows
 // Largest dynamic shared memory any kernel here is allowed to request.
 constexpr int kMaxDynSmem = 200 * 1024;
 
+// Launches of the decode-step kernels (norm, tensor-core matmul, decoder
+// attention, finish_step) made by this host thread use programmatic dependent
+// launch while on: each such kernel lets its successor's CTAs start during its
+// own tail and waits for its predecessor before touching global memory.
+void set_pdl(bool on);
+
 // Set per-device kernel attributes.  Call once per device, with it current.
 cudaError_t init_kernels();
 cudaError_t init_matmul_kernels();

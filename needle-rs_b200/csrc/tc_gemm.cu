@@ -299,6 +299,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_m = (M + TC_BM - 1) / TC_BM, num_n = (N + BN - 1) / BN;
   const int tiles = num_m * num_n, nkb = Kp / TC_BK;
+  pdl_trigger();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < TC_STAGES; ++s) {
@@ -320,6 +321,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *(volatile uint32_t *)tmem_slot;
+  // under programmatic dependent launch the setup above overlaps the previous
+  // kernel's tail; global memory is touched only after it has completed
+  pdl_wait();
 
   if (warp < 4) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(TC_REG_PRODUCER));
@@ -759,17 +763,12 @@ cudaError_t tc_matmul(const TcPlanes &A, int M, const TcPlanes &B, int N, const 
     return cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<TC_PAIR_STAGES>, *ah, *al, *bh, *bl, M, N, A.Kp, e, err,
                               b_lo_zero ? 1 : 0);
   }
-  if (tiles256 >= 2 * sms) {
-    const int grid = sms;
-    tc_gemm_kernel<256, 2><<<grid, TC_THREADS, tc_smem_bytes(256, 2), st>>>(*ah, *al, *bh, *bl, M, N, A.Kp, e, err,
-                                                                           b_lo_zero ? 1 : 0);
-  } else {
-    const int tiles = num_m * ((N + 127) / 128);
-    const int grid = tiles < sms ? tiles : sms;
-    tc_gemm_kernel<128, 3><<<grid, TC_THREADS, tc_smem_bytes(128, 3), st>>>(*ah, *al, *bh, *bl, M, N, A.Kp, e, err,
-                                                                           b_lo_zero ? 1 : 0);
-  }
-  return cudaGetLastError();
+  if (tiles256 >= 2 * sms)
+    return launch(tc_gemm_kernel<256, 2>, dim3(sms), dim3(TC_THREADS), tc_smem_bytes(256, 2), st, *ah, *al, *bh, *bl, M,
+                  N, A.Kp, e, err, b_lo_zero ? 1 : 0);
+  const int tiles = num_m * ((N + 127) / 128);
+  return launch(tc_gemm_kernel<128, 3>, dim3(tiles < sms ? tiles : sms), dim3(TC_THREADS), tc_smem_bytes(128, 3), st,
+                *ah, *al, *bh, *bl, M, N, A.Kp, e, err, b_lo_zero ? 1 : 0);
 }
 
 cudaError_t init_tc_kernels() {

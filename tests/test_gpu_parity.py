@@ -359,6 +359,21 @@ def test_long_decode_vs_oracle(full):
             assert close(glg[s], rlg[s]), (r, s, max_excess(glg[s], rlg[s]))
 
 
+def test_pdl_and_graphs_change_nothing(full):
+    # Programmatic dependent launch and the step graphs only change when
+    # kernels start: tokens and logits are bit-identical with and without
+    # them (20 steps: the self-attention pass sizes 16 and 32 both run).
+    eng, _ = full
+    ids_in, off = wl.random_prompts(144, 8, 80, 8192, seed=16)
+    prompts = [ids_in[off[i]:off[i + 1]] for i in range(144)]
+    masks = wl.random_masks(144, 20, 8192, 0.05, seed=17)
+    ref = eng.run_batch_ids(prompts, 20, mask_bits=masks, want_logits=True, graph=False, pdl=False)
+    for graph, pdl in ((True, True), (False, True), (True, False)):
+        got = eng.run_batch_ids(prompts, 20, mask_bits=masks, want_logits=True, graph=graph, pdl=pdl)
+        assert np.array_equal(got[0], ref[0]) and np.array_equal(got[1], ref[1]), (graph, pdl)
+        assert np.array_equal(got[2], ref[2]), (graph, pdl)
+
+
 def test_wide_prefill_tiles_vs_oracle(full):
     # Over 9,500 prompt rows: every prefill projection (the fused QKV with its
     # norm + RoPE epilogue included) runs with 128 x 256 output tiles.

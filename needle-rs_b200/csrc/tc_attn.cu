@@ -189,6 +189,42 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// Packed pairs of f32 (sm_100 two-lane FMA / add / sub / mul: each lane
+// rounds exactly as the scalar instruction) and the three-input maximum.
+__device__ __forceinline__ uint64_t f2pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2unpack(uint64_t v, float &a, float &b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fsub2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 // bf16 hi/lo split of two probabilities, packed as two bf16 per word (the
 // lower key in the low half, as the TS-form MMA reads K).
 __device__ __forceinline__ void split2(float p0, float p1, uint32_t &hi, uint32_t &lo) {
@@ -205,27 +241,38 @@ __device__ __forceinline__ void split2(float p0, float p1, uint32_t &hi, uint32_
 // and beyond get probability 0.
 template <bool MASK>
 __device__ __forceinline__ float p_row(const uint32_t *sr, float c, float m, int kvalid, uint32_t tS) {
-  float ps0 = 0.0f, ps1 = 0.0f;
+  // even and odd keys summed in the two lanes of ps, in key order
+  uint64_t ps = f2pack(0.0f, 0.0f);
+  const uint64_t cc = f2pack(c, c), nm = f2pack(-m, -m);
 #pragma unroll
   for (int ch = 0; ch < 4; ++ch) {
     uint32_t hw[16], lw[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
       const int k0 = ch * 32 + 2 * i;
-      float p0 = ex2(fmaf(__uint_as_float(sr[k0]), c, -m));
-      float p1 = ex2(fmaf(__uint_as_float(sr[k0 + 1]), c, -m));
+      float t0, t1;
+      f2unpack(ffma2(f2pack(__uint_as_float(sr[k0]), __uint_as_float(sr[k0 + 1])), cc, nm), t0, t1);
+      float p0 = ex2(t0), p1 = ex2(t1);
       if (MASK) {
         p0 = k0 < kvalid ? p0 : 0.0f;
         p1 = k0 + 1 < kvalid ? p1 : 0.0f;
       }
-      ps0 += p0;
-      ps1 += p1;
-      split2(p0, p1, hw[i], lw[i]);
+      const uint64_t p2 = f2pack(p0, p1);
+      ps = fadd2(ps, p2);
+      const __nv_bfloat162 h = __floats2bfloat162_rn(p0, p1);
+      const uint32_t hb = *reinterpret_cast<const uint32_t *>(&h);
+      float l0, l1;
+      f2unpack(fsub2(p2, f2pack(__uint_as_float(hb << 16), __uint_as_float(hb & 0xffff0000u))), l0, l1);
+      const __nv_bfloat162 lb = __floats2bfloat162_rn(l0, l1);
+      hw[i] = hb;
+      lw[i] = *reinterpret_cast<const uint32_t *>(&lb);
     }
     tmem_st16(tS + 32 * ch, hw);
     tmem_st16(tS + 32 * ch + 16, lw);
   }
-  return ps0 + ps1;
+  float s0, s1;
+  f2unpack(ps, s0, s1);
+  return s0 + s1;
 }
 
 struct AttnItem {
@@ -458,7 +505,8 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
         if (kvalid >= AT_BN) {
 #pragma unroll
-          for (int e = 0; e < 128; ++e) mx[e & 3] = fmaxf(mx[e & 3], __uint_as_float(sr[e]));
+          for (int e = 0; e < 128; e += 2)
+            mx[(e >> 1) & 3] = fmax3(mx[(e >> 1) & 3], __uint_as_float(sr[e]), __uint_as_float(sr[e + 1]));
         } else {
 #pragma unroll
           for (int e = 0; e < 128; ++e)
@@ -481,8 +529,14 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
 #pragma unroll
           for (int q = 0; q < 4; ++q) tmem_ld32_raw(tO + 32 * q, ov + 32 * q);
           asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+          const uint64_t cr2 = f2pack(corr, corr);
 #pragma unroll
-          for (int e = 0; e < 128; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * corr);
+          for (int e = 0; e < 128; e += 2) {
+            float a0, a1;
+            f2unpack(fmul2(f2pack(__uint_as_float(ov[e]), __uint_as_float(ov[e + 1])), cr2), a0, a1);
+            ov[e] = __float_as_uint(a0);
+            ov[e + 1] = __float_as_uint(a1);
+          }
 #pragma unroll
           for (int q = 0; q < 4; ++q) tmem_st32(tO + 32 * q, ov + 32 * q);
         }

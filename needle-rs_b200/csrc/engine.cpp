@@ -462,6 +462,7 @@ Batch::Batch(DevModel *m) : m_(m) {
   cudaGetDevice(&prev);
   cudaSetDevice(m_->device);
   if (cudaStreamCreateWithFlags(&st_, cudaStreamNonBlocking) != cudaSuccess) st_ = nullptr;
+  if (cudaStreamCreateWithFlags(&cst_, cudaStreamNonBlocking) != cudaSuccess) cst_ = nullptr;
   cudaSetDevice(prev);
 }
 
@@ -489,6 +490,11 @@ Batch::~Batch() {
   for (auto &g : graphs_)
     if (g) cudaGraphExecDestroy(g);
   if (st_) cudaStreamSynchronize(st_);
+  if (cst_) {
+    cudaStreamSynchronize(cst_);
+    cudaStreamDestroy(cst_);
+  }
+  if (mask_ev_) cudaEventDestroy(mask_ev_);
   for (auto &e : timed_) {
     cudaEventDestroy(e.a);
     cudaEventDestroy(e.b);
@@ -581,7 +587,15 @@ bool Batch::prepare(const BatchSpec &spec, std::string &err) {
       mask_ = const_cast<uint64_t *>(spec.mask);
     } else {
       if (!(mask_ = alloc<uint64_t>(n, err))) return false;
-      NDL_CK(cudaMemcpyAsync(mask_, spec.mask, n * sizeof(uint64_t), cudaMemcpyHostToDevice, st));
+      if (cst_ && (mask_ev_ || cudaEventCreateWithFlags(&mask_ev_, cudaEventDisableTiming) == cudaSuccess)) {
+        NDL_CK(cudaEventRecord(mask_ev_, st));  // the allocation, ordered on st, precedes the copy
+        NDL_CK(cudaStreamWaitEvent(cst_, mask_ev_, 0));
+        NDL_CK(cudaMemcpyAsync(mask_, spec.mask, n * sizeof(uint64_t), cudaMemcpyHostToDevice, cst_));
+        NDL_CK(cudaEventRecord(mask_ev_, cst_));
+        mask_async_ = true;
+      } else {
+        NDL_CK(cudaMemcpyAsync(mask_, spec.mask, n * sizeof(uint64_t), cudaMemcpyHostToDevice, st));
+      }
     }
   }
   std::vector<uint32_t> first(B, kEosId);  // decoding starts from EOS (engine.rs:287)
@@ -1046,7 +1060,6 @@ bool Batch::decode_step(std::string &err, bool capture, int att_rows) {
 
 bool Batch::begin(std::string &err) {
   NDL_CK(cudaSetDevice(m_->device));
-  NDL_CK(cudaSetDevice(m_->device));
   launches_ = 0;
   steps_done_ = 0;
   for (auto &e : timed_) {
@@ -1055,6 +1068,7 @@ bool Batch::begin(std::string &err) {
   }
   timed_.clear();
   if (!reset_decoder(err) || !prefill(err)) return false;
+  if (mask_async_) NDL_CK(cudaStreamWaitEvent(st_, mask_ev_, 0));  // masks in place before the first step
   use_graph_ = !(spec_.flags & BATCH_NO_GRAPH) && !timed_cls_ && spec_.max_new > 0;
   // one graph per self-attention row bound the steps of this batch reach
   for (int s = 0; use_graph_ && s < spec_.max_new; ++s) {
@@ -1116,6 +1130,7 @@ bool Batch::set_mask_row(int req, int step, const uint64_t *bits, std::string &e
     err = "set_mask_row: no such mask row";
     return false;
   }
+  if (mask_async_) NDL_CK(cudaStreamWaitEvent(st_, mask_ev_, 0));
   uint64_t *dst = mask_ + ((size_t)req * spec_.max_new + step) * W_;
   NDL_CK(cudaMemcpyAsync(dst, bits, (size_t)W_ * sizeof(uint64_t), cudaMemcpyHostToDevice, st_));
   return true;
@@ -1126,6 +1141,7 @@ bool Batch::set_mask_step(int step, const uint64_t *rows, std::string &err) {
     err = "set_mask_step: no such mask step";
     return false;
   }
+  if (mask_async_) NDL_CK(cudaStreamWaitEvent(st_, mask_ev_, 0));
   const size_t row = (size_t)W_ * sizeof(uint64_t);
   NDL_CK(cudaMemcpy2DAsync(mask_ + (size_t)step * W_, (size_t)spec_.max_new * row, rows, row, row,
                            (size_t)spec_.n_req, cudaMemcpyHostToDevice, st_));

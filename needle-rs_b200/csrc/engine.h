@@ -238,6 +238,11 @@ class Batch {
   unsigned int *n_done_ = nullptr;
   float *logits_ = nullptr;
   cudaGraphExec_t graphs_[3] = {nullptr, nullptr, nullptr};  // decode step, by att_slot
+  // host mask bitmaps are uploaded on cst_ (they are first read by the first
+  // decode step, so the copy overlaps the prefill); mask_ev_ marks its end
+  cudaStream_t cst_ = nullptr;
+  cudaEvent_t mask_ev_ = nullptr;
+  bool mask_async_ = false;
   bool use_graph_ = false;
   uint32_t *first_ids_ = nullptr;
   int steps_done_ = 0;

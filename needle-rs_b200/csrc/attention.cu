@@ -8,6 +8,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "tc_common.cuh"
 
 namespace ndl {
 
@@ -394,154 +395,66 @@ __device__ __forceinline__ void store_split(__nv_bfloat16 *hi, __nv_bfloat16 *lo
   *lo = __float2bfloat16_rn(v - __bfloat162float(h));
 }
 
-// Shared by cross-attention (attn.rs:281-337; rows = the request's encoder
-// K/V) and decoder self-attention (attn.rs:100-183; rows = the request's
-// cache).  The REP query heads of one KV head (GQA) share every K and V row
-// read: a half-warp reads one 256-byte row with float4s, four rows in
-// flight per half-warp.  qs: [REP][64] normed queries in shared memory.
-// Exact softmax as ops.rs:5-36 (max, exp, sum, scale), then P V.
-template <int REP, int NT>
-__device__ __forceinline__ void attend_hd64(const float *qs, const float *__restrict__ kb,
-                                            const float *__restrict__ vb, int kvd, int T, float scale, float *sc,
-                                            float *red, float *out_row, __nv_bfloat16 *hi_row = nullptr,
-                                            __nv_bfloat16 *lo_row = nullptr) {
-  constexpr int HD = 64, NHW = NT / 16, NW = NT / 32, UNR = 4, SPAN = NHW * UNR;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int hw = tid >> 4, hl = tid & 15;
-  float qr[REP][4];
-#pragma unroll
-  for (int j = 0; j < REP; ++j) {
-    float4 t = *reinterpret_cast<const float4 *>(qs + j * HD + hl * 4);
-    qr[j][0] = t.x;
-    qr[j][1] = t.y;
-    qr[j][2] = t.z;
-    qr[j][3] = t.w;
-  }
-  kb += hl * 4;
-  vb += hl * 4;
-  // Scores.  The loop bound is uniform over the block so both halves of a
-  // warp always reach the shuffles together.
-  for (int base = 0; base < T; base += SPAN) {
-    float4 kv[UNR];
-#pragma unroll
-    for (int u = 0; u < UNR; ++u) {
-      int t = base + hw + u * NHW;
-      kv[u] = t < T ? __ldg(reinterpret_cast<const float4 *>(kb + (int64_t)t * kvd)) : make_float4(0, 0, 0, 0);
-    }
-#pragma unroll
-    for (int u = 0; u < UNR; ++u) {
-      int t = base + hw + u * NHW;
-#pragma unroll
-      for (int j = 0; j < REP; ++j) {
-        float d = qr[j][0] * kv[u].x + qr[j][1] * kv[u].y + qr[j][2] * kv[u].z + qr[j][3] * kv[u].w;
-#pragma unroll
-        for (int o = 8; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-        if (hl == 0 && t < T) sc[j * T + t] = d * scale;
-      }
-    }
-  }
-  __syncthreads();
-  float *stat = red;  // [REP][NW]: maxes, then sums
-  float mx[REP], inv[REP];
-#pragma unroll
-  for (int j = 0; j < REP; ++j) {
-    float m = -INFINITY;
-    for (int t = tid; t < T; t += NT) m = fmaxf(m, sc[j * T + t]);
-    m = warp_max(m);
-    if (lane == 0) stat[j * NW + warp] = m;
-  }
-  __syncthreads();
-#pragma unroll
-  for (int j = 0; j < REP; ++j) {
-    float m = stat[j * NW];
-    for (int w = 1; w < NW; ++w) m = fmaxf(m, stat[j * NW + w]);
-    mx[j] = m;
-  }
-  __syncthreads();
-#pragma unroll
-  for (int j = 0; j < REP; ++j) {
-    float sum = 0.0f;
-    for (int t = tid; t < T; t += NT) {
-      float p = expf(sc[j * T + t] - mx[j]);
-      sc[j * T + t] = p;
-      sum += p;
-    }
-    sum = warp_sum(sum);
-    if (lane == 0) stat[j * NW + warp] = sum;
-  }
-  __syncthreads();
-#pragma unroll
-  for (int j = 0; j < REP; ++j) {
-    float sum = 0.0f;
-    for (int w = 0; w < NW; ++w) sum += stat[j * NW + w];
-    inv[j] = 1.0f / sum;
-  }
-  __syncthreads();
-  float acc[REP][4];
-#pragma unroll
-  for (int j = 0; j < REP; ++j)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) acc[j][e] = 0.0f;
-  for (int base = 0; base < T; base += SPAN) {
-    float4 vv[UNR];
-#pragma unroll
-    for (int u = 0; u < UNR; ++u) {
-      int t = base + hw + u * NHW;
-      vv[u] = t < T ? __ldg(reinterpret_cast<const float4 *>(vb + (int64_t)t * kvd)) : make_float4(0, 0, 0, 0);
-    }
-#pragma unroll
-    for (int u = 0; u < UNR; ++u) {
-      int t = base + hw + u * NHW;
-      if (t < T) {
-#pragma unroll
-        for (int j = 0; j < REP; ++j) {
-          float p = sc[j * T + t] * inv[j];
-          acc[j][0] = fmaf(p, vv[u].x, acc[j][0]);
-          acc[j][1] = fmaf(p, vv[u].y, acc[j][1]);
-          acc[j][2] = fmaf(p, vv[u].z, acc[j][2]);
-          acc[j][3] = fmaf(p, vv[u].w, acc[j][3]);
-        }
-      }
-    }
-  }
-#pragma unroll
-  for (int j = 0; j < REP; ++j)
-    *reinterpret_cast<float4 *>(red + (hw * REP + j) * HD + hl * 4) =
-        make_float4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]);
-  __syncthreads();
-  for (int i = tid; i < REP * HD; i += NT) {
-    int j = i / HD, d = i - j * HD;
-    float sum = 0.0f;
-    for (int w = 0; w < NHW; ++w) sum += red[(w * REP + j) * HD + d];
-    if (hi_row)
-      store_split(hi_row + j * HD + d, lo_row + j * HD + d, sum);
-    else
-      out_row[j * HD + d] = sum;
-  }
+constexpr int CA_TILE = 64, CA_STAGES = 3, CA_HD = 64, CA_REP = 2;
+
+// Dynamic shared memory of cross_attn_kernel for prompts of up to max_len:
+// 128 bytes of alignment slack, the ring, q, statistics, scores, barriers.
+inline size_t cross_attn_smem(int max_len) {
+  return 128 + ((size_t)CA_STAGES * CA_TILE * CA_HD + CA_REP * CA_HD + CA_REP * 8 + (size_t)CA_REP * max_len) * sizeof(float) +
+         CA_STAGES * sizeof(uint64_t) + 8;
 }
 
-// Decoder cross-attention (attn.rs:281-337).  CTA = (request, KV head).  The
+// Decoder cross-attention (attn.rs:281-337), head dim 64, two query heads
+// per KV head.  CTA = (request, KV head), 256 threads = 16 half-warps.  The
 // dominant HBM reader of batched decode: each CTA streams its request's
-// encoder K then V rows exactly once.
-template <int REP>
-__global__ void __launch_bounds__(256) cross_attn_kernel(const float *__restrict__ q, const float *__restrict__ qn,
-                                                         const float *__restrict__ kplane,
-                                                         const float *__restrict__ vplane,
+// encoder K rows, then its V rows, exactly once, through a ring of CA_STAGES
+// shared-memory tiles of 64 rows x 64 dimensions: one TMA load per tile
+// (thread 0; the head-major K/V planes as one [rows][64] tensor, in which
+// this head's rows of the request are contiguous),
+// completing on the stage's mbarrier, CA_STAGES - 1 tiles ahead of the tile
+// being read, so the V tiles are in flight while the softmax runs and no
+// register holds data in flight.  Rows past the request belong to the next
+// request (or read as zeros past the planes) and are masked.
+// Exact softmax as ops.rs:5-36: scores of all rows, maximum, exponentials
+// and their sum, then P V.  A half-warp reads one row (lane l: dimensions
+// 4l..4l+3) and the two query heads share every read.
+__global__ void __launch_bounds__(256) cross_attn_kernel(const __grid_constant__ CUtensorMap kvmap,
+                                                         const float *__restrict__ q, const float *__restrict__ qn,
+                                                         int64_t k_row0, int64_t v_row0, int64_t head_rows,
                                                          const int64_t *__restrict__ seq_off, float *out,
                                                          __nv_bfloat16 *hi, __nv_bfloat16 *lo, int64_t ldp,
-                                                         AttnDims a) {
-  constexpr int HD = 64;
-  extern __shared__ __align__(16) float sm[];
-  pdl_trigger();
-  pdl_wait();
+                                                         AttnDims a, int max_len, int *err) {
+  constexpr int HD = CA_HD, REP = CA_REP, NHW = 16, NW = 8, NT = 256;
+  extern __shared__ __align__(16) unsigned char ca_smem[];
+  float *sm = reinterpret_cast<float *>(((uintptr_t)ca_smem + 127) & ~(uintptr_t)127);
+  float(*ring)[CA_TILE][HD] = reinterpret_cast<float(*)[CA_TILE][HD]>(sm);
+  float *qs = sm + CA_STAGES * CA_TILE * HD;  // [REP][64]
+  float *stat = qs + REP * HD;                // [REP][NW]
+  float *sc = stat + REP * NW;                // [REP][T]
+  float *red = sm;                            // [16][REP][64], over the ring once it is drained
+  uint64_t *full = reinterpret_cast<uint64_t *>(((uintptr_t)(sc + REP * max_len) + 7) & ~(uintptr_t)7);
   const int b = blockIdx.y, g = blockIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, hw = tid >> 4, hl = tid & 15;
+  pdl_trigger();
+  if (tid == 0) {
+    for (int s = 0; s < CA_STAGES; ++s) tc::mbar_init(&full[s], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  pdl_wait();
   const int64_t off = seq_off[b];
   const int T = (int)(seq_off[b + 1] - off);
-  const int kvd = a.KVH * HD, qd = a.H * HD;
-  float *qs = sm;                   // [REP][64]
-  float *red = sm + REP * HD;       // [16][REP][64]
-  float *sc = red + 16 * REP * HD;  // [REP][T]
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qd = a.H * HD;
+  const int nt = (T + CA_TILE - 1) / CA_TILE, ntot = 2 * nt;  // K tiles, then V tiles
+  auto issue = [&](int k) {  // thread 0
+    const int s = k % CA_STAGES;
+    const bool isv = k >= nt;
+    const int64_t y = (isv ? v_row0 : k_row0) + g * head_rows + off + (int64_t)(isv ? k - nt : k) * CA_TILE;
+    tc::mbar_expect_tx(&full[s], (uint32_t)(CA_TILE * HD * 4));
+    tc::tma_load_2d(&ring[s][0][0], &kvmap, &full[s], 0, (int)y);
+  };
+  if (tid == 0)
+    for (int k = 0; k < CA_STAGES - 1 && k < ntot; ++k) issue(k);
   if (warp < REP) {  // q heads of this group, q_norm (attn.rs:296-300); no RoPE
     float *v = qs + warp * HD;
     const float *src = q + (int64_t)b * qd + (g * REP + warp) * HD;
@@ -551,9 +464,122 @@ __global__ void __launch_bounds__(256) cross_attn_kernel(const float *__restrict
     norm_rope_head(v, HD, qn, nullptr, nullptr, false, lane);
   }
   __syncthreads();
-  attend_hd64<REP, 256>(qs, kplane + off * kvd + g * HD, vplane + off * kvd + g * HD, kvd, T, a.scale, sc, red,
-                        out + (int64_t)b * qd + g * REP * HD, hi ? hi + (int64_t)b * ldp + g * REP * HD : nullptr,
-                        hi ? lo + (int64_t)b * ldp + g * REP * HD : nullptr);
+  float qr[REP][4];
+#pragma unroll
+  for (int j = 0; j < REP; ++j) {
+    const float4 t = *reinterpret_cast<const float4 *>(qs + j * HD + hl * 4);
+    qr[j][0] = t.x;
+    qr[j][1] = t.y;
+    qr[j][2] = t.z;
+    qr[j][3] = t.w;
+  }
+  float inv[REP], acc[REP][4];
+#pragma unroll
+  for (int j = 0; j < REP; ++j) {
+    inv[j] = 0.0f;
+    acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
+  }
+  int k = 0;
+  bool ok = true;  // the same in every thread
+  for (; k < ntot; ++k) {
+    // the stage of tile k + CA_STAGES - 1 was freed by the barrier ending tile k - 1
+    if (tid == 0 && k + CA_STAGES - 1 < ntot) issue(k + CA_STAGES - 1);
+    const int s = k % CA_STAGES;
+    ok = __syncthreads_and(tc::mbar_wait(&full[s], (uint32_t)(k / CA_STAGES) & 1u, err)) != 0;
+    if (!ok) break;
+    if (k < nt) {  // scores of K tile k
+      const int t0 = k * CA_TILE;
+#pragma unroll
+      for (int u = 0; u < CA_TILE / NHW; ++u) {
+        const int r = hw + NHW * u, t = t0 + r;
+        const float4 kv = *reinterpret_cast<const float4 *>(&ring[s][r][hl * 4]);
+#pragma unroll
+        for (int j = 0; j < REP; ++j) {
+          float d = qr[j][0] * kv.x + qr[j][1] * kv.y + qr[j][2] * kv.z + qr[j][3] * kv.w;
+#pragma unroll
+          for (int o = 8; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+          if (hl == 0 && t < T) sc[j * T + t] = d * a.scale;
+        }
+      }
+    } else {
+      if (k == nt) {  // every score is in: maximum, exponentials, sum
+#pragma unroll
+        for (int j = 0; j < REP; ++j) {
+          float m = -INFINITY;
+          for (int t = tid; t < T; t += NT) m = fmaxf(m, sc[j * T + t]);
+          m = warp_max(m);
+          if (lane == 0) stat[j * NW + warp] = m;
+        }
+        __syncthreads();
+        float mx[REP];
+#pragma unroll
+        for (int j = 0; j < REP; ++j) {
+          float m = stat[j * NW];
+          for (int w = 1; w < NW; ++w) m = fmaxf(m, stat[j * NW + w]);
+          mx[j] = m;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int j = 0; j < REP; ++j) {
+          float sum = 0.0f;
+          for (int t = tid; t < T; t += NT) {
+            const float p = expf(sc[j * T + t] - mx[j]);
+            sc[j * T + t] = p;
+            sum += p;
+          }
+          sum = warp_sum(sum);
+          if (lane == 0) stat[j * NW + warp] = sum;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int j = 0; j < REP; ++j) {
+          float sum = 0.0f;
+          for (int w = 0; w < NW; ++w) sum += stat[j * NW + w];
+          inv[j] = 1.0f / sum;
+        }
+      }
+      const int t0 = (k - nt) * CA_TILE;
+#pragma unroll
+      for (int u = 0; u < CA_TILE / NHW; ++u) {
+        const int r = hw + NHW * u, t = t0 + r;
+        if (t < T) {
+          const float4 vv = *reinterpret_cast<const float4 *>(&ring[s][r][hl * 4]);
+#pragma unroll
+          for (int j = 0; j < REP; ++j) {
+            const float p = sc[j * T + t] * inv[j];
+            acc[j][0] = fmaf(p, vv.x, acc[j][0]);
+            acc[j][1] = fmaf(p, vv.y, acc[j][1]);
+            acc[j][2] = fmaf(p, vv.z, acc[j][2]);
+            acc[j][3] = fmaf(p, vv.w, acc[j][3]);
+          }
+        }
+      }
+    }
+    __syncthreads();  // stage s free
+  }
+  if (!ok) {
+    // a wait gave up: let the copies already started land before the
+    // shared memory is released (each wait bounded), and write nothing
+    for (int kk = k; kk < ntot && kk < k + CA_STAGES; ++kk)
+      if (tid == 0) tc::mbar_drain(&full[kk % CA_STAGES], (uint32_t)(kk / CA_STAGES) & 1u);
+    __syncthreads();
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < REP; ++j)
+    *reinterpret_cast<float4 *>(red + (hw * REP + j) * HD + hl * 4) =
+        make_float4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]);
+  __syncthreads();
+  for (int i = tid; i < REP * HD; i += NT) {
+    const int j = i / HD, d = i - j * HD;
+    float sum = 0.0f;
+    for (int w = 0; w < NHW; ++w) sum += red[(w * REP + j) * HD + d];
+    const int64_t col = (int64_t)(g * REP + j) * HD + d;
+    if (hi)
+      store_split(hi + (int64_t)b * ldp + col, lo + (int64_t)b * ldp + col, sum);
+    else
+      out[(int64_t)b * qd + col] = sum;
+  }
 }
 
 // 16-byte global -> shared copy that completes asynchronously (no register
@@ -815,7 +841,7 @@ cudaError_t init_attention_kernels() {
   };
   set((const void *)encoder_attn_kernel);
   set((const void *)dec_self_attn_kernel);
-  set((const void *)cross_attn_kernel<2>);
+  set((const void *)cross_attn_kernel);
     set((const void *)cross_attn_generic_kernel);
   return e;
 }
@@ -900,15 +926,17 @@ cudaError_t decoder_self_attention(const float *qkv, const int32_t *step, const 
 
 cudaError_t decoder_cross_attention(const float *q, const float *q_norm, const float *kplane,
                                     const float *vplane, const int64_t *seq_off, int B, float *out, AttnDims a,
-                                    cudaStream_t st, int max_len, void *hi_, void *lo_, int64_t ldp) {
+                                    cudaStream_t st, int max_len, void *hi_, void *lo_, int64_t ldp, int *err,
+                                    const void *kv_map, int64_t k_row0, int64_t v_row0, int64_t head_rows) {
   __nv_bfloat16 *hi = static_cast<__nv_bfloat16 *>(hi_), *lo = static_cast<__nv_bfloat16 *>(lo_);
   if (B <= 0) return cudaSuccess;
   int rep = a.H / a.KVH;
   if (a.HD == 64 && rep == 2) {
-    size_t sm = ((size_t)rep * 64 + (size_t)16 * rep * 64 + (size_t)rep * max_len) * sizeof(float);
+    if (!err || !kv_map || head_rows <= 0 || v_row0 + a.KVH * head_rows > INT32_MAX) return cudaErrorInvalidValue;
+    const size_t sm = cross_attn_smem(max_len);
     if (sm > kMaxDynSmem) return cudaErrorInvalidValue;
-    return launch(cross_attn_kernel<2>, dim3(a.KVH, B), dim3(256), sm, st, q, q_norm, kplane, vplane, seq_off, out, hi,
-                  lo, ldp, a);
+    return launch(cross_attn_kernel, dim3(a.KVH, B), dim3(256), sm, st, *static_cast<const CUtensorMap *>(kv_map), q,
+                  q_norm, k_row0, v_row0, head_rows, seq_off, out, hi, lo, ldp, a, max_len, err);
   }
   if (hi) return cudaErrorInvalidValue;
   if (a.HD > 128 || (a.HD & 1)) return cudaErrorInvalidValue;

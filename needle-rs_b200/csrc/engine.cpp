@@ -690,6 +690,16 @@ bool Batch::prepare(const BatchSpec &spec, std::string &err) {
     if (attn_planes_make(pb, c.num_heads, c.num_kv_heads, (int)slab, attn_planes_) != cudaSuccess) tc_attn_ = false;
   }
   if (L > 0 && !(kv_planes_ = alloc<float>((size_t)2 * L * ttot_ * kvd, err))) return false;
+  kv_map_ok_ = false;
+  if (L > 0 && hd == 64 && c.num_heads == 2 * c.num_kv_heads) {  // the cross-attention kernel's tile loads
+    const int64_t rows = (int64_t)2 * L * c.num_kv_heads * ttot_;
+    if (rows > INT32_MAX) {
+      err = "batch too large for the cross-attention tile map";
+      return false;
+    }
+    NDL_CK(tma_map_f32(kv_planes_, rows, 64, 64, 64, kv_map_));
+    kv_map_ok_ = true;
+  }
   {  // tensor-core staging planes, shared by every batched GEMM of the call
     const int64_t rows = std::max<int64_t>(ct, B);
     std::vector<int> kps = {tc_padded_k(d), tc_padded_k(qd)};
@@ -915,10 +925,18 @@ bool Batch::prefill(std::string &err) {
       NDL_CK(cudaMemcpyAsync(enc_out_ + ch.tok0 * d, pxn_, (size_t)rows * d * 4, cudaMemcpyDeviceToDevice, st));
     if (L > 0) {  // fill_cross_kv (model.rs:196-231): all layers' K|V in one matmul
       MatmulOut o;
-      o.y = kv_planes_ + ch.tok0 * kvd;
-      o.ldy = kvd;
-      o.col_block = kvd;
-      o.block_stride = ttot_ * kvd;
+      if (kv_map_ok_) {  // head-major: one 64-column block per (layer, K|V, head)
+        o.y = kv_planes_ + ch.tok0 * 64;
+        o.ldy = 64;
+        o.col_block = 64;
+        o.block_stride = ttot_ * 64;
+        o.kv_block = kvd;
+      } else {
+        o.y = kv_planes_ + ch.tok0 * kvd;
+        o.ldy = kvd;
+        o.col_block = kvd;
+        o.block_stride = ttot_ * kvd;
+      }
       const bool fused_norm = (hd == 64) && (kvd % 64 == 0);
       o.epi = fused_norm ? EPI_KNORM : EPI_STORE;
       o.vec = m.cross_knorm;
@@ -1002,7 +1020,9 @@ bool Batch::decode_step(std::string &err, bool capture, int att_rows) {
     const float *kp = kv_planes_ + (size_t)2 * l * ttot_ * kvd, *vp = kp + (size_t)ttot_ * kvd;
     cudaEvent_t ev;
     if (!tbegin(TIME_CROSS_ATTENTION, capture, ev, err)) return false;
-    NDL_LK(decoder_cross_attention(q_, D.ca_qn, kp, vp, seq_off_, B, att_, m.ad, st, tmax_, ahi, alo, aldp));
+    NDL_LK(decoder_cross_attention(q_, D.ca_qn, kp, vp, seq_off_, B, att_, m.ad, st, tmax_, ahi, alo, aldp, m.kerr,
+                                   kv_map_ok_ ? kv_map_ : nullptr, (int64_t)2 * l * c.num_kv_heads * ttot_,
+                                   (int64_t)(2 * l + 1) * c.num_kv_heads * ttot_, ttot_));
     // algorithmic bytes: the encoder K and V rows once, q in, attention out
     if (!tend(ev, 4.0 * (double)ttot_ * kvd * c.num_heads / c.num_kv_heads,
               (double)ttot_ * kvd * 8 + (double)B * qd * 8, err))

@@ -220,7 +220,13 @@ class Batch {
   int64_t chunk_tok_max_ = 0;
   float *px_ = nullptr, *pxn_ = nullptr, *pqkv_ = nullptr, *patt_ = nullptr, *pffn_ = nullptr;
   // encoder outputs
-  float *kv_planes_ = nullptr;     // [2L][ttot][KVH*HD]  (K0 V0 K1 V1 ...)
+  // encoder K/V of the decoder layers (K0 V0 K1 V1 ...): head-major
+  // [2L][KVH][ttot][64] when kv_map_ok_ (head dim 64, two query heads per KV
+  // head: each head's rows are one contiguous stream for the cross-attention
+  // kernel's tile loads), else [2L][ttot][KVH*HD]
+  float *kv_planes_ = nullptr;
+  alignas(64) unsigned char kv_map_[128] = {};  // TMA descriptor of the head-major planes (64 x 64 boxes)
+  bool kv_map_ok_ = false;
   float *enc_out_ = nullptr;       // [ttot][d] when requested
   // decoder state
   float *self_k_ = nullptr, *self_v_ = nullptr;  // [L][B][cap][KVH*HD]

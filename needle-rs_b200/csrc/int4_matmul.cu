@@ -238,7 +238,7 @@ __global__ void __launch_bounds__(256) tile_kernel(const float *__restrict__ x, 
         // the half-warp.  Only K blocks (even column-block index) are normed.
         // (clamped so a column past N never indexes past the scale table;
         // such columns are not stored)
-        int blk = min(n, e.N - 1) / e.o.col_block;
+        int blk = min(n, e.N - 1) / (e.o.kv_block ? e.o.kv_block : e.o.col_block);
         if ((blk & 1) == 0) knorm16(v, e.o.vec + (int64_t)(blk >> 1) * 64, tx);
       }
       if (m < M && n < e.N) store4(e, m, n, v[0], v[1], v[2], v[3], yvec);
@@ -321,7 +321,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(const float *__restrict__ x, 
   if (e.o.epi == EPI_KNORM) {
     // NC == 64 == one head; normalise row m if this block is a K block.
     for (int m = tid; m < M; m += 256) {
-      int blk = n0 / e.o.col_block;
+      int blk = n0 / (e.o.kv_block ? e.o.kv_block : e.o.col_block);
       if ((blk & 1) == 0) {
         float *r = red + m * NC;
         float ss = 0.0f;
@@ -577,7 +577,9 @@ cudaError_t int4_matmul(const float *x, int64_t ldx, int M, const Int4Weight &W,
   // k-norm needs whole 64-column heads.
   if (o.col_block && (o.col_block % 4)) return cudaErrorInvalidValue;
   if (o.epi == EPI_QKV || o.epi == EPI_QKV_DEC || o.epi == EPI_ARGMAX) return cudaErrorInvalidValue;  // tensor-core only
-  if (o.epi == EPI_KNORM && (!o.col_block || (o.col_block % 64) || !o.vec)) return cudaErrorInvalidValue;
+  if (o.epi == EPI_KNORM &&
+      (!o.col_block || (o.col_block % 64) || !o.vec || (o.kv_block && (o.kv_block % o.col_block))))
+    return cudaErrorInvalidValue;
   if (o.epi == EPI_ACT && (W.N & 1)) return cudaErrorInvalidValue;
   EpiCtx e{o, W.N};
   const int Kp = W.G * W.gs;

@@ -60,6 +60,10 @@ struct MatmulOut {
   int col_block = 0;         // 0: plain; else columns are split into blocks of
   int64_t block_stride = 0;  //   col_block, block b written at y + b*block_stride
   int epi = EPI_STORE;
+  // EPI_KNORM: width of each K or V block of the K|V pairs (0: col_block);
+  // column n belongs to pair (n / kv_block) / 2, normed when that quotient is
+  // even.  Lets col_block be narrower (one head) than a K or V block.
+  int kv_block = 0;
   float gate = 0.0f;
   int act = ACT_DRELU;
   const float *vec = nullptr;  // EPI_KNORM: k_norm scale [64]
@@ -98,6 +102,10 @@ struct TcPlanes {
 constexpr int kTcMinRows = 128;  // batched GEMMs at least this tall use the tensor cores
 int tc_padded_k(int K);
 cudaError_t tc_make_planes(const void *hi, const void *lo, int rows, int Kp, int box_rows, TcPlanes &out);
+// TMA descriptor (128-byte CUtensorMap written to `map`) of a row-major f32
+// matrix [rows][cols] loaded in boxes of box_rows x box_cols, no swizzle,
+// rows past the end read as zeros.
+cudaError_t tma_map_f32(const void *base, int64_t rows, int cols, int box_rows, int box_cols, void *map);
 // W (reference INT4 layout, paired mode allowed) -> bf16 planes [N][Kp].
 cudaError_t tc_prep_weight(const Int4Weight &W, int Kp, void *hi, void *lo, cudaStream_t st);
 // f32 rows [M][K] -> bf16 planes [M][Kp] (zero padded past K).
@@ -207,11 +215,17 @@ cudaError_t decoder_self_attention(const float *qkv, const int32_t *step, const 
 // Decoder cross-attention (attn.rs:281-337): q [B, H*HD] (q_norm applied
 // here), K/V of request b at rows seq_off[b].. of kplane / vplane
 // [*, KVH*HD].  out: [B, H*HD] f32, or the bf16 hi/lo planes as for
-// decoder_self_attention.
+// decoder_self_attention.  The head-dim-64 kernel (two query heads per KV
+// head) needs err (device flag set when a bounded wait gives up) and kv_map:
+// a tma_map_f32 descriptor of head-major K/V planes ([*][64], 64 x 64
+// boxes), in which request b's K rows of KV head g start at row k_row0 +
+// g * head_rows + seq_off[b] and its V rows at v_row0 + g * head_rows +
+// seq_off[b] (kplane / vplane are then not read).
 cudaError_t decoder_cross_attention(const float *q, const float *q_norm, const float *kplane,
                                     const float *vplane, const int64_t *seq_off, int B, float *out, AttnDims a,
                                     cudaStream_t st, int max_len, void *hi = nullptr, void *lo = nullptr,
-                                    int64_t ldp = 0);
+                                    int64_t ldp = 0, int *err = nullptr, const void *kv_map = nullptr,
+                                    int64_t k_row0 = 0, int64_t v_row0 = 0, int64_t head_rows = 0);
 
 // Output head (model.rs:89-149) + additive mask (engine.rs:294-297) + argmax
 // (engine.rs:299-304), fused.  h: [B, d]; emb: [V, d].  Request b is at step

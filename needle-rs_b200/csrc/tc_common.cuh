@@ -55,6 +55,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity, int *err
   }
 }
 
+// Bounded wait that ignores the error flag: after a wait gave up, lets the
+// asynchronous copies already started into this CTA's shared memory land
+// before the CTA exits.
+__device__ __forceinline__ void mbar_drain(uint64_t *b, uint32_t parity) {
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 0; !mbar_try_wait(b, parity); ++i)
+    if ((i & 255) == 255 && globaltimer_ns() - t0 > kWaitNs) return;
+}
+
 // Bounded wait with one outcome for the whole (converged) warp, so that a
 // timeout can never split a warp ahead of a warp-collective tcgen05
 // instruction.

@@ -92,7 +92,7 @@ __device__ __forceinline__ void epi_row(const TcEpi &e, int m, int n0, float *v)
     return;
   }
   if (o.epi == EPI_KNORM) {
-    int blk = n0 / o.col_block;
+    int blk = n0 / (o.kv_block ? o.kv_block : o.col_block);
     if ((blk & 1) == 0) {  // K block: ZCRMSNorm each 64-column head (norm.rs:23-30)
       const float4 *sc = reinterpret_cast<const float4 *>(o.vec + (int64_t)(blk >> 1) * 64);
 #pragma unroll
@@ -680,6 +680,21 @@ cudaError_t tc_make_planes(const void *hi, const void *lo, int rows, int Kp, int
   return cudaSuccess;
 }
 
+cudaError_t tma_map_f32(const void *base, int64_t rows, int cols, int box_rows, int box_cols, void *map) {
+  auto fn = encode_fn();
+  if (!fn) return cudaErrorNotSupported;
+  if (((uintptr_t)base & 15) || rows <= 0 || (cols % 4) || (box_cols % 4) || box_cols > 256 || box_rows > 256)
+    return cudaErrorInvalidValue;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols * 4};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = fn(reinterpret_cast<CUtensorMap *>(map), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void *>(base),
+                  dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 cudaError_t tc_prep_weight(const Int4Weight &W, int Kp, void *hi, void *lo, cudaStream_t st) {
   int64_t n = (int64_t)W.N * Kp;
   prep_weight_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(W, Kp, (__nv_bfloat16 *)hi, (__nv_bfloat16 *)lo);
@@ -701,7 +716,8 @@ cudaError_t tc_matmul(const TcPlanes &A, int M, const TcPlanes &B, int N, const 
   if (A.Kp != B.Kp || A.box_rows != TC_BM || B.box_rows != 128 || M > A.rows || N > B.rows)
     return cudaErrorInvalidValue;
   if (o.col_block && (o.col_block % 64)) return cudaErrorInvalidValue;
-  if (o.epi == EPI_KNORM && (!o.col_block || !o.vec)) return cudaErrorInvalidValue;
+  if (o.epi == EPI_KNORM && (!o.col_block || !o.vec || (o.kv_block && (o.kv_block % o.col_block))))
+    return cudaErrorInvalidValue;
   if (o.epi == EPI_ARGMAX) {
     if (!o.keys || !o.pos || (o.mask && o.mask_words * 64 < N)) return cudaErrorInvalidValue;
   } else if (o.epi == EPI_QKV) {

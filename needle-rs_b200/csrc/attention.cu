@@ -399,8 +399,11 @@ constexpr int CA_TILE = 64, CA_STAGES = 3, CA_HD = 64, CA_REP = 2;
 
 // Dynamic shared memory of cross_attn_kernel for prompts of up to max_len:
 // 128 bytes of alignment slack, the ring, q, statistics, scores, barriers.
+inline int ca_pad(int n) { return (n + CA_TILE - 1) / CA_TILE * CA_TILE; }
 inline size_t cross_attn_smem(int max_len) {
-  return 128 + ((size_t)CA_STAGES * CA_TILE * CA_HD + CA_REP * CA_HD + CA_REP * 8 + (size_t)CA_REP * max_len) * sizeof(float) +
+  return 128 +
+         ((size_t)CA_STAGES * CA_TILE * CA_HD + CA_REP * CA_HD + CA_REP * 8 + (size_t)CA_REP * ca_pad(max_len)) *
+             sizeof(float) +
          CA_STAGES * sizeof(uint64_t) + 8;
 }
 
@@ -430,9 +433,11 @@ __global__ void __launch_bounds__(256) cross_attn_kernel(const __grid_constant__
   float(*ring)[CA_TILE][HD] = reinterpret_cast<float(*)[CA_TILE][HD]>(sm);
   float *qs = sm + CA_STAGES * CA_TILE * HD;  // [REP][64]
   float *stat = qs + REP * HD;                // [REP][NW]
-  float *sc = stat + REP * NW;                // [REP][T]
+  float *sc = stat + REP * NW;                // [REP][Tp] scores, then weights (0 past T)
   float *red = sm;                            // [16][REP][64], over the ring once it is drained
-  uint64_t *full = reinterpret_cast<uint64_t *>(((uintptr_t)(sc + REP * max_len) + 7) & ~(uintptr_t)7);
+  uint64_t *full =
+      reinterpret_cast<uint64_t *>(((uintptr_t)(sc + REP * ((max_len + CA_TILE - 1) / CA_TILE * CA_TILE)) + 7) &
+                                   ~(uintptr_t)7);
   const int b = blockIdx.y, g = blockIdx.x;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, hw = tid >> 4, hl = tid & 15;
   pdl_trigger();
@@ -446,6 +451,7 @@ __global__ void __launch_bounds__(256) cross_attn_kernel(const __grid_constant__
   const int T = (int)(seq_off[b + 1] - off);
   const int qd = a.H * HD;
   const int nt = (T + CA_TILE - 1) / CA_TILE, ntot = 2 * nt;  // K tiles, then V tiles
+  const int Tp = nt * CA_TILE;                                 // score rows, padded to whole tiles
   auto issue = [&](int k) {  // thread 0
     const int s = k % CA_STAGES;
     const bool isv = k >= nt;
@@ -473,40 +479,58 @@ __global__ void __launch_bounds__(256) cross_attn_kernel(const __grid_constant__
     qr[j][2] = t.z;
     qr[j][3] = t.w;
   }
-  float inv[REP], acc[REP][4];
+  float acc[REP][4];
 #pragma unroll
-  for (int j = 0; j < REP; ++j) {
-    inv[j] = 0.0f;
-    acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
-  }
+  for (int j = 0; j < REP; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
   int k = 0;
   bool ok = true;  // the same in every thread
+  const bool b3 = hl & 8, b2 = hl & 4, b1 = hl & 2;
   for (; k < ntot; ++k) {
     // the stage of tile k + CA_STAGES - 1 was freed by the barrier ending tile k - 1
     if (tid == 0 && k + CA_STAGES - 1 < ntot) issue(k + CA_STAGES - 1);
     const int s = k % CA_STAGES;
-    ok = __syncthreads_and(tc::mbar_wait(&full[s], (uint32_t)(k / CA_STAGES) & 1u, err)) != 0;
+    // warp 0 waits for the tile; the others block in the barrier
+    const bool got = warp != 0 || tc::warp_wait(&full[s], (uint32_t)(k / CA_STAGES) & 1u, err);
+    ok = __syncthreads_and(got) != 0;
     if (!ok) break;
     if (k < nt) {  // scores of K tile k
       const int t0 = k * CA_TILE;
+      // partial dots of this lane's 4 dimensions, value i = 2u + j for row
+      // hw + 16u and query head j
+      float v[8];
 #pragma unroll
-      for (int u = 0; u < CA_TILE / NHW; ++u) {
-        const int r = hw + NHW * u, t = t0 + r;
-        const float4 kv = *reinterpret_cast<const float4 *>(&ring[s][r][hl * 4]);
+      for (int u = 0; u < 4; ++u) {
+        const float4 kv = *reinterpret_cast<const float4 *>(&ring[s][hw + NHW * u][hl * 4]);
 #pragma unroll
-        for (int j = 0; j < REP; ++j) {
-          float d = qr[j][0] * kv.x + qr[j][1] * kv.y + qr[j][2] * kv.z + qr[j][3] * kv.w;
+        for (int j = 0; j < REP; ++j)
+          v[2 * u + j] = qr[j][0] * kv.x + qr[j][1] * kv.y + qr[j][2] * kv.z + qr[j][3] * kv.w;
+      }
+      // transposed reduction over the half-warp: at each level a lane keeps
+      // half of its values and adds its partner's copies of them, so lane hl
+      // ends with the full dot of value hl >> 1
+      float w[4], x[2];
 #pragma unroll
-          for (int o = 8; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-          if (hl == 0 && t < T) sc[j * T + t] = d * a.scale;
-        }
+      for (int e = 0; e < 4; ++e) {
+        const float send = b3 ? v[e] : v[e + 4], keep = b3 ? v[e + 4] : v[e];
+        w[e] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+      }
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float send = b2 ? w[e] : w[e + 2], keep = b2 ? w[e + 2] : w[e];
+        x[e] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+      }
+      float y = (b1 ? x[1] : x[0]) + __shfl_xor_sync(0xffffffffu, b1 ? x[0] : x[1], 2);
+      y += __shfl_xor_sync(0xffffffffu, y, 1);
+      if ((hl & 1) == 0) {
+        const int t = t0 + hw + NHW * (hl >> 2), j = (hl >> 1) & 1;
+        sc[j * Tp + t] = t < T ? y * a.scale : -INFINITY;
       }
     } else {
-      if (k == nt) {  // every score is in: maximum, exponentials, sum
+      if (k == nt) {  // every score is in: maximum, exponentials, sum, weights
 #pragma unroll
         for (int j = 0; j < REP; ++j) {
           float m = -INFINITY;
-          for (int t = tid; t < T; t += NT) m = fmaxf(m, sc[j * T + t]);
+          for (int t = tid; t < T; t += NT) m = fmaxf(m, sc[j * Tp + t]);
           m = warp_max(m);
           if (lane == 0) stat[j * NW + warp] = m;
         }
@@ -522,9 +546,9 @@ __global__ void __launch_bounds__(256) cross_attn_kernel(const __grid_constant__
 #pragma unroll
         for (int j = 0; j < REP; ++j) {
           float sum = 0.0f;
-          for (int t = tid; t < T; t += NT) {
-            const float p = expf(sc[j * T + t] - mx[j]);
-            sc[j * T + t] = p;
+          for (int t = tid; t < Tp; t += NT) {
+            const float p = expf(sc[j * Tp + t] - mx[j]);  // 0 past T
+            sc[j * Tp + t] = p;
             sum += p;
           }
           sum = warp_sum(sum);
@@ -535,23 +559,23 @@ __global__ void __launch_bounds__(256) cross_attn_kernel(const __grid_constant__
         for (int j = 0; j < REP; ++j) {
           float sum = 0.0f;
           for (int w = 0; w < NW; ++w) sum += stat[j * NW + w];
-          inv[j] = 1.0f / sum;
+          const float inv = 1.0f / sum;
+          for (int t = tid; t < Tp; t += NT) sc[j * Tp + t] *= inv;
         }
+        __syncthreads();
       }
       const int t0 = (k - nt) * CA_TILE;
 #pragma unroll
       for (int u = 0; u < CA_TILE / NHW; ++u) {
-        const int r = hw + NHW * u, t = t0 + r;
-        if (t < T) {
-          const float4 vv = *reinterpret_cast<const float4 *>(&ring[s][r][hl * 4]);
+        const int r = hw + NHW * u;
+        const float4 vv = *reinterpret_cast<const float4 *>(&ring[s][r][hl * 4]);
 #pragma unroll
-          for (int j = 0; j < REP; ++j) {
-            const float p = sc[j * T + t] * inv[j];
-            acc[j][0] = fmaf(p, vv.x, acc[j][0]);
-            acc[j][1] = fmaf(p, vv.y, acc[j][1]);
-            acc[j][2] = fmaf(p, vv.z, acc[j][2]);
-            acc[j][3] = fmaf(p, vv.w, acc[j][3]);
-          }
+        for (int j = 0; j < REP; ++j) {
+          const float p = sc[j * Tp + t0 + r];  // 0 past T
+          acc[j][0] = fmaf(p, vv.x, acc[j][0]);
+          acc[j][1] = fmaf(p, vv.y, acc[j][1]);
+          acc[j][2] = fmaf(p, vv.z, acc[j][2]);
+          acc[j][3] = fmaf(p, vv.w, acc[j][3]);
         }
       }
     }

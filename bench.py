@@ -38,10 +38,10 @@ CLASS_NAMES = {1: "cross_attention", 2: "prefill_matmul", 3: "decode_matmul", 4:
 # classes whose algorithmic work is accounted (candidates for the roofline line)
 ROOFLINE_CLASSES = (1, 2, 3, 4, 5)
 # DRAM bytes (read + write) per algorithmic byte, from one ncu capture of the
-# class's kernel on the 256-request case; a launch reads each encoder K/V row
+# class's kernel on the 512-request case; a launch reads each encoder K/V row
 # once, so its traffic grows in proportion to the rows and scales to the full
-# launch.  cross_attention: profiles/cross_attn_decode_256req.md
-DRAM_PER_ALG_BYTE = {1: 1.030}
+# launch.  cross_attention: profiles/cross_attn_decode_512req.md
+DRAM_PER_ALG_BYTE = {1: 1.017}
 METRIC = "generated tokens/s"
 
 
@@ -511,7 +511,7 @@ def main():
                  "algorithmic_per_launch": (dom_by if roof["bound"] == "hbm" else dom_fl) / max(dom_n, 1)})
     if dom in DRAM_PER_ALG_BYTE:
         roof["traffic"] = DRAM_PER_ALG_BYTE[dom] * dom_by / max(dom_n, 1)
-        roof["traffic_source"] = "ncu dram__bytes_read.sum + dram__bytes_write.sum per algorithmic byte, 256-request capture, scaled"
+        roof["traffic_source"] = "ncu dram__bytes_read.sum + dram__bytes_write.sum per algorithmic byte, 512-request capture, scaled"
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

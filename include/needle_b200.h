@@ -240,6 +240,12 @@ int needle_ffn_forward_noalloc(const float *x, size_t T, size_t d_model, size_t 
                                const uint8_t *down_data, const float *down_scales, int activation, float *out,
                                void *stream);
 
+/* Measurement helper (no reference counterpart): the device's streaming-read
+ * bandwidth in GB/s, from `iters` timed grid-stride float4 read passes over a
+ * fresh `bytes` buffer (allocated and freed here) on the current device's
+ * default stream.  Returns 0, or -1 on a CUDA error. */
+int needle_hbm_read_gbs(size_t bytes, int iters, double *gbs);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

@@ -104,6 +104,7 @@ def lib():
             "needle_constraint_free": (None, [P]),
             "needle_ffn_forward": (I, [P, S, S, S, P, P, P, P, P, P, I, P, P]),
             "needle_ffn_forward_noalloc": (I, [P, S, S, S, P, P, P, P, P, P, I, P, P]),
+            "needle_hbm_read_gbs": (I, [S, I, P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)

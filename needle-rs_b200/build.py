@@ -15,7 +15,7 @@ BUILD = os.path.join(HERE, "_build")
 NVCC = os.environ.get("NVCC", "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
-CU = ["int4_matmul.cu", "attention.cu", "head.cu", "tc_gemm.cu", "tc_attn.cu", "ffn_noalloc.cu"]
+CU = ["int4_matmul.cu", "attention.cu", "head.cu", "tc_gemm.cu", "tc_attn.cu", "ffn_noalloc.cu", "measure.cu"]
 CPP = ["safetensors.cpp", "frontend.cpp", "engine.cpp", "capi.cpp"]
 
 

@@ -193,7 +193,7 @@ def op_suite(args, nb, wl, torch, np, pk, eng, blob):
                 programmatic-dependent ("overlap") launches.
     int4_sweep  M in {1, 8, 64, 512, 4096} x (N, K) in {(512,512), (2048,512),
                 (512,2048), (8192,512)} through a prepared plan: CUDA-core
-                matvec / tile kernels below 128 rows, tcgen05 above; chains of
+                matvec up to 8 rows, tcgen05 from 9 rows; chains of
                 R ops on distinct weight and x copies (over 2 x L2 per replay).
     single_request  one request, 256-token prompt, 64 greedy steps, no mask,
                 through needle_run_batch_ids (host buffers).
@@ -262,7 +262,7 @@ def op_suite(args, nb, wl, torch, np, pk, eng, blob):
             rows = min(M, 64)
             cpu = _cpu_us(lambda: oracle.matmul(packed, scales, K, N, x[:rows], path=1), budget_s=0.2,
                           min_reps=1) * (M / rows)
-            path = "tcgen05" if M >= 128 else ("cuda-core gemv" if M <= 8 else "cuda-core tile")
+            path = "tcgen05" if M > 8 else "cuda-core gemv"
             gbs = alg_bytes(M, N, K) / t / 1e9
             tfl = 2.0 * M * N * K / t / 1e12
             sweep.append({"M": M, "N": N, "K": K, "path": path, "us": 1e6 * t, "GB/s": gbs,

@@ -174,14 +174,15 @@ void needle_constraint_free(NeedleConstraint *c);
 /* w_data: [(G*gs/2)][N] bytes, low nibble = row 2p, high = row 2p+1;
  * w_scales: [G][N] f32, gs = min(32, K).  stream: cudaStream_t or NULL. */
 
-/* y[M][N] = x[M][K] @ W  (QuantizedWeight::matmul, quant.rs:400-410). */
+/* y[M][N] = x[M][K] @ W  (QuantizedWeight::matmul, quant.rs:400-410).  Up to
+ * 8 rows run on the CUDA cores, 9 rows or more on the tensor-core GEMM. */
 int needle_int4_matmul(const float *x, size_t M, size_t K, const uint8_t *w_data, const float *w_scales, size_t N,
                        size_t num_groups, float *y, void *stream);
 /* needle_int4_matmul with launch flags.  NEEDLE_INT4_OVERLAP lets the launch
  * begin while the previous kernel in the stream is still running: its weight
  * and scale loads are issued at once, x is read only after that kernel has
  * finished (programmatic dependent launch).  The caller promises that no work
- * still in flight in the stream writes w_data or w_scales.  Used below 128
+ * still in flight in the stream writes w_data or w_scales.  Used up to 8
  * rows; ignored by the tensor-core path. */
 #define NEEDLE_INT4_OVERLAP 1u
 int needle_int4_matmul_ex(const float *x, size_t M, size_t K, const uint8_t *w_data, const float *w_scales, size_t N,

@@ -815,12 +815,19 @@ static int *device_err_flag() {
   return flags[dev];
 }
 
-// Y = x @ W with the tensor-core GEMM for tall x (W and x staged as bf16
-// hi/lo planes in per-call device buffers) and the CUDA-core kernels below
-// kTcMinRows rows.
+// The standalone INT4 matmul takes the tensor-core GEMM from 9 rows: the
+// CUDA-core kernels spread only the output columns over CTAs, so between 9
+// and 127 rows a narrow W leaves most SMs idle.  x is staged in planes of at
+// least one 128-row tile; the rows past M are never stored.
+constexpr int kTcMinRowsOp = 9;
+inline int tc_stage_rows(int M) { return M < 128 ? 128 : M; }
+
+// Y = x @ W with the tensor-core GEMM (W and x staged as bf16 hi/lo planes in
+// per-call device buffers) from kTcMinRowsOp rows, the CUDA-core kernels
+// below.
 static bool matmul_any(const float *x, int64_t ldx, int M, const Int4Weight &W, const MatmulOut &o, cudaStream_t st) {
   const bool aligned = ((uintptr_t)o.y % 16 == 0) && (o.ldy % 4 == 0);
-  if (M < kTcMinRows || !aligned) return dev_check(int4_matmul(x, ldx, M, W, o, st));
+  if (M < kTcMinRowsOp || !aligned) return dev_check(int4_matmul(x, ldx, M, W, o, st));
   int *flag = device_err_flag();
   if (!flag) {
     set_err("device error flag allocation failed");
@@ -828,12 +835,13 @@ static bool matmul_any(const float *x, int64_t ldx, int M, const Int4Weight &W, 
   }
   const int Kp = tc_padded_k(W.K);
   void *buf = nullptr;
-  size_t wbytes = (size_t)W.N * Kp * 2, xbytes = (size_t)M * Kp * 2;
+  size_t wbytes = (size_t)W.N * Kp * 2, xbytes = (size_t)tc_stage_rows(M) * Kp * 2;
   if (!dev_check(cudaMallocAsync(&buf, 2 * wbytes + 2 * xbytes + 1024, st))) return false;
   char *b = (char *)(((uintptr_t)buf + 255) & ~(uintptr_t)255);
   void *wh = b, *wl = b + wbytes, *xh = b + 2 * wbytes, *xl = b + 2 * wbytes + xbytes;
   TcPlanes A, B;
-  bool ok = dev_check(tc_make_planes(wh, wl, W.N, Kp, 128, B)) && dev_check(tc_make_planes(xh, xl, M, Kp, 128, A)) &&
+  bool ok = dev_check(tc_make_planes(wh, wl, W.N, Kp, 128, B)) &&
+            dev_check(tc_make_planes(xh, xl, tc_stage_rows(M), Kp, 128, A)) &&
             dev_check(tc_prep_weight(W, Kp, wh, wl, st)) && dev_check(tc_split_rows(x, ldx, M, W.K, Kp, xh, xl, st)) &&
             dev_check(tc_matmul(A, M, B, W.N, o, flag, st));
   cudaFreeAsync(buf, st);
@@ -879,7 +887,7 @@ int needle_int4_matmul_ex(const float *x, size_t M, size_t K, const uint8_t *w, 
   MatmulOut o;
   o.y = y;
   o.ldy = (int64_t)N;
-  if (M < (size_t)kTcMinRows)
+  if (M < (size_t)kTcMinRowsOp)
     return dev_check(int4_matmul(x, (int64_t)K, (int)M, W, o, (cudaStream_t)stream, (flags & NEEDLE_INT4_OVERLAP) != 0))
                ? 0
                : -1;
@@ -913,11 +921,11 @@ NeedleInt4Plan *needle_int4_plan_create(const uint8_t *w, const float *s, size_t
   cudaGetDevice(&p->device);
   p->W = Int4Weight{w, s, (int)K, (int)N, (int)G, (int)(K < 32 ? K : 32)};
   p->max_m = (int)max_m;
-  p->tc = max_m >= (size_t)kTcMinRows;
+  p->tc = max_m >= (size_t)kTcMinRowsOp;
   if (p->tc) {
     cudaStream_t st = (cudaStream_t)stream;
     p->Kp = tc_padded_k((int)K);
-    const size_t wbytes = N * (size_t)p->Kp * 2, xbytes = max_m * (size_t)p->Kp * 2;
+    const size_t wbytes = N * (size_t)p->Kp * 2, xbytes = (size_t)tc_stage_rows((int)max_m) * p->Kp * 2;
     p->flag = device_err_flag();
     if (!p->flag || !dev_check(cudaMalloc(&p->buf, 2 * wbytes + 2 * xbytes + 1024))) {
       if (!p->flag) set_err("device error flag allocation failed");
@@ -927,7 +935,7 @@ NeedleInt4Plan *needle_int4_plan_create(const uint8_t *w, const float *s, size_t
     char *b = (char *)(((uintptr_t)p->buf + 255) & ~(uintptr_t)255);
     void *wh = b, *wl = b + wbytes, *xh = b + 2 * wbytes, *xl = b + 2 * wbytes + xbytes;
     if (!dev_check(tc_make_planes(wh, wl, (int)N, p->Kp, 128, p->B)) ||
-        !dev_check(tc_make_planes(xh, xl, (int)max_m, p->Kp, 128, p->A)) ||
+        !dev_check(tc_make_planes(xh, xl, tc_stage_rows((int)max_m), p->Kp, 128, p->A)) ||
         !dev_check(tc_prep_weight(p->W, p->Kp, wh, wl, st)) || !dev_check(cudaStreamSynchronize(st))) {
       cudaFree(p->buf);
       delete p;
@@ -947,7 +955,7 @@ int needle_int4_plan_matmul(NeedleInt4Plan *p, const float *x, size_t M, float *
   MatmulOut o;
   o.y = y;
   o.ldy = (int64_t)p->W.N;
-  if (!p->tc || M < (size_t)kTcMinRows || ((uintptr_t)y % 16) != 0 || (p->W.N % 4) != 0)
+  if (!p->tc || M < (size_t)kTcMinRowsOp || ((uintptr_t)y % 16) != 0 || (p->W.N % 4) != 0)
     return dev_check(int4_matmul(x, (int64_t)p->W.K, (int)M, p->W, o, st, (flags & NEEDLE_INT4_OVERLAP) != 0)) ? 0
                                                                                                               : -1;
   if (!dev_check(tc_split_rows(x, (int64_t)p->W.K, (int)M, p->W.K, p->Kp, const_cast<void *>(p->A.hi_ptr), const_cast<void *>(p->A.lo_ptr), st)) ||

@@ -126,6 +126,26 @@ def test_int4_plan_vs_oracle(M):
         plan.close()
 
 
+@pytest.mark.parametrize("M,max_m,N,K", [(9, 64, 512, 512), (64, 64, 512, 2048), (33, 40, 8192, 512)])
+def test_int4_plan_short_workspace_vs_oracle(M, max_m, N, K):
+    # plans for fewer than 128 rows still take the tensor-core GEMM from 9
+    # rows: x is staged in a one-tile (128-row) workspace whose extra rows are
+    # never stored
+    x, packed, scales = wl.int4_case(M, N, K, seed=5 * M + N)
+    ref = orc.matmul(packed, scales, K, N, x, path=1)
+    wd, sd = dev(packed), dev(scales)
+    plan = nb.Int4Plan(wd.data_ptr(), sd.data_ptr(), K, N, scales.shape[0], max_m=max_m)
+    try:
+        y = torch.full((M, N), float("nan"), device="cuda")
+        plan.matmul(dev(x).data_ptr(), M, y.data_ptr())
+        plan.status()
+        got = y.cpu().numpy()
+        assert not np.isnan(got).any()
+        assert close_act(got, ref), max_excess(got, ref, True)
+    finally:
+        plan.close()
+
+
 @pytest.mark.parametrize("M,N,K", [(4800, 2176, 512), (4736, 2048, 96)])
 def test_int4_plan_wide_tiles_vs_oracle(M, N, K):
     # Tall matrices take the 128 x 256 output tiles; N = 2176 leaves a

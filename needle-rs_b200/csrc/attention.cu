@@ -867,13 +867,6 @@ cudaError_t init_attention_kernels() {
   set((const void *)dec_self_attn_kernel);
   set((const void *)cross_attn_kernel);
   set((const void *)cross_attn_generic_kernel);
-  for (const void *f : {(const void *)rms_norm_planes_kernel, (const void *)rms_norm_kernel,
-                        (const void *)embed_kernel, (const void *)cross_attn_kernel,
-                        (const void *)self_attn_step_kernel<false, 16>, (const void *)self_attn_step_kernel<false, 32>,
-                        (const void *)self_attn_step_kernel<false, 64>, (const void *)self_attn_step_kernel<true, 64>}) {
-    cudaError_t r = max_shared_carveout(f);
-    if (r != cudaSuccess) e = r;
-  }
   return e;
 }
 

@@ -43,14 +43,6 @@ __device__ __forceinline__ int sign_extend4(uint32_t nib) {
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
-// Every kernel of the batched path asks for the same L1 / shared-memory split:
-// the most shared memory, which the tensor-core kernels need.  An SM then
-// never drains and reconfigures between two kernels of different splits, and
-// a kernel's CTAs can start during its predecessor's tail.
-inline cudaError_t max_shared_carveout(const void *f) {
-  return cudaFuncSetAttribute(f, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
-}
-
 // Whether launches from this host thread currently use programmatic
 // dependent launch (set_pdl in kernels.h).
 bool pdl_on();

@@ -235,7 +235,6 @@ cudaError_t init_head_kernels() {
     cudaError_t r = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
     if (r != cudaSuccess) e = r;
   }
-  if (e == cudaSuccess) e = max_shared_carveout((const void *)finish_step_kernel);
   return e;
 }
 

@@ -796,9 +796,6 @@ cudaError_t init_tc_kernels() {
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(tc_gemm_pair_kernel<TC_PAIR_STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)tc_smem_pair_bytes());
-  for (const void *f : {(const void *)tc_gemm_kernel<128, 3>, (const void *)tc_gemm_kernel<256, 2>,
-                        (const void *)tc_gemm_pair_kernel<TC_PAIR_STAGES>, (const void *)split_rows_kernel})
-    if (e == cudaSuccess) e = max_shared_carveout(f);
   return e;
 }
 

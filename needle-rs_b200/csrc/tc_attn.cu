@@ -337,145 +337,145 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
   if (warp < 4) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(AT_REG_PRODUCER));
     if (warp == 0) {
-    if (lane == 0) {  // ── TMA producer ──
-      int stage = 0;
-      uint32_t phase = 0;
-      int it = 0;
-      bool ok = true;
-      for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++it) {
-        const AttnItem item = decode_item(items[w]);
-        const int64_t off = seq_off[item.req];
-        const int T = (int)(seq_off[item.req + 1] - off);
-        const int nk = (T + AT_BN - 1) / AT_BN;
-        if (!(ok = mbar_wait(q_empty, (it & 1) ^ 1, err))) break;
-        mbar_expect_tx(q_full, (item.two ? 4 : 2) * AT_TILE);
-        for (int x = 0; x < (item.two ? 2 : 1); ++x) {
-          const int qrow = item.head[x] * slab + (int)off + item.qt[x] * AT_BM;
-          tma_load_2d(sm + AT_Q + 2 * x * AT_TILE, &tmQh, q_full, 0, qrow);
-          tma_load_2d(sm + AT_Q + (2 * x + 1) * AT_TILE, &tmQl, q_full, 0, qrow);
+      if (lane == 0) {  // ── TMA producer ──
+        int stage = 0;
+        uint32_t phase = 0;
+        int it = 0;
+        bool ok = true;
+        for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++it) {
+          const AttnItem item = decode_item(items[w]);
+          const int64_t off = seq_off[item.req];
+          const int T = (int)(seq_off[item.req + 1] - off);
+          const int nk = (T + AT_BN - 1) / AT_BN;
+          if (!(ok = mbar_wait(q_empty, (it & 1) ^ 1, err))) break;
+          mbar_expect_tx(q_full, (item.two ? 4 : 2) * AT_TILE);
+          for (int x = 0; x < (item.two ? 2 : 1); ++x) {
+            const int qrow = item.head[x] * slab + (int)off + item.qt[x] * AT_BM;
+            tma_load_2d(sm + AT_Q + 2 * x * AT_TILE, &tmQh, q_full, 0, qrow);
+            tma_load_2d(sm + AT_Q + (2 * x + 1) * AT_TILE, &tmQl, q_full, 0, qrow);
+          }
+          for (int j = 0; j < nk; ++j) {
+            if (!(ok = mbar_wait(&kv_empty[stage], phase ^ 1, err))) break;
+            uint8_t *st = sm + AT_KV + stage * AT_STAGE;
+            const int krow = item.g * slab + (int)off + j * AT_BN;
+            mbar_expect_tx(&kv_full[stage], AT_STAGE);
+            tma_load_2d(st, &tmKh, &kv_full[stage], 0, krow);
+            tma_load_2d(st + AT_TILE, &tmKl, &kv_full[stage], 0, krow);
+            tma_load_2d(st + 2 * AT_TILE, &tmVh, &kv_full[stage], 0, krow);
+            tma_load_2d(st + 3 * AT_TILE, &tmVl, &kv_full[stage], 0, krow);
+            if (++stage == 2) {
+              stage = 0;
+              phase ^= 1;
+            }
+          }
         }
-        for (int j = 0; j < nk; ++j) {
-          if (!(ok = mbar_wait(&kv_empty[stage], phase ^ 1, err))) break;
-          uint8_t *st = sm + AT_KV + stage * AT_STAGE;
-          const int krow = item.g * slab + (int)off + j * AT_BN;
-          mbar_expect_tx(&kv_full[stage], AT_STAGE);
-          tma_load_2d(st, &tmKh, &kv_full[stage], 0, krow);
-          tma_load_2d(st + AT_TILE, &tmKl, &kv_full[stage], 0, krow);
-          tma_load_2d(st + 2 * AT_TILE, &tmVh, &kv_full[stage], 0, krow);
-          tma_load_2d(st + 3 * AT_TILE, &tmVl, &kv_full[stage], 0, krow);
+        // drain: every issued copy consumed before the CTA exits
+        for (int s = 0; s < 2 && ok; ++s) {
+          ok = mbar_wait(&kv_empty[stage], phase ^ 1, err);
           if (++stage == 2) {
             stage = 0;
             phase ^= 1;
           }
         }
+        if (ok) mbar_wait(q_empty, (it & 1) ^ 1, err);
       }
-      // drain: every issued copy consumed before the CTA exits
-      for (int s = 0; s < 2 && ok; ++s) {
-        ok = mbar_wait(&kv_empty[stage], phase ^ 1, err);
-        if (++stage == 2) {
-          stage = 0;
-          phase ^= 1;
-        }
-      }
-      if (ok) mbar_wait(q_empty, (it & 1) ^ 1, err);
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {  // ── MMA issuer ──
-      constexpr uint32_t ID_S = umma_idesc(AT_BM, AT_BN);
-      constexpr uint32_t ID_PV2 = umma_idesc(AT_BM, 2 * AT_HD, true);  // P_hi x [V_hi | V_lo]
-      constexpr uint32_t ID_PV = umma_idesc(AT_BM, AT_HD, true);       // P_lo x V_hi
-      // per-slot phase counters (scalars: x is 0 or 1)
-      uint32_t pv_issued0 = 0, pv_issued1 = 0, pv_waited0 = 0, pv_waited1 = 0, p_seen0 = 0, p_seen1 = 0;
-      uint32_t items0 = 0, items1 = 0;
-      // S_x = Q_x K^T from stage st, once the slot's previous PV (which reads
-      // P over S_x) has completed.
-      auto issue_s = [&](int x, int st) -> bool {
-        const uint32_t waited = x ? pv_waited1 : pv_waited0;
-        if ((x ? pv_issued1 : pv_issued0) > waited) {
-          if (!mbar_wait(&pv_done[x], waited & 1, err)) return false;
-          if (x) ++pv_waited1; else ++pv_waited0;
-        }
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        uint8_t *kvs = sm + AT_KV + st * AT_STAGE;
-        const uint32_t d = tmem + (uint32_t)(x * AT_BN);
-#pragma unroll 1
-        for (int ks = 0; ks < AT_HD / 16; ++ks) {
-          const uint64_t adv = (uint64_t)((ks * 32) >> 4);
-          const uint64_t qh = umma_desc(sm + AT_Q + 2 * x * AT_TILE) + adv;
-          const uint64_t ql = umma_desc(sm + AT_Q + (2 * x + 1) * AT_TILE) + adv;
-          const uint64_t kh = umma_desc(kvs) + adv, kl = umma_desc(kvs + AT_TILE) + adv;
-          umma_bf16(d, qh, kh, ID_S, ks ? 1u : 0u);
-          umma_bf16(d, qh, kl, ID_S, 1u);
-          umma_bf16(d, ql, kh, ID_S, 1u);
-        }
-        umma_commit(&s_full[x]);
-        return true;
-      };
-      // O_x (+)= P_x V from stage st, once the softmax has written P_x (and,
-      // on an item's first tile, the previous item's O_x has been read out).
-      auto issue_pv = [&](int x, int st, int j, bool last) -> bool {
-        const uint32_t seen = x ? p_seen1 : p_seen0;
-        if (!mbar_wait(&p_full[x], seen & 1, err)) return false;
-        if (x) ++p_seen1; else ++p_seen0;
-        const uint32_t items = x ? items1 : items0;
-        if (j == 0 && items > 0 && !mbar_wait(&o_free[x], (items - 1) & 1, err)) return false;
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        uint8_t *kvs = sm + AT_KV + st * AT_STAGE;
-        const uint32_t d = tmem + 256u + (uint32_t)(x * 2 * AT_HD);
-        const uint32_t pbase = tmem + (uint32_t)(x * AT_BN);
-#pragma unroll 1
-        for (int ks = 0; ks < AT_BN / 16; ++ks) {
-          // keys 16ks..16ks+15: chunk ks/2, hi at 32(ks/2) + 8(ks%2), lo 16 columns on
-          const uint32_t ph = pbase + 32u * (ks >> 1) + 8u * (ks & 1), pl = ph + 16u;
-          // V_lo sits one plane tile (AT_TILE bytes) after V_hi: the second MN atom
-          const uint64_t vhl = umma_desc_mn(kvs + 2 * AT_TILE + ks * 2048, AT_TILE);
-          const uint64_t vh = umma_desc_mn(kvs + 2 * AT_TILE + ks * 2048);
-          umma_bf16_ts(d, ph, vhl, ID_PV2, (j > 0 || ks > 0) ? 1u : 0u);
-          umma_bf16_ts(d, pl, vh, ID_PV, 1u);
-        }
-        umma_commit(&pv_done[x]);
-        if (x) ++pv_issued1; else ++pv_issued0;
-        if (last) umma_commit(&o_done[x]);
-        return true;
-      };
-      int stage = 0;
-      uint32_t phase = 0;
-      int it = 0;
-      bool ok = true;
-      for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++it) {
-        const AttnItem item = decode_item(items[w]);
-        const int T = (int)(seq_off[item.req + 1] - seq_off[item.req]);
-        const int nk = (T + AT_BN - 1) / AT_BN;
-        if (!(ok = mbar_wait(q_full, it & 1, err))) break;
-        if (!(ok = mbar_wait(&kv_full[stage], phase, err))) break;
-        if (!(ok = issue_s(0, stage))) break;
-        if (item.two && !(ok = issue_s(1, stage))) break;
-        if (nk == 1) umma_commit(q_empty);  // every S of the item issued
-        for (int j = 0; j < nk && ok; ++j) {
-          const int cur = stage;
-          const int nxt = stage ^ 1;
-          const uint32_t nph = stage == 1 ? phase ^ 1 : phase;
-          const bool more = j + 1 < nk, last = j + 1 == nk;
-          if (!(ok = issue_pv(0, cur, j, last))) break;
-          if (more) {
-            if (!(ok = mbar_wait(&kv_full[nxt], nph, err))) break;
-            if (!(ok = issue_s(0, nxt))) break;
+    } else if (warp == 1) {
+      if (lane == 0) {  // ── MMA issuer ──
+        constexpr uint32_t ID_S = umma_idesc(AT_BM, AT_BN);
+        constexpr uint32_t ID_PV2 = umma_idesc(AT_BM, 2 * AT_HD, true);  // P_hi x [V_hi | V_lo]
+        constexpr uint32_t ID_PV = umma_idesc(AT_BM, AT_HD, true);       // P_lo x V_hi
+        // per-slot phase counters (scalars: x is 0 or 1)
+        uint32_t pv_issued0 = 0, pv_issued1 = 0, pv_waited0 = 0, pv_waited1 = 0, p_seen0 = 0, p_seen1 = 0;
+        uint32_t items0 = 0, items1 = 0;
+        // S_x = Q_x K^T from stage st, once the slot's previous PV (which reads
+        // P over S_x) has completed.
+        auto issue_s = [&](int x, int st) -> bool {
+          const uint32_t waited = x ? pv_waited1 : pv_waited0;
+          if ((x ? pv_issued1 : pv_issued0) > waited) {
+            if (!mbar_wait(&pv_done[x], waited & 1, err)) return false;
+            if (x) ++pv_waited1; else ++pv_waited0;
           }
-          if (item.two) {
-            if (!(ok = issue_pv(1, cur, j, last))) break;
-            if (more && !(ok = issue_s(1, nxt))) break;
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          uint8_t *kvs = sm + AT_KV + st * AT_STAGE;
+          const uint32_t d = tmem + (uint32_t)(x * AT_BN);
+  #pragma unroll 1
+          for (int ks = 0; ks < AT_HD / 16; ++ks) {
+            const uint64_t adv = (uint64_t)((ks * 32) >> 4);
+            const uint64_t qh = umma_desc(sm + AT_Q + 2 * x * AT_TILE) + adv;
+            const uint64_t ql = umma_desc(sm + AT_Q + (2 * x + 1) * AT_TILE) + adv;
+            const uint64_t kh = umma_desc(kvs) + adv, kl = umma_desc(kvs + AT_TILE) + adv;
+            umma_bf16(d, qh, kh, ID_S, ks ? 1u : 0u);
+            umma_bf16(d, qh, kl, ID_S, 1u);
+            umma_bf16(d, ql, kh, ID_S, 1u);
           }
-          if (j + 2 == nk) umma_commit(q_empty);
-          umma_commit(&kv_empty[cur]);  // every S and PV reading K_j / V_j issued before this commit
-          stage = nxt;
-          phase = nph;
-        }
-        if (ok) {
-          ++items0;
-          if (item.two) ++items1;
+          umma_commit(&s_full[x]);
+          return true;
+        };
+        // O_x (+)= P_x V from stage st, once the softmax has written P_x (and,
+        // on an item's first tile, the previous item's O_x has been read out).
+        auto issue_pv = [&](int x, int st, int j, bool last) -> bool {
+          const uint32_t seen = x ? p_seen1 : p_seen0;
+          if (!mbar_wait(&p_full[x], seen & 1, err)) return false;
+          if (x) ++p_seen1; else ++p_seen0;
+          const uint32_t items = x ? items1 : items0;
+          if (j == 0 && items > 0 && !mbar_wait(&o_free[x], (items - 1) & 1, err)) return false;
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          uint8_t *kvs = sm + AT_KV + st * AT_STAGE;
+          const uint32_t d = tmem + 256u + (uint32_t)(x * 2 * AT_HD);
+          const uint32_t pbase = tmem + (uint32_t)(x * AT_BN);
+  #pragma unroll 1
+          for (int ks = 0; ks < AT_BN / 16; ++ks) {
+            // keys 16ks..16ks+15: chunk ks/2, hi at 32(ks/2) + 8(ks%2), lo 16 columns on
+            const uint32_t ph = pbase + 32u * (ks >> 1) + 8u * (ks & 1), pl = ph + 16u;
+            // V_lo sits one plane tile (AT_TILE bytes) after V_hi: the second MN atom
+            const uint64_t vhl = umma_desc_mn(kvs + 2 * AT_TILE + ks * 2048, AT_TILE);
+            const uint64_t vh = umma_desc_mn(kvs + 2 * AT_TILE + ks * 2048);
+            umma_bf16_ts(d, ph, vhl, ID_PV2, (j > 0 || ks > 0) ? 1u : 0u);
+            umma_bf16_ts(d, pl, vh, ID_PV, 1u);
+          }
+          umma_commit(&pv_done[x]);
+          if (x) ++pv_issued1; else ++pv_issued0;
+          if (last) umma_commit(&o_done[x]);
+          return true;
+        };
+        int stage = 0;
+        uint32_t phase = 0;
+        int it = 0;
+        bool ok = true;
+        for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++it) {
+          const AttnItem item = decode_item(items[w]);
+          const int T = (int)(seq_off[item.req + 1] - seq_off[item.req]);
+          const int nk = (T + AT_BN - 1) / AT_BN;
+          if (!(ok = mbar_wait(q_full, it & 1, err))) break;
+          if (!(ok = mbar_wait(&kv_full[stage], phase, err))) break;
+          if (!(ok = issue_s(0, stage))) break;
+          if (item.two && !(ok = issue_s(1, stage))) break;
+          if (nk == 1) umma_commit(q_empty);  // every S of the item issued
+          for (int j = 0; j < nk && ok; ++j) {
+            const int cur = stage;
+            const int nxt = stage ^ 1;
+            const uint32_t nph = stage == 1 ? phase ^ 1 : phase;
+            const bool more = j + 1 < nk, last = j + 1 == nk;
+            if (!(ok = issue_pv(0, cur, j, last))) break;
+            if (more) {
+              if (!(ok = mbar_wait(&kv_full[nxt], nph, err))) break;
+              if (!(ok = issue_s(0, nxt))) break;
+            }
+            if (item.two) {
+              if (!(ok = issue_pv(1, cur, j, last))) break;
+              if (more && !(ok = issue_s(1, nxt))) break;
+            }
+            if (j + 2 == nk) umma_commit(q_empty);
+            umma_commit(&kv_empty[cur]);  // every S and PV reading K_j / V_j issued before this commit
+            stage = nxt;
+            phase = nph;
+          }
+          if (ok) {
+            ++items0;
+            if (item.two) ++items1;
+          }
         }
       }
-    }
     }
   } else {  // ── softmax: warps 4-7 slot a, warps 8-11 slot b ──
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(AT_REG_SOFTMAX));

@@ -327,82 +327,82 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
   if (warp < 4) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(TC_REG_PRODUCER));
-  if (warp == 0) {
-    // ── TMA producer ──
-    if (lane == 0) {
-      asm volatile("prefetch.tensormap [%0];" ::"l"(&tmAh) : "memory");
-      asm volatile("prefetch.tensormap [%0];" ::"l"(&tmAl) : "memory");
-      asm volatile("prefetch.tensormap [%0];" ::"l"(&tmBh) : "memory");
-      asm volatile("prefetch.tensormap [%0];" ::"l"(&tmBl) : "memory");
-      int stage = 0;
-      uint32_t phase = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-        const int mt = t / num_n, nt = t - mt * num_n;
-        for (int kb = 0; kb < nkb; ++kb) {
-          if (!(ok = mbar_wait(&empty[stage], phase ^ 1, err))) break;
-          uint8_t *st = smem + stage * STAGE_BYTES;
-          mbar_expect_tx(&full[stage], STAGE_BYTES);
-          tma_load_2d(st, &tmAh, &full[stage], kb * TC_BK, mt * TC_BM);
-          tma_load_2d(st + A_BYTES, &tmAl, &full[stage], kb * TC_BK, mt * TC_BM);
-#pragma unroll
-          for (int h = 0; h < BN / 128; ++h) {  // 128-row boxes, contiguous in shared memory
-            tma_load_2d(st + 2 * A_BYTES + h * (B_BYTES * 128 / BN), &tmBh, &full[stage], kb * TC_BK,
-                        nt * BN + 128 * h);
-            tma_load_2d(st + 2 * A_BYTES + B_BYTES + h * (B_BYTES * 128 / BN), &tmBl, &full[stage], kb * TC_BK,
-                        nt * BN + 128 * h);
+    if (warp == 0) {
+      // ── TMA producer ──
+      if (lane == 0) {
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&tmAh) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&tmAl) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&tmBh) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&tmBl) : "memory");
+        int stage = 0;
+        uint32_t phase = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+          const int mt = t / num_n, nt = t - mt * num_n;
+          for (int kb = 0; kb < nkb; ++kb) {
+            if (!(ok = mbar_wait(&empty[stage], phase ^ 1, err))) break;
+            uint8_t *st = smem + stage * STAGE_BYTES;
+            mbar_expect_tx(&full[stage], STAGE_BYTES);
+            tma_load_2d(st, &tmAh, &full[stage], kb * TC_BK, mt * TC_BM);
+            tma_load_2d(st + A_BYTES, &tmAl, &full[stage], kb * TC_BK, mt * TC_BM);
+  #pragma unroll
+            for (int h = 0; h < BN / 128; ++h) {  // 128-row boxes, contiguous in shared memory
+              tma_load_2d(st + 2 * A_BYTES + h * (B_BYTES * 128 / BN), &tmBh, &full[stage], kb * TC_BK,
+                          nt * BN + 128 * h);
+              tma_load_2d(st + 2 * A_BYTES + B_BYTES + h * (B_BYTES * 128 / BN), &tmBl, &full[stage], kb * TC_BK,
+                          nt * BN + 128 * h);
+            }
+            if (++stage == TC_STAGES) {
+              stage = 0;
+              phase ^= 1;
+            }
           }
+        }
+        // Drain: wait until the MMAs consumed every issued stage, so no TMA
+        // write is still in flight when the CTA exits.
+        for (int s = 0; s < TC_STAGES && ok; ++s) {
+          ok = mbar_wait(&empty[stage], phase ^ 1, err);
           if (++stage == TC_STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
       }
-      // Drain: wait until the MMAs consumed every issued stage, so no TMA
-      // write is still in flight when the CTA exits.
-      for (int s = 0; s < TC_STAGES && ok; ++s) {
-        ok = mbar_wait(&empty[stage], phase ^ 1, err);
-        if (++stage == TC_STAGES) {
-          stage = 0;
-          phase ^= 1;
-        }
-      }
-    }
-  } else if (warp == 1) {
-    // ── MMA issuer ──
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      int i = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++i) {
-        const int buf = i & 1;
-        if (!(ok = mbar_wait(&tempty[buf], ((i >> 1) & 1) ^ 1, err))) break;
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t d = tmem + (uint32_t)(buf * BN);
-        for (int kb = 0; kb < nkb; ++kb) {
-          if (!(ok = mbar_wait(&full[stage], phase, err))) break;
+    } else if (warp == 1) {
+      // ── MMA issuer ──
+      if (lane == 0) {
+        int stage = 0;
+        uint32_t phase = 0;
+        int i = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++i) {
+          const int buf = i & 1;
+          if (!(ok = mbar_wait(&tempty[buf], ((i >> 1) & 1) ^ 1, err))) break;
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          uint8_t *st = smem + stage * STAGE_BYTES;
-          const uint64_t ah = umma_desc(st), al = umma_desc(st + A_BYTES);
-          const uint64_t bh = umma_desc(st + 2 * A_BYTES), bl = umma_desc(st + 2 * A_BYTES + B_BYTES);
-#pragma unroll
-          for (int k = 0; k < TC_BK / 16; ++k) {
-            const uint64_t adv = (uint64_t)((k * 32) >> 4);  // 16 bf16 = 32 bytes along K
-            umma_bf16(d, ah + adv, bh + adv, IDESC, (kb | k) ? 1u : 0u);
-            if (!b_lo_zero) umma_bf16(d, ah + adv, bl + adv, IDESC, 1u);
-            umma_bf16(d, al + adv, bh + adv, IDESC, 1u);
+          const uint32_t d = tmem + (uint32_t)(buf * BN);
+          for (int kb = 0; kb < nkb; ++kb) {
+            if (!(ok = mbar_wait(&full[stage], phase, err))) break;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            uint8_t *st = smem + stage * STAGE_BYTES;
+            const uint64_t ah = umma_desc(st), al = umma_desc(st + A_BYTES);
+            const uint64_t bh = umma_desc(st + 2 * A_BYTES), bl = umma_desc(st + 2 * A_BYTES + B_BYTES);
+  #pragma unroll
+            for (int k = 0; k < TC_BK / 16; ++k) {
+              const uint64_t adv = (uint64_t)((k * 32) >> 4);  // 16 bf16 = 32 bytes along K
+              umma_bf16(d, ah + adv, bh + adv, IDESC, (kb | k) ? 1u : 0u);
+              if (!b_lo_zero) umma_bf16(d, ah + adv, bl + adv, IDESC, 1u);
+              umma_bf16(d, al + adv, bh + adv, IDESC, 1u);
+            }
+            umma_commit(&empty[stage]);  // frees the stage once these MMAs complete
+            if (++stage == TC_STAGES) {
+              stage = 0;
+              phase ^= 1;
+            }
           }
-          umma_commit(&empty[stage]);  // frees the stage once these MMAs complete
-          if (++stage == TC_STAGES) {
-            stage = 0;
-            phase ^= 1;
-          }
+          if (ok) umma_commit(&tfull[buf]);
         }
-        if (ok) umma_commit(&tfull[buf]);
       }
     }
-  }
   } else {
     // ── epilogue: warpgroup `half` takes columns [half * BN/2, (half + 1) * BN/2) ──
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(TC_REG_EPILOGUE));

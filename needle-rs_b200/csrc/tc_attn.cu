@@ -17,7 +17,7 @@
 // (warps 2-3 idle), and warpgroups 1 / 2 run the softmax of slot a / slot b
 // (thread = one query row, all 128 keys of a tile held in registers; the
 // producer warpgroup hands its registers to them with setmaxnreg).  TMEM: S_a and S_b (128 columns each; P is written back over its own
-// S), O_a and O_b (64 columns each).  Per key tile j and slot x:
+// S), O_a and O_b (128 columns each).  Per key tile j and slot x:
 //   S_x = Q_x K_j^T      tcgen05.mma M128 N128 K16, A and B K-major in smem
 //   p = 2^(s*c - m)      c = hd^-0.5 * log2(e); m is raised only when a row's
 //                        maximum passes it by more than 8, so p <= 256; p and
@@ -325,7 +325,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 1) {  // S_a, S_b: 2 x 128 columns; O_a, O_b: 2 x 64 columns
+  if (warp == 1) {  // S_a, S_b: 2 x 128 columns; O_a, O_b: 2 x 128 columns
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(512));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");

@@ -609,7 +609,7 @@ bool Batch::prepare(const BatchSpec &spec, std::string &err) {
   NDL_CK(cudaMemcpyAsync(first_d, first.data(), B * 4, cudaMemcpyHostToDevice, st));
 
   // prefill chunks bounded by a token budget
-  const int64_t budget = std::max<int64_t>(262144, tmax_);
+  const int64_t budget = std::max<int64_t>(524288, tmax_);
   chunks_.clear();
   chunk_tok_max_ = 0;
   std::vector<int64_t> rel_all;

@@ -394,6 +394,25 @@ def test_pdl_and_graphs_change_nothing(full):
         assert np.array_equal(got[2], ref[2]), (graph, pdl)
 
 
+def test_multi_chunk_prefill_vs_oracle(full):
+    # Over 524,288 prompt tokens, so the prefill runs in two chunks: requests
+    # on both sides of the chunk boundary, and the first and last, match the
+    # oracle.
+    eng, ref = full
+    n = 1100
+    ids_in, off = wl.random_prompts(n, 490, 512, 8192, seed=18)
+    assert int(off[-1]) > 524288
+    prompts = [ids_in[off[i]:off[i + 1]] for i in range(n)]
+    steps = 2
+    ids, lens, lg = eng.run_batch_ids(prompts, steps, want_logits=True)
+    first2 = int(np.searchsorted(off, 524288, side="right")) - 1  # the request that opens chunk 2
+    tol = 2 * (ATOL + RTOL * 10.0)
+    for r in (0, first2 - 1, first2, n - 1):
+        rid, rmarg, rlg = ref.generate(prompts[r], steps, want_logits=True)
+        assert tokens_match(ids[r], rid, rmarg, tol), r
+        assert close(lg[r, 0], rlg[0]), (r, max_excess(lg[r, 0], rlg[0]))
+
+
 def test_wide_prefill_tiles_vs_oracle(full):
     # Over 9,500 prompt rows: every prefill projection (the fused QKV with its
     # norm + RoPE epilogue included) runs with 128 x 256 output tiles.

@@ -1,22 +1,33 @@
 #!/usr/bin/env python3
 """bench.py — batched Needle generation throughput on B200.
 
-Workload (per GPU, weak scaling): 4096 independent requests with prompt
-lengths uniform in [64, 512] and token ids uniform over the vocabulary,
-64 greedy decode steps each under a constrained-decoding mask (every step a
-random vocabulary bitmap with 5% of the entries allowed plus one forced
-token).  The model is random-init at the shipped config dims (d=512, 8 Q /
-4 KV heads, 12 encoder + 8 decoder layers, V=8192, INT4 group-32
-projections), in the reference's SafeTensors format.  One step = prefill of
-all prompts + the 64 decode steps.  Requests are sharded over ranks with no
-collective (each rank owns its own 4096 requests).
+Workload: 4096 independent requests with prompt lengths uniform in [64, 512]
+and token ids uniform over the vocabulary, 64 greedy decode steps each under a
+constrained-decoding mask (every step a random vocabulary bitmap with 5% of
+the entries allowed plus one forced token).  The model is random-init at the
+shipped config dims (d=512, 8 Q / 4 KV heads, 12 encoder + 8 decoder layers,
+V=8192, INT4 group-32 projections), in the reference's SafeTensors format.
+One step = prefill of all prompts + the 64 decode steps.
 
-  value  generated tokens/s, all ranks, inputs already in HBM, CUDA events on
-         the batch's stream, max over ranks
+Scaling: by default the one seeded 4096-request set is split across the ranks
+(one process per GPU) by the length-balanced LPT splitter
+(needle_shard_requests), with no collective on the data path: strong
+scaling, total work fixed.  With more than one rank a second, weak-scaled
+measurement (4096 requests on every GPU) is printed on its own line before
+the headline.  --requests-per-gpu N selects the weak-scaled workload for the
+headline instead.
+
+  value  generated tokens/s of all ranks, inputs already in HBM, CUDA events
+         on each batch's stream, max over ranks
   e2e    the same through needle_run_batch_ids with pinned host buffers:
          prompt ids + offsets + mask bitmaps in, token ids + lengths out
-  --impl reference   the CPU oracle (a C++ restatement of the reference Rust
-         path) on the host's cores, same metric, bounded request sample
+  parity the GPU tokens of the headline run against the oracle (a CPU
+         restatement of the reference path) on a prefix of rank 0's requests
+  --impl reference   the oracle on the host's cores, same metric, bounded
+         request sample
+
+Before the headline line, rank 0 (one GPU) prints the other INT4-path
+workloads as one {"ops": ...} line.
 """
 import argparse
 import ctypes
@@ -39,11 +50,18 @@ CLASS_NAMES = {1: "cross_attention", 2: "prefill_matmul", 3: "decode_matmul", 4:
 # classes whose algorithmic work is accounted (candidates for the roofline line)
 ROOFLINE_CLASSES = (1, 2, 3, 4, 5)
 # DRAM bytes (read + write) per algorithmic byte, from one ncu capture of the
-# class's kernel on the 512-request case; a launch reads each encoder K/V row
-# once, so its traffic grows in proportion to the rows and scales to the full
-# launch.  cross_attention: profiles/cross_attn_decode_512req.md
+# class's kernel on a 512-request batch; a cross-attention launch reads each
+# encoder K/V row once, so its traffic grows in proportion to the rows and
+# the ratio carries over to the full-size launch
 DRAM_PER_ALG_BYTE = {1: 1.017}
 METRIC = "generated tokens/s"
+PRECISION = ("f32 inputs, outputs and accumulation; tensor-core products formed from bf16 hi/lo splits "
+             "(hi*hi + hi*lo + lo*hi); INT4 weights dequantized to bf16 hi/lo planes at load")
+# Token parity (north_star): GPU and oracle token ids must agree wherever the
+# oracle's top-2 logit margin exceeds the logit tolerance; 2 * (1e-4 + 1e-3 *
+# 10) covers logits up to |10| on both of the two compared entries.
+MARGIN_TOL = 2 * (1e-4 + 1e-3 * 10.0)
+L2_BYTES = 126e6
 
 
 def pkg():
@@ -65,70 +83,134 @@ def env_rank():
             int(os.environ.get("LOCAL_RANK", 0)))
 
 
-def workload(args, wl, rank):
+def full_set(args, wl, n, seed_off=0):
+    ids, off = wl.random_prompts(n, args.min_len, args.max_len, 8192, seed=1000 + seed_off + args.seed)
+    masks = wl.random_masks(n, args.max_new, 8192, args.mask_frac, seed=2000 + seed_off + args.seed)
+    return ids, off, masks
+
+
+def subset(ids, off, masks, sel):
+    """The requests `sel` (indices into one CSR set) as their own CSR set."""
+    import numpy as np
+
+    lens = (off[1:] - off[:-1])[sel]
+    sub_off = np.zeros(len(sel) + 1, np.uint64)
+    np.cumsum(lens, out=sub_off[1:])
+    sub_ids = np.concatenate([ids[int(off[i]):int(off[i + 1])] for i in sel]) if len(sel) else ids[:0]
+    return np.ascontiguousarray(sub_ids), sub_off, np.ascontiguousarray(masks[sel])
+
+
+def workload(args, wl, nb, rank, world, per_gpu=None):
+    """(blob, ids, off, masks, total requests of all ranks) for this rank.
+
+    per_gpu=None: this rank's LPT share of one seeded args.total_requests set
+    (strong scaling).  per_gpu=n: n requests of this rank's own seed (weak)."""
+    import numpy as np
+
     blob = wl.random_model(seed=args.seed)
-    ids, off = wl.random_prompts(args.requests, args.min_len, args.max_len, 8192, seed=1000 + 7919 * rank + args.seed)
-    masks = wl.random_masks(args.requests, args.max_new, 8192, args.mask_frac, seed=2000 + 7919 * rank + args.seed)
-    return blob, ids, off, masks
+    if per_gpu:
+        ids, off, masks = full_set(args, wl, per_gpu, seed_off=7919 * rank)
+        return blob, ids, off, masks, per_gpu * world
+    ids, off, masks = full_set(args, wl, args.total_requests)
+    if world > 1:
+        sel = np.nonzero(nb.shard_requests(off, world) == rank)[0]
+        ids, off, masks = subset(ids, off, masks, sel)
+    return blob, ids, off, masks, args.total_requests
 
 
-def config_desc(args):
+def config_desc(args, world, per_gpu=None):
+    n = per_gpu if per_gpu else args.total_requests
+    where = (f"{n} requests per GPU" if per_gpu else
+             f"{n} requests in total, split across {world} GPU(s) by the LPT splitter")
     return {
-        "workload": (f"{args.requests} requests per GPU, prompt length U[{args.min_len},{args.max_len}], "
-                     f"{args.max_new} greedy steps, {args.mask_frac:.0%} random vocab mask + 1 forced token; "
-                     "random-init model at the shipped dims (d=512, 8/4 heads, 12+8 layers, V=8192, INT4 g32)"),
-        "requests_per_gpu": args.requests,
+        "workload": (f"{where}, prompt length U[{args.min_len},{args.max_len}], {args.max_new} greedy steps, "
+                     f"{args.mask_frac:.0%} random vocab mask + 1 forced token; random-init model at the shipped "
+                     "dims (d=512, 8/4 heads, 12+8 layers, V=8192, INT4 g32)"),
+        "requests": n * (world if per_gpu else 1),
+        "requests_per_gpu": per_gpu if per_gpu else None,
         "prompt_len": [args.min_len, args.max_len],
         "max_new": args.max_new,
         "mask_fraction": args.mask_frac,
-        "parallelism": "request-sharded, no collective",
-        "l2": "inputs larger than L2 (encoder K/V about 19 GB per GPU)",
+        "parallelism": f"request-sharded over {world} GPU(s), no collective",
+        "precision": PRECISION,
+        "l2": "inputs larger than L2 (encoder K/V about 19 GB for 4096 requests)",
     }
 
 
 _ORACLE = {}
 
 
-def cpu_sample(args, blob, ids, off, masks, max_seconds):
-    """Oracle (C++ restatement of the reference path) on this host's cores
-    over a bounded prefix of the same requests -> (tokens/s, threads, n)."""
-    import numpy as np
+def oracle_model(blob):
     import oracle
 
+    if _ORACLE.get("key") != id(blob):
+        _ORACLE.update(key=id(blob), model=oracle.Model(data=blob))
+    return _ORACLE["model"]
+
+
+def cpu_sample(args, blob, ids, off, masks, max_seconds, min_req=0):
+    """Oracle (C++ restatement of the reference path) on this host's cores
+    over a bounded prefix of the requests -> (tokens/s, threads, requests,
+    seconds, token ids, margins)."""
+    import numpy as np
+
     threads = os.cpu_count() or 1
-    key = id(blob)
-    if _ORACLE.get("key") != key:
-        _ORACLE.update(key=key, model=oracle.Model(data=blob))
-    m = _ORACLE["model"]
+    m = oracle_model(blob)
+    n_all = off.size - 1
     done_req, t_total = 0, 0.0
-    n = min(args.requests, max(threads, 8))
-    while done_req < args.requests:
-        r1 = min(args.requests, done_req + n)
+    n = min(n_all, max(threads, 8))
+    toks, margs = [], []
+    while done_req < n_all:
+        r1 = min(n_all, done_req + n)
         sub_off = off[done_req:r1 + 1] - off[done_req]
         sub_ids = ids[int(off[done_req]):int(off[r1])]
         t0 = time.perf_counter()
-        m.run_batch(sub_ids, sub_off, args.max_new, mask_bits=masks[done_req:r1], n_threads=threads)
+        out, _, marg = m.run_batch(sub_ids, sub_off, args.max_new, mask_bits=masks[done_req:r1], n_threads=threads)
         t_total += time.perf_counter() - t0
+        toks.append(out)
+        margs.append(marg)
         done_req = r1
-        if t_total >= max_seconds:
+        if t_total >= max_seconds and done_req >= min_req:
             break
-    return done_req * args.max_new / t_total, threads, done_req, t_total
+    return (done_req * args.max_new / t_total, threads, done_req, t_total, np.concatenate(toks),
+            np.concatenate(margs))
+
+
+def parity(gpu_ids, ref_ids, ref_margins):
+    """GPU tokens vs the oracle's under the margin rule: exact up to the
+    first step whose oracle top-2 margin is within MARGIN_TOL."""
+    matched, ties, bad = 0, 0, []
+    for r in range(ref_ids.shape[0]):
+        ok = True
+        for s in range(ref_ids.shape[1]):
+            if ref_margins[r, s] <= MARGIN_TOL:
+                ties += 1
+                break
+            if gpu_ids[r, s] != ref_ids[r, s]:
+                ok = False
+                bad.append({"request": r, "step": s, "margin": float(ref_margins[r, s])})
+                break
+        matched += ok
+    return {"requests": int(ref_ids.shape[0]), "tokens_match": not bad, "requests_matched": matched,
+            "stopped_at_tie": ties, "margin_tol": MARGIN_TOL,
+            "first_divergence_margin": bad[0]["margin"] if bad else None, "divergences": bad[:4],
+            "checker": "oracle (reference path restated in C++, AVX2 order), same requests and masks"}
 
 
 def run_reference(args):
     rank, world, _ = env_rank()
     if rank != 0:
         return 0
-    import numpy as np  # noqa: F401
-
     _, wl = pkg()
-    blob, ids, off, masks = workload(args, wl, 0)
+    per_gpu = args.requests_per_gpu
+    blob = wl.random_model(seed=args.seed)
+    ids, off, masks = full_set(args, wl, per_gpu if per_gpu else args.total_requests)
     vals = []
     info = None
     for _ in range(args.warmup):
         cpu_sample(args, blob, ids, off, masks, args.cpu_seconds / 4)
     for _ in range(args.steps):
-        v, threads, n, t = cpu_sample(args, blob, ids, off, masks, args.cpu_seconds)
+        v, threads, n, t, _, _ = cpu_sample(args, blob, ids, off, masks, args.cpu_seconds)
         vals.append(v)
         info = (threads, n, t)
     value = statistics.mean(vals)
@@ -136,18 +218,15 @@ def run_reference(args):
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * n * args.max_new / value,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": config_desc(args),
+        "higher_is_better": True, "scaling": "weak" if per_gpu else "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": config_desc(args, world, per_gpu),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
-                         "sample": f"first {n} of the {args.requests} requests per step ({t:.1f} s), one request "
+                         "sample": f"first {n} requests of the seeded set per step ({t:.1f} s), one request "
                                    f"per host thread; the reference Rust path restated in C++ (oracle/)"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
-
-
-L2_BYTES = 126e6
 
 
 def _graph_ms(torch, launch, reps=5):
@@ -174,6 +253,22 @@ def _graph_ms(torch, launch, reps=5):
     return ms
 
 
+def _events_ms(torch, launch, reps=5):
+    """launch(stream_handle) eagerly, reps times, timed with CUDA events on
+    that stream after one warm-up call."""
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        launch(s.cuda_stream)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(reps):
+            launch(s.cuda_stream)
+        e1.record(s)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
 def _cpu_us(fn, budget_s=0.3, min_reps=3):
     fn()
     t0, n = time.perf_counter(), 0
@@ -187,17 +282,22 @@ def op_suite(args, nb, wl, torch, np, pk, eng, blob):
     """The other INT4-path workloads, measured beside the headline line.
 
     int4_gemv   one INT4 matvec, x f32 [1, 512], W [N=2048, K=512] group-32
-                (quant.rs:160-297): a chain of R launches over R distinct
-                weight copies (R x 665,600 B > 2 x L2) captured in one CUDA
-                graph, each launch a separate op; plain launches and
-                programmatic-dependent ("overlap") launches.
+                (quant.rs:160-297).  single_launch: one launch over N = 2048 x
+                512 columns (the same matvec on 512 distinct weight copies
+                side by side, 335 MB > 2 x L2): the kernel's streaming rate.
+                chain: 512 dependent launches of the N=2048 op, each on its
+                own weight copy, in one CUDA graph (plain and programmatic-
+                dependent "overlap" launches): per-op latency.
     int4_sweep  M in {1, 8, 64, 512, 4096} x (N, K) in {(512,512), (2048,512),
                 (512,2048), (8192,512)} through a prepared plan: CUDA-core
-                matvec up to 8 rows, tcgen05 from 9 rows; chains of
-                R ops on distinct weight and x copies (over 2 x L2 per replay).
+                matvec up to 8 rows, tcgen05 from 9 rows; chains of R ops on
+                distinct weight and x copies (over 2 x L2 per replay).
     single_request  one request, 256-token prompt, 64 greedy steps, no mask,
                 through needle_run_batch_ids (host buffers).
-    mlp_block   ffn_forward over T = 256 tokens, d 512 -> 2048 -> 512, drelu.
+    mlp_block   the MLP block over T = 256 tokens, d 512 -> 2048 -> 512,
+                drelu: the prepared tensor-core plan (needle_ffn_plan_forward)
+                and the allocation-free CUDA-core entry point
+                (needle_ffn_forward_noalloc).
     Each carries the oracle's single-thread time of the same work (cpu_us:
     the reference path restated in C++, AVX2 order)."""
     import oracle
@@ -212,12 +312,29 @@ def op_suite(args, nb, wl, torch, np, pk, eng, blob):
     # ── config 0: INT4 GEMV ──
     M, N, K = 1, 2048, 512
     x, packed, scales = wl.int4_case(M, N, K, seed=0)
+    G = scales.shape[0]
     R = 512
+    ref = oracle.matmul(packed, scales, K, N, x, path=1)
+    res = {"shape": [M, N, K], "bytes_per_op": alg_bytes(M, N, K)}
+    # single launch over R copies side by side: W [K/2][R*N], scales [G][R*N]
+    Wwide = dev(np.tile(packed.reshape(K // 2, N), (1, R)))
+    Swide = dev(np.tile(scales, (1, R)))
+    xd = dev(x)
+    Ywide = torch.empty((1, R * N), device="cuda")
+
+    def wide(st):
+        nb.int4_matmul(xd.data_ptr(), M, K, Wwide.data_ptr(), Swide.data_ptr(), R * N, G, Ywide.data_ptr(), stream=st)
+    ms = _events_ms(torch, wide, reps=10)
+    wb = alg_bytes(M, R * N, K)
+    gbs = wb / (ms / 1e3) / 1e9
+    gotw = Ywide.cpu().numpy().reshape(R, N)
+    res["single_launch"] = {"columns": R * N, "bytes": wb, "us": 1e3 * ms, "GB/s": gbs,
+                            "frac_of_measured_hbm": gbs / hbm, "frac_of_8TBs": gbs / 8000.0,
+                            "max_abs_err_vs_oracle": float(np.max(np.abs(gotw - ref[0][None, :])))}
+    del Wwide, Swide, Ywide
     W = dev(np.broadcast_to(packed.reshape(1, -1), (R, packed.size)))
     S = dev(np.broadcast_to(scales.reshape(1, -1), (R, scales.size)))
-    xd = dev(x)
     Y = torch.empty((R, N), device="cuda")
-    G = scales.shape[0]
 
     def chain(overlap):
         def launch(st):
@@ -226,15 +343,13 @@ def op_suite(args, nb, wl, torch, np, pk, eng, blob):
                                stream=st, overlap=overlap)
         return launch
 
-    ref = oracle.matmul(packed, scales, K, N, x, path=1)
-    res = {"shape": [M, N, K], "copies": R, "bytes_per_op": alg_bytes(M, N, K)}
-    for name, ov in (("plain", False), ("overlap", True)):
+    for name, ov in (("chain", False), ("chain_overlap", True)):
         ms = _graph_ms(torch, chain(ov))
         gbs = R * alg_bytes(M, N, K) / (ms / 1e3) / 1e9
-        res[name] = {"us_per_op": 1e3 * ms / R, "GB/s": gbs, "frac_of_measured_hbm": gbs / hbm,
-                     "frac_of_8TBs": gbs / 8000.0}
-    got = Y[R - 1].cpu().numpy()
-    res["max_abs_err_vs_oracle"] = float(np.max(np.abs(got - ref)))
+        res[name] = {"ops": R, "us_per_op": 1e3 * ms / R, "GB/s": gbs, "frac_of_measured_hbm": gbs / hbm,
+                     "note": "dependent launches: per-op latency, not streaming rate"}
+    got = Y.cpu().numpy()
+    res["max_abs_err_vs_oracle"] = float(np.max(np.abs(got - ref[0][None, :])))
     res["cpu_us"] = _cpu_us(lambda: oracle.matmul(packed, scales, K, N, x, path=1))
     out["int4_gemv"] = res
     del W, S, Y
@@ -250,16 +365,18 @@ def op_suite(args, nb, wl, torch, np, pk, eng, blob):
             Wd = dev(np.broadcast_to(packed.reshape(1, -1), (R, packed.size)))
             Sd = dev(np.broadcast_to(scales.reshape(1, -1), (R, scales.size)))
             Xd = dev(np.broadcast_to(x.reshape(1, -1), (R, x.size)))
-            Yd = torch.empty((M, N), device="cuda")
+            Yd = torch.empty((R, M, N), device="cuda")
             plans = [nb.Int4Plan(Wd[r].data_ptr(), Sd[r].data_ptr(), K, N, G, M) for r in range(R)]
 
             def launch(st, plans=plans, Xd=Xd, Yd=Yd, M=M):
                 for r, pl in enumerate(plans):
-                    pl.matmul(Xd[r].data_ptr(), M, Yd.data_ptr(), stream=st, overlap=M <= 8)
+                    pl.matmul(Xd[r].data_ptr(), M, Yd[r].data_ptr(), stream=st, overlap=True)
             ms = _graph_ms(torch, launch, reps=3)
             plans[0].status()
             t = ms / 1e3 / R
             rows = min(M, 64)
+            ref = oracle.matmul(packed, scales, K, N, x[:rows], path=1)
+            err = float(max(np.max(np.abs(Yd[r, :rows].cpu().numpy() - ref)) for r in (0, R - 1)))
             cpu = _cpu_us(lambda: oracle.matmul(packed, scales, K, N, x[:rows], path=1), budget_s=0.2,
                           min_reps=1) * (M / rows)
             path = "tcgen05" if M > 8 else "cuda-core gemv"
@@ -267,7 +384,7 @@ def op_suite(args, nb, wl, torch, np, pk, eng, blob):
             tfl = 2.0 * M * N * K / t / 1e12
             sweep.append({"M": M, "N": N, "K": K, "path": path, "us": 1e6 * t, "GB/s": gbs,
                           "frac_hbm": gbs / hbm, "TFLOP/s": tfl, "frac_bf16": tfl / tcp, "cpu_us": cpu,
-                          "copies": R})
+                          "copies": R, "max_abs_err_vs_oracle": err})
             for pl in plans:
                 pl.close()
             del Wd, Sd, Xd, Yd
@@ -283,16 +400,14 @@ def op_suite(args, nb, wl, torch, np, pk, eng, blob):
         t0 = time.perf_counter()
         gpu_ids, _ = eng.run_batch_ids(prompt, 64)
         times.append(time.perf_counter() - t0)
-    if _ORACLE.get("key") != id(blob):
-        _ORACLE.update(key=id(blob), model=oracle.Model(data=blob))
     t0 = time.perf_counter()
-    ref_ids = _ORACLE["model"].generate(ids, 64)[0]
+    ref_ids, ref_marg = oracle_model(blob).generate(ids, 64)
     cpu_s = time.perf_counter() - t0
     ms = 1e3 * statistics.median(times)
+    p1 = parity(np.asarray(gpu_ids[:1]), np.asarray(ref_ids)[None, :], np.asarray(ref_marg)[None, :])
     out["single_request"] = {"prompt": 256, "steps": 64, "ms": ms, "tokens/s": 64 / (ms / 1e3),
-                             "cpu_ms": 1e3 * cpu_s, "cpu_cores": 1,
-                             "first_tokens_match": bool(np.array_equal(np.asarray(gpu_ids[0][:8]),
-                                                                       np.asarray(ref_ids[:8])))}
+                             "us_per_token": 1e3 * ms / 64, "cpu_ms": 1e3 * cpu_s, "cpu_cores": 1,
+                             "tokens_match": p1["tokens_match"]}
 
     # ── config 2: MLP block ──
     T, d, ff = 256, 512, 2048
@@ -301,19 +416,34 @@ def op_suite(args, nb, wl, torch, np, pk, eng, blob):
     g, u, dn = wl.random_int4(rng, d, ff), wl.random_int4(rng, d, ff), wl.random_int4(rng, ff, d)
     gd, ud, dd = [dev(a) for a in g], [dev(a) for a in u], [dev(a) for a in dn]
     xd, od = dev(x), torch.empty((T, d), device="cuda")
-
-    def mlp(st):
-        for _ in range(8):
-            nb.ffn_forward_noalloc(xd.data_ptr(), T, d, ff, [a.data_ptr() for a in gd], [a.data_ptr() for a in ud],
-                                   [a.data_ptr() for a in dd], 0, od.data_ptr(), stream=st)
-    ms = _graph_ms(torch, mlp) / 8
-    ref0 = oracle.ffn_forward(g, u, dn, d, ff, x[0], 0)
+    refs = np.stack([oracle.ffn_forward(g, u, dn, d, ff, x[t], 0) for t in (0, T // 2, T - 1)])
     cpu = _cpu_us(lambda: [oracle.ffn_forward(g, u, dn, d, ff, x[t], 0) for t in range(16)], budget_s=0.3,
                   min_reps=1) * (T / 16)
     fl = 3 * 2.0 * T * d * ff
-    out["mlp_block"] = {"T": T, "d": d, "d_ff": ff, "activation": "drelu", "us": 1e3 * ms,
-                        "TFLOP/s": fl / (ms / 1e3) / 1e12, "cpu_us": cpu,
-                        "max_abs_err_row0": float(np.max(np.abs(od[0].cpu().numpy() - ref0)))}
+    mlp = {"T": T, "d": d, "d_ff": ff, "activation": "drelu", "flops": fl, "cpu_us": cpu}
+    plan = nb.FfnPlan(d, ff, [a.data_ptr() for a in gd], [a.data_ptr() for a in ud], [a.data_ptr() for a in dd],
+                      max_t=T)
+    try:
+        def mlp_plan(st):
+            for _ in range(8):
+                plan.forward(xd.data_ptr(), T, 0, od.data_ptr(), stream=st)
+        ms = _graph_ms(torch, mlp_plan) / 8
+        plan.status()
+        err = float(np.max(np.abs(od.cpu().numpy()[[0, T // 2, T - 1]] - refs)))
+        mlp["tensor_core_plan"] = {"us": 1e3 * ms, "TFLOP/s": fl / (ms / 1e3) / 1e12, "max_abs_err_vs_oracle": err,
+                                   "entry": "needle_ffn_plan_forward"}
+    finally:
+        plan.close()
+
+    def mlp_noalloc(st):
+        for _ in range(8):
+            nb.ffn_forward_noalloc(xd.data_ptr(), T, d, ff, [a.data_ptr() for a in gd], [a.data_ptr() for a in ud],
+                                   [a.data_ptr() for a in dd], 0, od.data_ptr(), stream=st)
+    ms = _graph_ms(torch, mlp_noalloc) / 8
+    err = float(np.max(np.abs(od.cpu().numpy()[[0, T // 2, T - 1]] - refs)))
+    mlp["cuda_core_noalloc"] = {"us": 1e3 * ms, "TFLOP/s": fl / (ms / 1e3) / 1e12, "max_abs_err_vs_oracle": err,
+                                "entry": "needle_ffn_forward_noalloc"}
+    out["mlp_block"] = mlp
     return out
 
 
@@ -363,7 +493,10 @@ def main():
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--requests", type=int, default=4096, help="requests per GPU")
+    ap.add_argument("--total-requests", type=int, default=4096,
+                    help="requests of the one seeded set split across the ranks (strong scaling)")
+    ap.add_argument("--requests-per-gpu", type=int, default=0,
+                    help="weak scaling instead: this many requests on every rank")
     ap.add_argument("--max-new", type=int, default=64)
     ap.add_argument("--min-len", type=int, default=64)
     ap.add_argument("--max-len", type=int, default=512)
@@ -373,6 +506,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-ops", action="store_true", help="skip the INT4 op / single-request / MLP measurements")
+    ap.add_argument("--no-weak", action="store_true", help="skip the weak-scaled line at more than one rank")
     ap.add_argument("--profile-run", action="store_true",
                     help="one untimed run of the workload and exit (for ncu launch lists)")
     args = ap.parse_args()
@@ -404,16 +538,18 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    blob, ids, off, masks = workload(args, wl, rank)
+    per_gpu = args.requests_per_gpu or None
+    blob, ids, off, masks, n_total = workload(args, wl, nb, rank, world, per_gpu)
+    n_req = off.size - 1
     eng = nb.NeedleEngine.from_bytes(blob, "a\nb\n", device=local)
     batch = eng.prepare_batch(ids, off, args.max_new, masks, flags=0)
     stream = torch.cuda.ExternalStream(batch.stream, device=local)
-    tokens_per_step = args.requests * args.max_new
+    tokens_total = n_total * args.max_new
     if args.profile_run:
         batch.run()
         batch.sync()
         print(json.dumps({"profile_run": True, "kernel_launches": batch.kernel_launches(),
-                          "requests": args.requests}), flush=True)
+                          "requests": n_req}), flush=True)
         batch.close()
         eng.close()
         return 0
@@ -440,7 +576,6 @@ def main():
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     launches = 0
-    dom_ms = dom_n = dom_fl = dom_by = 0.0
     e0.record(stream)
     for _ in range(args.steps):
         batch.run()
@@ -450,11 +585,10 @@ def main():
     torch.cuda.synchronize()
     clk = clocks.stop()
     barrier()
-    ms, n, fl, by = batch.kernel_timing()  # events of the last timed run
-    dom_ms, dom_n, dom_fl, dom_by = ms, n, fl, by
+    dom_ms, dom_n, dom_fl, dom_by = batch.kernel_timing()  # events of the last timed run
     elapsed = e0.elapsed_time(e1)
     ms_step = max_over_ranks(elapsed / args.steps)
-    value = world * tokens_per_step / (ms_step / 1e3)
+    value = tokens_total / (ms_step / 1e3)
     out_ids, lens = batch.results()
     assert int(lens.min()) == args.max_new
 
@@ -471,12 +605,12 @@ def main():
         _, ids_p = pinned(ids)
         _, off_p = pinned(off)
         _, mask_p = pinned(masks)
-        _, out_p = pinned(np.zeros((args.requests, args.max_new), np.uint32))
-        _, lens_p = pinned(np.zeros(args.requests, np.uint32))
+        _, out_p = pinned(np.zeros((n_req, args.max_new), np.uint32))
+        _, lens_p = pinned(np.zeros(n_req, np.uint32))
         L = nb.lib()
 
         def call():
-            rc = L.needle_run_batch_ids(eng._h, nb._p(ids_p), nb._p(off_p), args.requests, args.max_new,
+            rc = L.needle_run_batch_ids(eng._h, nb._p(ids_p), nb._p(off_p), n_req, args.max_new,
                                         nb._p(mask_p), 0, nb._p(out_p), nb._p(lens_p))
             if rc != 0:
                 raise nb.NeedleError(nb.last_error())
@@ -491,9 +625,10 @@ def main():
             times.append(time.perf_counter() - t0)
         e2e_s = max_over_ranks(statistics.mean(times))
         h2d = ids.nbytes + off.nbytes + masks.nbytes
-        d2h = args.requests * args.max_new * 4 + args.requests * 4
-        e2e = {"value": world * tokens_per_step / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": int(h2d),
+        d2h = n_req * args.max_new * 4 + n_req * 4
+        e2e = {"value": tokens_total / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": int(h2d),
                "d2h_bytes_per_step": int(d2h), "ms_per_step": 1e3 * e2e_s,
+               "bytes_are": "rank 0's copies (every rank copies its own shard)",
                "tokens_match_device_run": bool(np.array_equal(out_p, out_ids))}
 
     # ── roofline of the dominant kernel (its launches in the last timed run) ──
@@ -520,21 +655,27 @@ def main():
                                              "this GPU, after the timed region"})
     if dom in DRAM_PER_ALG_BYTE:
         roof["traffic"] = DRAM_PER_ALG_BYTE[dom] * dom_by / max(dom_n, 1)
-        roof["traffic_source"] = "ncu dram__bytes_read.sum + dram__bytes_write.sum per algorithmic byte, 512-request capture, scaled"
+        roof["traffic_source"] = ("ncu dram__bytes_read.sum + dram__bytes_write.sum per algorithmic byte, "
+                                  "512-request capture, scaled to this launch's rows")
 
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, threads, n, t = cpu_sample(args, blob, ids, off, masks, args.cpu_seconds)
-        cpu = {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
-               "sample": f"first {n} of the {args.requests} requests ({t:.1f} s), one request per host thread; "
-                         "the reference Rust path restated in C++ (oracle/)"}
+    # ── oracle checks: CPU baseline (one GPU) and token parity (every run) ──
+    cpu = par = None
+    if rank == 0:
+        budget = args.cpu_seconds if (world == 1 and not args.no_cpu_baseline) else 0.0
+        v, threads, n, t, ref_ids, ref_marg = cpu_sample(args, blob, ids, off, masks, budget,
+                                                         min_req=min(n_req, 16))
+        par = parity(out_ids[:n], ref_ids, ref_marg)
+        if world == 1 and not args.no_cpu_baseline:
+            cpu = {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
+                   "sample": f"first {n} of the {n_req} requests ({t:.1f} s), one request per host thread; "
+                             "the reference Rust path restated in C++ (oracle/)"}
 
     # ── the decode path against the HBM roofline: its algorithmic bytes (the
     # encoder K/V rows read by cross-attention every step, the self-attention
     # K/V cache, the decode projections and the head) over the summed time of
     # those kernel classes in the breakdown run ──
     L_dec = 8
-    self_kv = L_dec * args.requests * (args.max_new * (args.max_new + 1) // 2) * 2 * 256 * 4
+    self_kv = L_dec * n_req * (args.max_new * (args.max_new + 1) // 2) * 2 * 256 * 4
     dec_cls = ("cross_attention", "self_attention", "decode_matmul", "head_mask_argmax")
     dec_ms = sum(breakdown[c]["ms"] for c in dec_cls)
     dec_bytes = (breakdown["cross_attention"]["bytes"] + self_kv + breakdown["decode_matmul"]["bytes"]
@@ -542,23 +683,66 @@ def main():
     dec_gbs = dec_bytes / (dec_ms / 1e3) / 1e9
     decode_path = {"bytes_per_step": dec_bytes, "ms_per_step": dec_ms, "GB/s": dec_gbs,
                    "frac_of_measured_hbm": dec_gbs / pk["hbm_gbs"], "frac_of_8TBs": dec_gbs / 8000.0,
-                   "classes": list(dec_cls)}
+                   "classes": list(dec_cls), "rank": rank}
+
+    batch.close()
+
+    # ── weak-scaled second measurement (4096 requests on every GPU) ──
+    weak = None
+    if world > 1 and not per_gpu and not args.no_weak:
+        wblob, wids, woff, wmasks, wtot = workload(args, wl, nb, rank, world, args.total_requests)
+        wb = eng.prepare_batch(wids, woff, args.max_new, wmasks, flags=0)
+        wstream = torch.cuda.ExternalStream(wb.stream, device=local)
+        wsteps = max(1, min(args.steps, 3))
+        for _ in range(3):
+            wb.run()
+        wb.sync()
+        barrier()
+        torch.cuda.synchronize()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record(wstream)
+        for _ in range(wsteps):
+            wb.run()
+        a1.record(wstream)
+        torch.cuda.synchronize()
+        barrier()
+        wms = max_over_ranks(a0.elapsed_time(a1) / wsteps)
+        weak = {"weak_scaling": {"requests_per_gpu": args.total_requests, "n_gpus": world, "steps": wsteps,
+                                 "warmup": 3, "ms_per_step": wms, "unit": "tokens/s",
+                                 "value": wtot * args.max_new / (wms / 1e3),
+                                 "note": "every GPU runs its own 4096-request set; device-resident inputs, "
+                                         "CUDA events, max over ranks"}}
+        wb.close()
 
     ops = None
     if rank == 0 and world == 1 and not args.no_ops:
         ops = op_suite(args, nb, wl, torch, np, pk, eng, blob)
 
     if rank == 0:
+        if ops is not None:
+            print(json.dumps({"ops": ops}), flush=True)
+        if weak is not None:
+            print(json.dumps(weak), flush=True)
+        ops_summary = None
+        if ops is not None:
+            g = ops["int4_gemv"]
+            ops_summary = {
+                "int4_gemv_single_launch_GBs": g["single_launch"]["GB/s"],
+                "int4_gemv_single_launch_frac_hbm": g["single_launch"]["frac_of_measured_hbm"],
+                "int4_gemv_chain_us_per_op": g["chain_overlap"]["us_per_op"],
+                "single_request_tokens_s": ops["single_request"]["tokens/s"],
+                "mlp_block_us": ops["mlp_block"]["tensor_core_plan"]["us"],
+            }
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config_desc(args),
-            "e2e": e2e, "gpu_launches": int(launches), "roofline": roof, "cpu_baseline": cpu, "clocks": clk,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "weak" if per_gpu else "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": config_desc(args, world, per_gpu), "e2e": e2e, "gpu_launches": int(launches),
+            "roofline": roof, "cpu_baseline": cpu, "parity": par, "clocks": clk,
             "kernel_breakdown_ms": {k: round(v["ms"], 3) for k, v in breakdown.items()},
-            "decode_path": decode_path, "ops": ops,
+            "decode_path": decode_path, "ops_summary": ops_summary,
         }
         print(json.dumps(line), flush=True)
-    batch.close()
     eng.close()
     if world > 1:
         dist.destroy_process_group()

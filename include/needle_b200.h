@@ -241,6 +241,40 @@ int needle_ffn_forward_noalloc(const float *x, size_t T, size_t d_model, size_t 
                                const uint8_t *down_data, const float *down_scales, int activation, float *out,
                                void *stream);
 
+/* A prepared MLP block for repeated calls (the engine's own form of
+ * ffn_forward, crates/needle-core/src/ffn.rs:19-56): gate and up interleaved
+ * into one INT4 weight, the tensor-core bf16 hi/lo staging of it and of
+ * down, and a workspace for up to max_tokens rows, all allocated here.
+ * needle_ffn_plan_forward is asynchronous in `stream` and allocates nothing;
+ * from 9 tokens it runs x -> planes, one gate|up GEMM whose epilogue writes
+ * act(gate) * up straight as the down GEMM's operand planes, and the down
+ * GEMM.  Calls on one plan share its workspace and must be ordered (one
+ * stream).  needle_ffn_plan_status synchronises the device and returns -1
+ * if a bounded wait inside a tensor-core launch expired since the last
+ * check.  Activations as needle_ffn_forward. */
+typedef struct NeedleFfnPlan NeedleFfnPlan;
+NeedleFfnPlan *needle_ffn_plan_create(size_t d_model, size_t d_ff, const uint8_t *gate_data, const float *gate_scales,
+                                      const uint8_t *up_data, const float *up_scales, const uint8_t *down_data,
+                                      const float *down_scales, size_t max_tokens, void *stream);
+int needle_ffn_plan_forward(NeedleFfnPlan *plan, const float *x, size_t T, int activation, float *out, void *stream);
+int needle_ffn_plan_status(NeedleFfnPlan *plan);
+void needle_ffn_plan_free(NeedleFfnPlan *plan);
+
+/* ── SafeTensors reader (crates/needle-infer/src/safetensors.rs:43-128) ── */
+/* The weight-file reader needle_load uses, on a host buffer: header JSON with
+ * a string-valued __metadata__ object, dtypes F32 / BF16 / F16 / I8 and the
+ * packed I4.  needle_safetensors_parse returns NULL (error set) for a
+ * malformed buffer (SafeTensors::from_bytes); _metadata returns a borrowed
+ * string valid until _free, or NULL when the key is absent (get_metadata);
+ * _get_f32 converts a tensor to f32 (get_f32), writes min(count, cap) values
+ * and returns the count, or (size_t)-1 when the tensor is absent or is an I4
+ * tensor whose byte count does not match its shape. */
+typedef struct NeedleSafeTensors NeedleSafeTensors;
+NeedleSafeTensors *needle_safetensors_parse(const uint8_t *data, size_t len);
+const char *needle_safetensors_metadata(const NeedleSafeTensors *st, const char *key);
+size_t needle_safetensors_get_f32(const NeedleSafeTensors *st, const char *name, float *out, size_t cap);
+void needle_safetensors_free(NeedleSafeTensors *st);
+
 /* Measurement helper (no reference counterpart): the device's streaming-read
  * bandwidth in GB/s, from `iters` timed grid-stride float4 read passes over a
  * fresh `bytes` buffer (allocated and freed here) on the current device's

@@ -105,6 +105,14 @@ def lib():
             "needle_ffn_forward": (I, [P, S, S, S, P, P, P, P, P, P, I, P, P]),
             "needle_ffn_forward_noalloc": (I, [P, S, S, S, P, P, P, P, P, P, I, P, P]),
             "needle_hbm_read_gbs": (I, [S, I, P]),
+            "needle_ffn_plan_create": (P, [S, S, P, P, P, P, P, P, S, P]),
+            "needle_ffn_plan_forward": (I, [P, P, S, I, P, P]),
+            "needle_ffn_plan_status": (I, [P]),
+            "needle_ffn_plan_free": (None, [P]),
+            "needle_safetensors_parse": (P, [P, S]),
+            "needle_safetensors_metadata": (C.c_char_p, [P, C.c_char_p]),
+            "needle_safetensors_get_f32": (S, [P, C.c_char_p, P, S]),
+            "needle_safetensors_free": (None, [P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -423,6 +431,69 @@ def int4_dequantize(data_ptr, scales_ptr, K, N, G, out_ptr, stream=None):
 
 def ffn_forward(x_ptr, T, d, ff, g, u, dn, act, out_ptr, stream=None):
     _check(lib().needle_ffn_forward(x_ptr, T, d, ff, g[0], g[1], u[0], u[1], dn[0], dn[1], act, out_ptr, stream))
+
+
+class FfnPlan:
+    """A prepared MLP block (needle_ffn_plan_*): gate / up / down as
+    (packed, scales) device-pointer pairs in the reference layout; forward()
+    is asynchronous and allocates nothing."""
+
+    def __init__(self, d, ff, g, u, dn, max_t, stream=None):
+        self.d, self.ff, self.max_t = d, ff, max_t
+        self._h = lib().needle_ffn_plan_create(d, ff, g[0], g[1], u[0], u[1], dn[0], dn[1], max_t, stream)
+        if not self._h:
+            raise NeedleError(last_error() or "needle_ffn_plan_create failed")
+
+    def forward(self, x_ptr, T, act, out_ptr, stream=None):
+        _check(lib().needle_ffn_plan_forward(self._h, x_ptr, T, act, out_ptr, stream))
+
+    def status(self):
+        _check(lib().needle_ffn_plan_status(self._h))
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().needle_ffn_plan_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class SafeTensors:
+    """The library's SafeTensors reader (SafeTensors::from_bytes / get_metadata
+    / get_f32 of crates/needle-infer/src/safetensors.rs) on a bytes buffer."""
+
+    def __init__(self, data):
+        self._buf = np.frombuffer(bytes(data), np.uint8)
+        self._h = lib().needle_safetensors_parse(_p(self._buf) if self._buf.size else None, self._buf.size)
+        if not self._h:
+            raise NeedleError(last_error() or "SafeTensors parse failed")
+
+    def get_metadata(self, key):
+        v = lib().needle_safetensors_metadata(self._h, key.encode())
+        return None if v is None else v.decode()
+
+    def get_f32(self, name):
+        n = lib().needle_safetensors_get_f32(self._h, name.encode(), None, 0)
+        if n == C.c_size_t(-1).value:
+            return None
+        out = np.zeros(n, np.float32)
+        lib().needle_safetensors_get_f32(self._h, name.encode(), _p(out), n)
+        return out
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().needle_safetensors_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def ffn_forward_noalloc(x_ptr, T, d, ff, g, u, dn, act, out_ptr, stream=None):

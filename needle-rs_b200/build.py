@@ -35,17 +35,24 @@ def up_to_date():
 def build(force=False, debug=False):
     if not force and up_to_date():
         return OUT
+    from concurrent.futures import ThreadPoolExecutor
+
     os.makedirs(BUILD, exist_ok=True)
     opt = ["-O0", "-g", "-G"] if debug else ["-O3"]
     common = ["-std=c++17", "-Xcompiler", "-fPIC", "-lineinfo", "-I" + SRC] + opt
-    objs = []
+    cmds, objs = [], []
     for f in CU + CPP:
         o = os.path.join(BUILD, f + ".o")
         cmd = [NVCC] + ARCH + common + ["-c", os.path.join(SRC, f), "-o", o]
         if f.endswith(".cpp"):
             cmd[1:1] = ["-x", "cu"]
-        subprocess.run(cmd, check=True)
+        cmds.append(cmd)
         objs.append(o)
+    # one nvcc per translation unit, in parallel
+    with ThreadPoolExecutor(max_workers=max(1, min(len(cmds), os.cpu_count() or 1))) as ex:
+        for r in list(ex.map(lambda c: subprocess.run(c), cmds)):
+            if r.returncode != 0:
+                raise subprocess.CalledProcessError(r.returncode, r.args)
     subprocess.run([NVCC] + ARCH + ["-shared", "--cudart=static", "-o", OUT] + objs, check=True)
     return OUT
 

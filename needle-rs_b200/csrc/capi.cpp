@@ -991,6 +991,162 @@ void needle_int4_plan_free(NeedleInt4Plan *p) {
   delete p;
 }
 
+}  // extern "C"
+
+// A prepared MLP block (ffn_forward, crates/needle-core/src/ffn.rs:19-56):
+// gate and up interleaved into one weight, its bf16 hi/lo staging and the
+// down projection's, plus the per-call workspace (x planes, hidden planes,
+// f32 hidden for the CUDA-core path), all allocated at creation.
+struct NeedleFfnPlan {
+  int device = 0;
+  int d = 0, ff = 0, max_t = 0, Kd = 0, Kf = 0;
+  ndl::Int4Weight gu{}, dn{};
+  bool tc = false;
+  void *buf = nullptr;
+  float *hidden = nullptr;  // [max_t][ff] for the CUDA-core path
+  ndl::TcPlanes Wgu, Wdn, X, H;
+  int *flag = nullptr;
+};
+
+extern "C" {
+
+NeedleFfnPlan *needle_ffn_plan_create(size_t d, size_t ff, const uint8_t *gd, const float *gs, const uint8_t *ud,
+                                      const float *us, const uint8_t *dd, const float *ds, size_t max_t,
+                                      void *stream) {
+  clear_err();
+  if (!gd || !gs || !ud || !us || !dd || !ds || d == 0 || ff == 0 || max_t == 0 || d > (1u << 20) ||
+      ff > (1u << 20) || max_t > INT32_MAX || max_t * ff > ((size_t)1 << 34)) {
+    set_err("invalid ffn plan arguments");
+    return nullptr;
+  }
+  if (!ensure_kernels()) return nullptr;
+  auto *p = new NeedleFfnPlan();
+  cudaGetDevice(&p->device);
+  p->d = (int)d;
+  p->ff = (int)ff;
+  p->max_t = (int)max_t;
+  const int gs1 = (int)(d < 32 ? d : 32), gs2 = (int)(ff < 32 ? ff : 32);
+  p->gu = Int4Weight{gd, gs, (int)d, (int)(2 * ff), (int)((d + gs1 - 1) / gs1), gs1};
+  p->gu.w2 = ud;
+  p->gu.s2 = us;
+  p->dn = Int4Weight{dd, ds, (int)ff, (int)d, (int)((ff + gs2 - 1) / gs2), gs2};
+  p->tc = max_t >= (size_t)kTcMinRowsOp && d % 4 == 0;
+  cudaStream_t st = (cudaStream_t)stream;
+  const size_t hbytes = max_t * ff * sizeof(float);
+  size_t total = hbytes + 256;
+  size_t wgu = 0, wdn = 0, xb = 0, hb = 0;
+  if (p->tc) {
+    p->Kd = tc_padded_k((int)d);
+    p->Kf = tc_padded_k((int)ff);
+    const size_t rows = (size_t)tc_stage_rows((int)max_t);
+    wgu = 2 * ff * (size_t)p->Kd * 2;
+    wdn = d * (size_t)p->Kf * 2;
+    xb = rows * p->Kd * 2;
+    hb = rows * p->Kf * 2;
+    total += 2 * (wgu + wdn + xb + hb) + 8 * 256;
+    p->flag = device_err_flag();
+    if (!p->flag) {
+      set_err("device error flag allocation failed");
+      delete p;
+      return nullptr;
+    }
+  }
+  if (!dev_check(cudaMalloc(&p->buf, total))) {
+    delete p;
+    return nullptr;
+  }
+  char *b = (char *)(((uintptr_t)p->buf + 255) & ~(uintptr_t)255);
+  auto take = [&](size_t n) {
+    char *r = b;
+    b += (n + 255) & ~(size_t)255;
+    return (void *)r;
+  };
+  p->hidden = (float *)take(hbytes);
+  bool ok = true;
+  if (p->tc) {
+    void *guh = take(wgu), *gul = take(wgu), *dnh = take(wdn), *dnl = take(wdn);
+    void *xh = take(xb), *xl = take(xb), *hh = take(hb), *hl = take(hb);
+    const int rows = tc_stage_rows((int)max_t);
+    // the hidden planes' pad columns (ff .. Kf) are never written: zero them once
+    ok = dev_check(cudaMemsetAsync(hh, 0, hb, st)) && dev_check(cudaMemsetAsync(hl, 0, hb, st)) &&
+         dev_check(tc_make_planes(guh, gul, (int)(2 * ff), p->Kd, 128, p->Wgu)) &&
+         dev_check(tc_make_planes(dnh, dnl, (int)d, p->Kf, 128, p->Wdn)) &&
+         dev_check(tc_make_planes(xh, xl, rows, p->Kd, 128, p->X)) &&
+         dev_check(tc_make_planes(hh, hl, rows, p->Kf, 128, p->H)) &&
+         dev_check(tc_prep_weight(p->gu, p->Kd, guh, gul, st)) && dev_check(tc_prep_weight(p->dn, p->Kf, dnh, dnl, st));
+  }
+  if (!ok || !dev_check(cudaStreamSynchronize(st))) {
+    cudaFree(p->buf);
+    delete p;
+    return nullptr;
+  }
+  return p;
+}
+
+int needle_ffn_plan_forward(NeedleFfnPlan *p, const float *x, size_t T, int act, float *out, void *stream) {
+  clear_err();
+  if (!p || !x || !out || T == 0 || T > (size_t)p->max_t || act < 0 || act > 2) {
+    set_err("invalid ffn plan arguments");
+    return -1;
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  MatmulOut o;
+  o.y = out;
+  o.ldy = p->d;
+  if (!p->tc || T < (size_t)kTcMinRowsOp || ((uintptr_t)out % 16) || (p->d % 4)) {
+    MatmulOut a;
+    a.y = p->hidden;
+    a.ldy = p->ff;
+    a.epi = EPI_ACT;
+    a.act = act;
+    return dev_check(int4_matmul(x, p->d, (int)T, p->gu, a, st)) &&
+                   dev_check(int4_matmul(p->hidden, p->ff, (int)T, p->dn, o, st))
+               ? 0
+               : -1;
+  }
+  // x -> bf16 planes; gate|up GEMM whose epilogue writes act(gate) * up as the
+  // down projection's operand planes; down GEMM into out
+  MatmulOut a;
+  a.epi = EPI_ACT;
+  a.act = act;
+  a.planes[0] = const_cast<void *>(p->H.hi_ptr);
+  a.planes[1] = const_cast<void *>(p->H.lo_ptr);
+  a.ldy = p->Kf;
+  return dev_check(tc_split_rows(x, p->d, (int)T, p->d, p->Kd, const_cast<void *>(p->X.hi_ptr),
+                                 const_cast<void *>(p->X.lo_ptr), st)) &&
+                 dev_check(tc_matmul(p->X, (int)T, p->Wgu, 2 * p->ff, a, p->flag, st)) &&
+                 dev_check(tc_matmul(p->H, (int)T, p->Wdn, p->d, o, p->flag, st))
+             ? 0
+             : -1;
+}
+
+int needle_ffn_plan_status(NeedleFfnPlan *p) {
+  clear_err();
+  if (!p) {
+    set_err("null plan");
+    return -1;
+  }
+  if (!dev_check(cudaDeviceSynchronize())) return -1;
+  if (!p->flag) return 0;
+  int kerr = 0;
+  if (!dev_check(cudaMemcpy(&kerr, p->flag, sizeof(int), cudaMemcpyDeviceToHost))) return -1;
+  if (kerr) {
+    cudaMemset(p->flag, 0, sizeof(int));
+    set_err("a tensor-core GEMM wait timed out");
+    return -1;
+  }
+  return 0;
+}
+
+void needle_ffn_plan_free(NeedleFfnPlan *p) {
+  if (!p) return;
+  if (p->buf) {
+    cudaDeviceSynchronize();
+    cudaFree(p->buf);
+  }
+  delete p;
+}
+
 int needle_int4_quantize(const float *w, size_t K, size_t N, uint8_t *data, float *scales, void *stream) {
   clear_err();
   if (!w || !data || !scales || K == 0 || N == 0 || K > INT32_MAX || N > INT32_MAX) {
@@ -1046,5 +1202,47 @@ int needle_ffn_forward(const float *x, size_t T, size_t d, size_t ff, const uint
   cudaFreeAsync(hid, st);
   return ok ? 0 : -1;
 }
+
+}  // extern "C"
+
+// ── SafeTensors reader (crates/needle-infer/src/safetensors.rs) ──
+
+struct NeedleSafeTensors {
+  ndl::SafeTensors st;
+};
+
+extern "C" {
+
+NeedleSafeTensors *needle_safetensors_parse(const uint8_t *data, size_t len) {
+  clear_err();
+  if (!data && len) {
+    set_err("null pointer passed to needle_safetensors_parse");
+    return nullptr;
+  }
+  auto *p = new NeedleSafeTensors();
+  std::string err;
+  if (!p->st.parse(std::vector<uint8_t>(data, data + len), err)) {
+    set_err("SafeTensors error: " + err);
+    delete p;
+    return nullptr;
+  }
+  return p;
+}
+
+const char *needle_safetensors_metadata(const NeedleSafeTensors *p, const char *key) {
+  if (!p || !key) return nullptr;
+  const std::string *v = p->st.metadata(key);
+  return v ? v->c_str() : nullptr;
+}
+
+size_t needle_safetensors_get_f32(const NeedleSafeTensors *p, const char *name, float *out, size_t cap) {
+  if (!p || !name) return (size_t)-1;
+  std::vector<float> v;
+  if (!p->st.get_f32(name, v)) return (size_t)-1;
+  if (out) std::memcpy(out, v.data(), std::min(cap, v.size()) * sizeof(float));
+  return v.size();
+}
+
+void needle_safetensors_free(NeedleSafeTensors *p) { delete p; }
 
 }  // extern "C"

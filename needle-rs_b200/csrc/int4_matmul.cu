@@ -580,7 +580,7 @@ cudaError_t int4_matmul(const float *x, int64_t ldx, int M, const Int4Weight &W,
   if (o.epi == EPI_KNORM &&
       (!o.col_block || (o.col_block % 64) || !o.vec || (o.kv_block && (o.kv_block % o.col_block))))
     return cudaErrorInvalidValue;
-  if (o.epi == EPI_ACT && (W.N & 1)) return cudaErrorInvalidValue;
+  if (o.epi == EPI_ACT && ((W.N & 1) || o.planes[0])) return cudaErrorInvalidValue;  // planes: tensor-core only
   EpiCtx e{o, W.N};
   const int Kp = W.G * W.gs;
   if (M <= 8 && !W.w2 && o.epi != EPI_KNORM && (W.N % 16) == 0 && ((uintptr_t)W.w % 16) == 0 &&

@@ -36,7 +36,9 @@ struct Int4Weight {
 enum Epilogue : int {
   EPI_STORE = 0,  // y = acc
   EPI_RESID = 1,  // y += gate * acc           (layers.rs:70-74 gated residual)
-  EPI_ACT = 2,    // columns interleaved (gate_i, up_i) -> y[i] = act(gate_i, up_i)
+  EPI_ACT = 2,    // columns interleaved (gate_i, up_i) -> y[i] = act(gate_i, up_i); on the
+                  // tensor-core path with planes[0] set, written instead as the
+                  // bf16 hi/lo planes planes[0] / planes[1] (row stride ldy)
   EPI_KNORM = 3,  // y = acc, then per-64-column ZCRMSNorm with `vec` on blocks
                   // whose column-block index is even (the K half of K|V pairs)
   EPI_ARGMAX = 4, // output head: acc = logit of (row m, vocab n); add the mask,

@@ -85,6 +85,32 @@ template <int cnt>
 __device__ __forceinline__ void epi_row(const TcEpi &e, int m, int n0, float *v) {
   const MatmulOut &o = e.o;
   if (o.epi == EPI_ACT) {
+    if (o.planes[0]) {  // bf16 hi/lo operand planes of the next matmul (row stride ldy elements)
+      static_assert(cnt % 16 == 0, "whole 8-output groups");
+      const int64_t off = (int64_t)m * o.ldy + (n0 >> 1);
+      uint4 *dh = reinterpret_cast<uint4 *>((__nv_bfloat16 *)o.planes[0] + off);
+      uint4 *dl = reinterpret_cast<uint4 *>((__nv_bfloat16 *)o.planes[1] + off);
+#pragma unroll
+      for (int q = 0; q < cnt / 16; ++q) {
+        uint32_t hw[4], lw[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int j = 16 * q + 4 * i;
+          const float a0 = (n0 + j + 1 < e.N) ? act_apply_tc(o.act, v[j], v[j + 1]) : 0.0f;
+          const float a1 = (n0 + j + 3 < e.N) ? act_apply_tc(o.act, v[j + 2], v[j + 3]) : 0.0f;
+          __nv_bfloat162 h = __floats2bfloat162_rn(a0, a1);
+          float2 hf = __bfloat1622float2(h);
+          __nv_bfloat162 lo = __floats2bfloat162_rn(a0 - hf.x, a1 - hf.y);
+          hw[i] = *reinterpret_cast<uint32_t *>(&h);
+          lw[i] = *reinterpret_cast<uint32_t *>(&lo);
+        }
+        if (n0 + 16 * q < e.N) {
+          dh[q] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+          dl[q] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        }
+      }
+      return;
+    }
     float *p = o.y + (int64_t)m * o.ldy + (n0 >> 1);
 #pragma unroll
     for (int j = 0; j + 1 < cnt; j += 2)
@@ -730,6 +756,10 @@ cudaError_t tc_matmul(const TcPlanes &A, int M, const TcPlanes &B, int N, const 
     if (N != (o.heads_q + 2 * o.heads_kv) * 64 || !o.pos || !o.q_norm || !o.k_norm || !o.rope_cos || !o.rope_sin ||
         !o.kcache || !o.vcache || o.cache_cap <= 0 || (o.ldy % 4) || ((uintptr_t)o.y % 16) ||
         ((uintptr_t)o.kcache % 16) || ((uintptr_t)o.vcache % 16))
+      return cudaErrorInvalidValue;
+  } else if (o.epi == EPI_ACT && o.planes[0]) {
+    if (!o.planes[1] || ((uintptr_t)o.planes[0] % 16) || ((uintptr_t)o.planes[1] % 16) || (o.ldy % 8) ||
+        o.col_block)
       return cudaErrorInvalidValue;
   } else if ((o.ldy % 4) || ((uintptr_t)o.y % 16) || (o.col_block && (o.block_stride % 4))) {
     return cudaErrorInvalidValue;

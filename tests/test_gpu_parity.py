@@ -438,3 +438,31 @@ def test_argument_errors(full):
         eng.run_batch_ids([list(range(1025))], 2)
     ids, lens = eng.run_batch_ids([[3, 4]], 0)
     assert lens[0] == 0
+
+
+@pytest.mark.parametrize("act,T", [(0, 256), (1, 64), (2, 200), (0, 5), (1, 1)])
+def test_ffn_plan_vs_oracle(act, T):
+    # The prepared MLP block: the gate|up GEMM's epilogue writes the hidden
+    # activation as the down GEMM's operand planes (tensor cores from 9
+    # tokens), the CUDA-core kernels below; two calls in a row reuse the
+    # plan's workspace.
+    d, ff = 512, 2048
+    rng = np.random.default_rng(40 + act + T)
+    x = rng.standard_normal((T, d)).astype(np.float32)
+    g, u, dn = wl.random_int4(rng, d, ff), wl.random_int4(rng, d, ff), wl.random_int4(rng, ff, d)
+    ref = np.stack([orc.ffn_forward(g, u, dn, d, ff, x[t], act) for t in range(T)])
+    gd, ud, dd = [dev(a) for a in g], [dev(a) for a in u], [dev(a) for a in dn]
+    plan = nb.FfnPlan(d, ff, [t.data_ptr() for t in gd], [t.data_ptr() for t in ud], [t.data_ptr() for t in dd],
+                      max_t=256)
+    try:
+        xd = dev(x)
+        for _ in range(2):
+            out = torch.full((T, d), float("nan"), device="cuda")
+            plan.forward(xd.data_ptr(), T, act, out.data_ptr())
+            plan.status()
+            got = out.cpu().numpy()
+            assert close_act(got, ref), max_excess(got, ref, True)
+        with pytest.raises(nb.NeedleError):
+            plan.forward(xd.data_ptr(), 257, act, out.data_ptr())
+    finally:
+        plan.close()

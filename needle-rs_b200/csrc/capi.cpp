@@ -836,14 +836,18 @@ static bool matmul_any(const float *x, int64_t ldx, int M, const Int4Weight &W, 
   const int Kp = tc_padded_k(W.K);
   void *buf = nullptr;
   size_t wbytes = (size_t)W.N * Kp * 2, xbytes = (size_t)tc_stage_rows(M) * Kp * 2;
-  if (!dev_check(cudaMallocAsync(&buf, 2 * wbytes + 2 * xbytes + 1024, st))) return false;
+  wbytes = (wbytes + 255) & ~(size_t)255;
+  xbytes = (xbytes + 255) & ~(size_t)255;
+  if (!dev_check(cudaMallocAsync(&buf, 2 * wbytes + 2 * xbytes + tc_splitk_ws_bytes() + 1024, st))) return false;
   char *b = (char *)(((uintptr_t)buf + 255) & ~(uintptr_t)255);
   void *wh = b, *wl = b + wbytes, *xh = b + 2 * wbytes, *xl = b + 2 * wbytes + xbytes;
+  MatmulOut os = o;
+  os.splitk_ws = (float *)(b + 2 * wbytes + 2 * xbytes);
   TcPlanes A, B;
   bool ok = dev_check(tc_make_planes(wh, wl, W.N, Kp, 128, B)) &&
             dev_check(tc_make_planes(xh, xl, tc_stage_rows(M), Kp, 128, A)) &&
             dev_check(tc_prep_weight(W, Kp, wh, wl, st)) && dev_check(tc_split_rows(x, ldx, M, W.K, Kp, xh, xl, st)) &&
-            dev_check(tc_matmul(A, M, B, W.N, o, flag, st));
+            dev_check(tc_matmul(A, M, B, W.N, os, flag, st));
   cudaFreeAsync(buf, st);
   if (!ok) return false;
   int kerr = 0;
@@ -900,8 +904,9 @@ struct NeedleInt4Plan {
   int device = 0;
   ndl::Int4Weight W{};
   int Kp = 0, max_m = 0;
-  void *buf = nullptr;  // weight hi/lo planes, then x hi/lo planes
+  void *buf = nullptr;  // weight hi/lo planes, x hi/lo planes, split-K workspace
   ndl::TcPlanes A, B;
+  float *ws = nullptr;
   bool tc = false;
   int *flag = nullptr;
 };
@@ -925,15 +930,18 @@ NeedleInt4Plan *needle_int4_plan_create(const uint8_t *w, const float *s, size_t
   if (p->tc) {
     cudaStream_t st = (cudaStream_t)stream;
     p->Kp = tc_padded_k((int)K);
-    const size_t wbytes = N * (size_t)p->Kp * 2, xbytes = (size_t)tc_stage_rows((int)max_m) * p->Kp * 2;
+    size_t wbytes = N * (size_t)p->Kp * 2, xbytes = (size_t)tc_stage_rows((int)max_m) * p->Kp * 2;
+    wbytes = (wbytes + 255) & ~(size_t)255;
+    xbytes = (xbytes + 255) & ~(size_t)255;
     p->flag = device_err_flag();
-    if (!p->flag || !dev_check(cudaMalloc(&p->buf, 2 * wbytes + 2 * xbytes + 1024))) {
+    if (!p->flag || !dev_check(cudaMalloc(&p->buf, 2 * wbytes + 2 * xbytes + tc_splitk_ws_bytes() + 1024))) {
       if (!p->flag) set_err("device error flag allocation failed");
       delete p;
       return nullptr;
     }
     char *b = (char *)(((uintptr_t)p->buf + 255) & ~(uintptr_t)255);
     void *wh = b, *wl = b + wbytes, *xh = b + 2 * wbytes, *xl = b + 2 * wbytes + xbytes;
+    p->ws = (float *)(b + 2 * wbytes + 2 * xbytes);
     if (!dev_check(tc_make_planes(wh, wl, (int)N, p->Kp, 128, p->B)) ||
         !dev_check(tc_make_planes(xh, xl, tc_stage_rows((int)max_m), p->Kp, 128, p->A)) ||
         !dev_check(tc_prep_weight(p->W, p->Kp, wh, wl, st)) || !dev_check(cudaStreamSynchronize(st))) {
@@ -955,6 +963,7 @@ int needle_int4_plan_matmul(NeedleInt4Plan *p, const float *x, size_t M, float *
   MatmulOut o;
   o.y = y;
   o.ldy = (int64_t)p->W.N;
+  o.splitk_ws = p->ws;
   if (!p->tc || M < (size_t)kTcMinRowsOp || ((uintptr_t)y % 16) != 0 || (p->W.N % 4) != 0)
     return dev_check(int4_matmul(x, (int64_t)p->W.K, (int)M, p->W, o, st, (flags & NEEDLE_INT4_OVERLAP) != 0)) ? 0
                                                                                                               : -1;
@@ -1005,6 +1014,7 @@ struct NeedleFfnPlan {
   void *buf = nullptr;
   float *hidden = nullptr;  // [max_t][ff] for the CUDA-core path
   ndl::TcPlanes Wgu, Wdn, X, H;
+  float *ws = nullptr;  // split-K workspace
   int *flag = nullptr;
 };
 
@@ -1043,7 +1053,7 @@ NeedleFfnPlan *needle_ffn_plan_create(size_t d, size_t ff, const uint8_t *gd, co
     wdn = d * (size_t)p->Kf * 2;
     xb = rows * p->Kd * 2;
     hb = rows * p->Kf * 2;
-    total += 2 * (wgu + wdn + xb + hb) + 8 * 256;
+    total += 2 * (wgu + wdn + xb + hb) + tc_splitk_ws_bytes() + 9 * 256;
     p->flag = device_err_flag();
     if (!p->flag) {
       set_err("device error flag allocation failed");
@@ -1066,6 +1076,7 @@ NeedleFfnPlan *needle_ffn_plan_create(size_t d, size_t ff, const uint8_t *gd, co
   if (p->tc) {
     void *guh = take(wgu), *gul = take(wgu), *dnh = take(wdn), *dnl = take(wdn);
     void *xh = take(xb), *xl = take(xb), *hh = take(hb), *hl = take(hb);
+    p->ws = (float *)take(tc_splitk_ws_bytes());
     const int rows = tc_stage_rows((int)max_t);
     // the hidden planes' pad columns (ff .. Kf) are never written: zero them once
     ok = dev_check(cudaMemsetAsync(hh, 0, hb, st)) && dev_check(cudaMemsetAsync(hl, 0, hb, st)) &&
@@ -1093,6 +1104,7 @@ int needle_ffn_plan_forward(NeedleFfnPlan *p, const float *x, size_t T, int act,
   MatmulOut o;
   o.y = out;
   o.ldy = p->d;
+  o.splitk_ws = p->ws;
   if (!p->tc || T < (size_t)kTcMinRowsOp || ((uintptr_t)out % 16) || (p->d % 4)) {
     MatmulOut a;
     a.y = p->hidden;
@@ -1112,6 +1124,7 @@ int needle_ffn_plan_forward(NeedleFfnPlan *p, const float *x, size_t T, int act,
   a.planes[0] = const_cast<void *>(p->H.hi_ptr);
   a.planes[1] = const_cast<void *>(p->H.lo_ptr);
   a.ldy = p->Kf;
+  a.splitk_ws = p->ws;
   return dev_check(tc_split_rows(x, p->d, (int)T, p->d, p->Kd, const_cast<void *>(p->X.hi_ptr),
                                  const_cast<void *>(p->X.lo_ptr), st)) &&
                  dev_check(tc_matmul(p->X, (int)T, p->Wgu, 2 * p->ff, a, p->flag, st)) &&

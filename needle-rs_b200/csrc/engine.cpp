@@ -707,7 +707,8 @@ bool Batch::prepare(const BatchSpec &spec, std::string &err) {
     int kmax = *std::max_element(kps.begin(), kps.end());
     if (rows >= kTcMinRows) {
       if (!(tc_hi_ = alloc<__nv_bfloat16>((size_t)rows * kmax, err)) ||
-          !(tc_lo_ = alloc<__nv_bfloat16>((size_t)rows * kmax, err)))
+          !(tc_lo_ = alloc<__nv_bfloat16>((size_t)rows * kmax, err)) ||
+          !(splitk_ws_ = alloc<float>(tc_splitk_ws_bytes() / sizeof(float), err)))
         return false;
       tc_maps_.clear();
       for (int kp : kps) {
@@ -809,8 +810,10 @@ bool Batch::mm(int cls, bool capture, const float *x, int64_t ldx, int M, const 
     for (auto &t : tc_maps_)
       if (t.Kp == w.tc.Kp && M <= t.rows) ap = &t;
   if (ap) {
+    MatmulOut os = o;
+    os.splitk_ws = splitk_ws_;
     NDL_LK(tc_split_rows(x, ldx, M, w.K, ap->Kp, tc_hi_, tc_lo_, st_));
-    NDL_LK(tc_matmul(*ap, M, w.tc, w.N, o, m_->kerr, st_));
+    NDL_LK(tc_matmul(*ap, M, w.tc, w.N, os, m_->kerr, st_));
   } else {
     NDL_LK(int4_matmul(x, ldx, M, w.view(), o, st_));
   }
@@ -834,7 +837,9 @@ bool Batch::mm_in(int cls, bool capture, const TcPlanes *planes, const float *x,
   }
   cudaEvent_t a;
   if (!tbegin(cls, capture, a, err)) return false;
-  NDL_LK(tc_matmul(*planes, M, w.tc, w.N, o, m_->kerr, st_));
+  MatmulOut os = o;
+  os.splitk_ws = splitk_ws_;
+  NDL_LK(tc_matmul(*planes, M, w.tc, w.N, os, m_->kerr, st_));
   return tend(a, mm_flops(M, w), mm_bytes(M, w), err);
 }
 
@@ -1066,6 +1071,7 @@ bool Batch::decode_step(std::string &err, bool capture, int att_rows) {
     o.pos = pos_;
     o.keys = keys_;
     o.logits = logits_;
+    o.splitk_ws = splitk_ws_;
     NDL_LK(tc_matmul(*hp, B, m.emb_tc, c.vocab_size, o, m.kerr, st, m.emb_bf16_exact));
   } else {
     NDL_LK(head_argmax(h_, B, m.emb, c.vocab_size, d, mask_, W_, logits_, spec_.max_new, pos_, keys_, st));

@@ -236,6 +236,7 @@ class Batch {
   AttnPlanes attn_planes_;
   // tensor-core activation staging (bf16 hi/lo planes) and its TMA maps
   void *tc_hi_ = nullptr, *tc_lo_ = nullptr;
+  float *splitk_ws_ = nullptr;  // partial tiles of the split-K GEMMs (ordered on st_)
   std::vector<TcPlanes> tc_maps_;  // one per distinct padded K
   unsigned long long *keys_ = nullptr;
   int32_t *pos_ = nullptr;

@@ -85,6 +85,10 @@ struct MatmulOut {
   // EPI_QKV_DEC: caches [M][cache_cap][heads_kv*64] f32
   float *kcache = nullptr, *vcache = nullptr;
   int cache_cap = 0;
+  // Tensor-core path: workspace of tc_splitk_ws_bytes() for the split-K
+  // kernel's partial tiles, or NULL (no split).  Launches that share one
+  // workspace must be ordered (one stream).
+  float *splitk_ws = nullptr;
 };
 
 // Y[M, N] (epilogue) X[M, K] @ W.  x row stride ldx (floats).
@@ -120,6 +124,9 @@ cudaError_t tc_split_rows(const float *x, int64_t ldx, int M, int K, int Kp, voi
 cudaError_t tc_matmul(const TcPlanes &A, int M, const TcPlanes &B, int N, const MatmulOut &o, int *err,
                       cudaStream_t st, bool b_lo_zero = false);
 cudaError_t init_tc_kernels();
+// Bytes of the split-K workspace for the current device (one 128 x 128 f32
+// partial tile per SM).
+size_t tc_splitk_ws_bytes();
 
 // ContrastiveHead::encode (engine.rs:37-69) after the mean pool of
 // encode_contrastive (engine.rs:163-179), one CTA per request: out[r][c] from

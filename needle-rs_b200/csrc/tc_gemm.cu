@@ -40,6 +40,8 @@
 #include <cuda_bf16.h>
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "tc_common.cuh"
@@ -50,6 +52,9 @@ namespace {
 using namespace tc;
 
 constexpr int TC_BM = 128, TC_BK = 64, TC_THREADS = 384;
+// The split-K kernel: warps 0-3 producer / MMA, warps 4-7 one epilogue
+// warpgroup; 256 threads leave every thread up to 255 registers.
+constexpr int TC_SPLITK_THREADS = 256;
 // Registers a thread: launched at 168 (65,536 / 384, rounded down to 8); the
 // producer warpgroup drops to 56 and the two epilogue warpgroups rise to 224:
 // 128 x 56 + 256 x 224 = 384 x 168.
@@ -607,6 +612,259 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   }
 }
 
+// Split-K: shared-memory staging of 128 x 128 f32 rows, float (r, c) at
+// r * kSkRs + c + 8 * (c / 32).  The stride (4 mod 32) and the pad after each
+// 32 columns keep every access pattern used here free of bank conflicts:
+// 8 lanes on 8 rows at one column (TMEM copy), a warp along one row
+// (workspace copies), 8 threads on 2 rows x 4 column blocks or 4 rows x 2
+// heads (epilogue units).
+constexpr int kSkRs = 164;
+__device__ __forceinline__ int sk_off(int r, int c) { return r * kSkRs + c + 8 * (c >> 5); }
+
+// Epilogue of one (row, CW-column) unit of the reduced rows staged in
+// shared memory: CW = 64 for the epilogues that need whole 64-column heads,
+// 32 otherwise.  Unit u covers staged row u / (128 / CW) = tile row
+// row0 + that, columns (u % (128 / CW)) * CW.
+template <int CW>
+__device__ __forceinline__ void splitk_finish(const TcEpi &e, int M, int N, const float *stg, int row0, int mt,
+                                              int nt, int u) {
+  constexpr int UPR = 128 / CW;
+  const int rl = u / UPR, c0 = (u % UPR) * CW;
+  const float4 *p4 = reinterpret_cast<const float4 *>(stg + sk_off(rl, c0));
+  float v[CW];
+#pragma unroll
+  for (int j = 0; j < CW / 4; ++j) {
+    const float4 x = p4[j + (j >= 8 ? 2 : 0)];  // the 8-float pad after 32 columns
+    v[4 * j] = x.x;
+    v[4 * j + 1] = x.y;
+    v[4 * j + 2] = x.z;
+    v[4 * j + 3] = x.w;
+  }
+  const int m = mt * TC_BM + row0 + rl, n0 = nt * 128 + c0;
+  if (m >= M || n0 >= N) return;
+  if constexpr (CW == 64) {
+    if (e.o.epi == EPI_KNORM)
+      epi_row<64>(e, m, n0, v);
+    else
+      epi_qkv64(e, m, n0, v);
+  } else {
+    if (e.o.epi == EPI_ARGMAX)
+      atomicMax(e.o.keys + m, epi_argmax32(e, m, n0, v));
+    else
+      epi_row<32>(e, m, n0, v);
+  }
+}
+
+// Split-K GEMM for grids with few output tiles (decode-sized M): a cluster
+// of S CTAs shares one 128 x 128 output tile, CTA r of the cluster taking
+// k-blocks [r * nkb / S, (r + 1) * nkb / S).  Every SM ingests at most ~64
+// bytes per clock from L2, so a lone CTA walking all of K spends most of its
+// time waiting for operands; S CTAs load and multiply S slices at once.
+// Reduction through L2: every CTA writes its partial tile from TMEM to its
+// own 64 KB block of the caller's workspace (o.splitk_ws), one cluster
+// barrier (release / acquire at cluster scope) orders those writes before
+// the reads, and CTA r sums the S partials of tile rows [r * 128 / S,
+// (r + 1) * 128 / S) in rank order and applies the epilogue.  Partial rows
+// move through shared memory so that every global access of a warp covers
+// one contiguous 512-byte row: a thread storing its own accumulator row
+// scatters each warp instruction over 32 rows and reaches a fraction of the
+// SM's bandwidth (distributed shared memory behaves the same way).
+// Under programmatic dependent launch the first weight tiles are requested
+// before the wait for the previous kernel; only the activation tiles wait.
+// Every mbarrier wait is bounded; a wait that gives up still reaches the
+// cluster barrier.
+template <int S>
+__global__ void __launch_bounds__(TC_SPLITK_THREADS, 1)
+    tc_gemm_splitk_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
+                          const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl, int M,
+                          int N, int Kp, TcEpi e, int *err, int b_lo_zero) {
+  constexpr int BN = 128, STAGES = 3;
+  constexpr int A_BYTES = TC_BM * TC_BK * 2, B_BYTES = BN * TC_BK * 2;
+  constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
+  constexpr uint32_t IDESC = umma_idesc(TC_BM, BN);
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t *full = (uint64_t *)(smem + STAGES * STAGE_BYTES);
+  uint64_t *empty = full + STAGES;
+  uint64_t *tfull = empty + STAGES;
+  uint32_t *tmem_slot = (uint32_t *)(tfull + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int tile = blockIdx.x / S, num_n = (N + BN - 1) / BN;
+  const int mt = tile / num_n, nt = tile - mt * num_n;
+  const int kper = Kp / TC_BK / S, kb0 = (int)rank * kper;
+  float *tile_ws = e.o.splitk_ws + (size_t)tile * S * (128 * 128);
+  pdl_trigger();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(tfull, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {  // one 128-column f32 accumulator
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(BN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *(volatile uint32_t *)tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ── TMA producer: this CTA's K slice.  The weight (B) tiles of the first
+    // stages are requested before the previous kernel has finished: no
+    // kernel of the stream writes weights. ──
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmBh) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmBl) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmAh) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmAl) : "memory");
+    const int pre = kper < STAGES ? kper : STAGES;
+    for (int kk = 0; kk < pre; ++kk) {  // fresh barriers: every stage is free
+      const int kx = (kb0 + kk) * TC_BK;
+      uint8_t *st = smem + kk * STAGE_BYTES;
+      mbar_expect_tx(&full[kk], STAGE_BYTES);
+      tma_load_2d(st + 2 * A_BYTES, &tmBh, &full[kk], kx, nt * BN);
+      tma_load_2d(st + 2 * A_BYTES + B_BYTES, &tmBl, &full[kk], kx, nt * BN);
+    }
+    pdl_wait();
+    for (int kk = 0; kk < pre; ++kk) {
+      const int kx = (kb0 + kk) * TC_BK;
+      uint8_t *st = smem + kk * STAGE_BYTES;
+      tma_load_2d(st, &tmAh, &full[kk], kx, mt * TC_BM);
+      tma_load_2d(st + A_BYTES, &tmAl, &full[kk], kx, mt * TC_BM);
+    }
+    int stage = pre % STAGES;
+    uint32_t phase = pre == STAGES ? 1u : 0u;
+    bool ok = true;
+    for (int kk = pre; kk < kper; ++kk) {
+      if (!(ok = mbar_wait(&empty[stage], phase ^ 1, err))) break;
+      const int kx = (kb0 + kk) * TC_BK;
+      uint8_t *st = smem + stage * STAGE_BYTES;
+      mbar_expect_tx(&full[stage], STAGE_BYTES);
+      tma_load_2d(st, &tmAh, &full[stage], kx, mt * TC_BM);
+      tma_load_2d(st + A_BYTES, &tmAl, &full[stage], kx, mt * TC_BM);
+      tma_load_2d(st + 2 * A_BYTES, &tmBh, &full[stage], kx, nt * BN);
+      tma_load_2d(st + 2 * A_BYTES + B_BYTES, &tmBl, &full[stage], kx, nt * BN);
+      if (++stage == STAGES) {
+        stage = 0;
+        phase ^= 1;
+      }
+    }
+    // Drain: every issued stage consumed before the CTA moves on
+    for (int s = 0; s < STAGES && ok; ++s) {
+      ok = mbar_wait(&empty[stage], phase ^ 1, err);
+      if (++stage == STAGES) {
+        stage = 0;
+        phase ^= 1;
+      }
+    }
+  } else {
+    pdl_wait();  // global memory (the workspace, the epilogue's output) after the previous kernel
+    if (warp == 1 && lane == 0) {
+      // ── MMA issuer ──
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int kk = 0; kk < kper; ++kk) {
+        if (!(ok = mbar_wait(&full[stage], phase, err))) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        uint8_t *st = smem + stage * STAGE_BYTES;
+        const uint64_t ah = umma_desc(st), al = umma_desc(st + A_BYTES);
+        const uint64_t bh = umma_desc(st + 2 * A_BYTES), bl = umma_desc(st + 2 * A_BYTES + B_BYTES);
+#pragma unroll
+        for (int k = 0; k < TC_BK / 16; ++k) {
+          const uint64_t adv = (uint64_t)((k * 32) >> 4);  // 16 bf16 = 32 bytes along K
+          umma_bf16(tmem, ah + adv, bh + adv, IDESC, (kk | k) ? 1u : 0u);
+          if (!b_lo_zero) umma_bf16(tmem, ah + adv, bl + adv, IDESC, 1u);
+          umma_bf16(tmem, al + adv, bh + adv, IDESC, 1u);
+        }
+        umma_commit(&empty[stage]);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (ok) umma_commit(tfull);
+    } else if (warp >= 4) {
+      // ── partial tile -> this CTA's workspace block: warp q copies TMEM lanes
+      // (rows) 32q.. into shared memory over the drained operand ring, then
+      // writes them out one 512-byte row per instruction ──
+      const int q = warp & 3;
+      float *stg = reinterpret_cast<float *>(smem);
+      if (warp_wait(tfull, 0, err)) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const int row = q * 32 + lane;
+        const uint32_t base = tmem + ((uint32_t)(q * 32) << 16);
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          float v[32];
+          tmem_ld32(base + c, v);
+          float4 *d4 = reinterpret_cast<float4 *>(stg + sk_off(row, c));
+#pragma unroll
+          for (int j = 0; j < 8; ++j) d4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        }
+        __syncwarp();
+        float4 *dst = reinterpret_cast<float4 *>(tile_ws + (size_t)rank * (128 * 128));
+#pragma unroll 4
+        for (int r = q * 32; r < q * 32 + 32; ++r)
+          __stcg(dst + r * 32 + lane, *reinterpret_cast<const float4 *>(stg + sk_off(r, 4 * lane)));
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  cluster_sync();  // every CTA's partial tile is in the workspace
+
+  if (warp >= 4) {
+    // ── reduction of tile rows [rank * ROWS, (rank + 1) * ROWS): warp q sums
+    // rows q, q + 4, ... over the S partials in rank order (lane = 4 columns,
+    // all 32 loads of a lane in flight at once), stages them, then every
+    // epilogue thread takes (row, column-block) units ──
+    constexpr int ROWS = TC_BM / S, RPW = ROWS / 4;  // RPW * S = 32 loads per lane
+    const int q = warp & 3, row0 = (int)rank * ROWS;
+    float *stg = reinterpret_cast<float *>(smem);
+    const float4 *src = reinterpret_cast<const float4 *>(tile_ws);
+    float4 x[RPW][S];
+#pragma unroll
+    for (int i = 0; i < RPW; ++i)
+#pragma unroll
+      for (int r = 0; r < S; ++r) x[i][r] = __ldcg(src + (size_t)r * (128 * 32) + (row0 + q + 4 * i) * 32 + lane);
+#pragma unroll
+    for (int i = 0; i < RPW; ++i) {
+      float4 a = x[i][0];
+#pragma unroll
+      for (int r = 1; r < S; ++r) {
+        a.x += x[i][r].x;
+        a.y += x[i][r].y;
+        a.z += x[i][r].z;
+        a.w += x[i][r].w;
+      }
+      *reinterpret_cast<float4 *>(stg + sk_off(q + 4 * i, 4 * lane)) = a;
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");  // the 4 epilogue warps
+    const int epi = e.o.epi;
+    const bool wide = epi == EPI_KNORM || epi == EPI_QKV || epi == EPI_QKV_DEC;
+    const int units = ROWS * (BN / (wide ? 64 : 32));
+#pragma unroll 1
+    for (int u = threadIdx.x - 128; u < units; u += 128) {
+      if (wide)
+        splitk_finish<64>(e, M, N, stg, row0, mt, nt, u);
+      else
+        splitk_finish<32>(e, M, N, stg, row0, mt, nt, u);
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN));
+  }
+}
+
 // W (reference INT4 layout) -> bf16 hi/lo planes [N][Kp], K contiguous.
 __global__ void prep_weight_kernel(Int4Weight W, int Kp, __nv_bfloat16 *hi, __nv_bfloat16 *lo) {
   int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -679,10 +937,62 @@ static_assert(tc_smem_bytes(128, 3) <= 232448 && tc_smem_bytes(256, 2) <= 232448
 constexpr int TC_PAIR_STAGES = 3;
 constexpr size_t tc_smem_pair_bytes() { return 1024 + (size_t)TC_PAIR_STAGES * (4 * 128 * TC_BK * 2) + 256; }
 static_assert(tc_smem_pair_bytes() <= 232448, "exceeds the 227 KB of dynamic shared memory per block");
+constexpr size_t tc_smem_splitk_bytes() { return tc_smem_bytes(128, 3); }
+static_assert(tc_smem_splitk_bytes() <= 232448, "exceeds the 227 KB of dynamic shared memory per block");
+
+// NEEDLE_NO_SPLITK=1 keeps every GEMM on the persistent kernels (for
+// comparisons; results differ only in the order of the K summation).
+bool splitk_disabled() {
+  static const bool off = [] {
+    const char *v = std::getenv("NEEDLE_NO_SPLITK");
+    return v && *v && *v != '0';
+  }();
+  return off;
+}
+
+// Cluster size of the split-K kernel for `tiles` 128 x 128 output tiles over
+// nkb k-blocks: the largest S in {8, 4, 2} that divides nkb and keeps all
+// tiles' clusters resident at once (fits[i]: clusters of size 2 << i the
+// device holds at a time); 1 (persistent kernel) when the tiles alone
+// fill half the SMs.
+int splitk_factor(int tiles, int nkb, int sms, const int fits[3]) {
+  if (2 * tiles > sms) return 1;
+  for (int i = 2; i >= 0; --i) {
+    const int S = 2 << i;
+    if (nkb % S == 0 && tiles <= fits[i]) return S;
+  }
+  return 1;
+}
+
+template <int S>
+cudaError_t launch_splitk(const CUtensorMap *ah, const CUtensorMap *al, const CUtensorMap *bh, const CUtensorMap *bl,
+                          int M, int N, int Kp, const TcEpi &e, int *err, int b_lo_zero, int tiles, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(tiles * S);
+  cfg.blockDim = dim3(TC_SPLITK_THREADS);
+  cfg.dynamicSmemBytes = tc_smem_splitk_bytes();
+  cfg.stream = st;
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = S;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  int na = 1;
+  if (pdl_on()) {
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
+    na = 2;
+  }
+  cfg.attrs = at;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, tc_gemm_splitk_kernel<S>, *ah, *al, *bh, *bl, M, N, Kp, e, err, b_lo_zero);
+}
 
 }  // namespace
 
 int tc_padded_k(int K) { return (K + TC_BK - 1) / TC_BK * TC_BK; }
+
+size_t tc_splitk_ws_bytes() { return (size_t)tc_sm_count() * 128 * 128 * sizeof(float); }
 
 cudaError_t tc_make_planes(const void *hi, const void *lo, int rows, int Kp, int box_rows, TcPlanes &out) {
   auto fn = encode_fn();
@@ -813,6 +1123,39 @@ cudaError_t tc_matmul(const TcPlanes &A, int M, const TcPlanes &B, int N, const 
     return launch(tc_gemm_kernel<256, 2>, dim3(sms), dim3(TC_THREADS), tc_smem_bytes(256, 2), st, *ah, *al, *bh, *bl, M,
                   N, A.Kp, e, err, b_lo_zero ? 1 : 0);
   const int tiles = num_m * ((N + 127) / 128);
+  // clusters of 2, 4 and 8 split-K CTAs this device holds at once (0: the
+  // split-K kernels are unavailable)
+  static int fits[64][3];
+  static bool probed[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !probed[dev]) {
+    const void *fs[3] = {(const void *)tc_gemm_splitk_kernel<2>, (const void *)tc_gemm_splitk_kernel<4>,
+                         (const void *)tc_gemm_splitk_kernel<8>};
+    for (int i = 0; i < 3; ++i) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2 << i);
+      cfg.blockDim = dim3(TC_SPLITK_THREADS);
+      cfg.dynamicSmemBytes = tc_smem_splitk_bytes();
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeClusterDimension;
+      at[0].val.clusterDim.x = 2 << i;
+      at[0].val.clusterDim.y = 1;
+      at[0].val.clusterDim.z = 1;
+      cfg.attrs = at;
+      cfg.numAttrs = 1;
+      int n = 0;
+      fits[dev][i] = cudaOccupancyMaxActiveClusters(&n, fs[i], &cfg) == cudaSuccess ? n : 0;
+    }
+    cudaGetLastError();  // a failed query leaves no sticky error
+    probed[dev] = true;
+  }
+  int S = (o.splitk_ws && dev >= 0 && dev < 64 && !splitk_disabled()) ? splitk_factor(tiles, A.Kp / TC_BK, sms, fits[dev])
+                                                                       : 1;
+  if (tiles * S > sms || ((uintptr_t)o.splitk_ws % 16)) S = 1;  // the workspace holds one tile per SM
+  if (S == 8) return launch_splitk<8>(ah, al, bh, bl, M, N, A.Kp, e, err, b_lo_zero ? 1 : 0, tiles, st);
+  if (S == 4) return launch_splitk<4>(ah, al, bh, bl, M, N, A.Kp, e, err, b_lo_zero ? 1 : 0, tiles, st);
+  if (S == 2) return launch_splitk<2>(ah, al, bh, bl, M, N, A.Kp, e, err, b_lo_zero ? 1 : 0, tiles, st);
   return launch(tc_gemm_kernel<128, 3>, dim3(tiles < sms ? tiles : sms), dim3(TC_THREADS), tc_smem_bytes(128, 3), st,
                 *ah, *al, *bh, *bl, M, N, A.Kp, e, err, b_lo_zero ? 1 : 0);
 }
@@ -826,6 +1169,10 @@ cudaError_t init_tc_kernels() {
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(tc_gemm_pair_kernel<TC_PAIR_STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)tc_smem_pair_bytes());
+  for (const void *f : {(const void *)tc_gemm_splitk_kernel<2>, (const void *)tc_gemm_splitk_kernel<4>,
+                        (const void *)tc_gemm_splitk_kernel<8>})
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc_smem_splitk_bytes());
   return e;
 }
 

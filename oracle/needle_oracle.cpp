@@ -671,7 +671,7 @@ inline uint32_t total_order_key(float f) {
 // engine.rs:286-322 on token IDs.
 size_t generate(const Model &m, const uint32_t *ids, size_t T, size_t max_new,
                 const uint64_t *mask_bits, int stop_on_eos, uint32_t *out_ids, float *margins,
-                float *logits_out) {
+                float *logits_out, float *tops = nullptr) {
   size_t V = m.cfg.vocab_size, words = (V + 63) / 64;
   auto enc_kv = make_enc_kv(m, T);
   auto dec_kv = make_dec_kv(m);
@@ -696,6 +696,7 @@ size_t generate(const Model &m, const uint32_t *ids, size_t T, size_t max_new,
         if (v != best) second = std::max(second, logits[v]);
       margins[step] = logits[best] - second;
     }
+    if (tops) tops[step] = logits[best];
     if (logits_out) std::memcpy(logits_out + step * V, logits.data(), V * sizeof(float));
     uint32_t next = (uint32_t)best;
     if (stop_on_eos && next == EOS_ID) break;
@@ -1327,7 +1328,7 @@ size_t orc_generate(const void *mp, const uint32_t *enc_ids, size_t n_enc, size_
 
 int orc_run_batch(const void *mp, const uint32_t *ids, const uint64_t *offsets, size_t n_req,
                   size_t max_new, const uint64_t *mask_bits, int stop_on_eos, uint32_t *out_ids,
-                  uint32_t *out_lens, float *margins, int n_threads) {
+                  uint32_t *out_lens, float *margins, int n_threads, float *tops) {
   const Model &m = *(const Model *)mp;
   size_t words = (m.cfg.vocab_size + 63) / 64;
   std::atomic<size_t> next{0};
@@ -1345,7 +1346,8 @@ int orc_run_batch(const void *mp, const uint32_t *ids, const uint64_t *offsets, 
       out_lens[r] = (uint32_t)generate(m, ids + a, b - a, max_new,
                                        mask_bits ? mask_bits + r * max_new * words : nullptr,
                                        stop_on_eos, out_ids + r * max_new,
-                                       margins ? margins + r * max_new : nullptr, nullptr);
+                                       margins ? margins + r * max_new : nullptr, nullptr,
+                                       tops ? tops + r * max_new : nullptr);
     }
   };
   int nt = std::max(1, n_threads);

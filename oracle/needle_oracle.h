@@ -99,7 +99,7 @@ size_t orc_generate(const void *model, const uint32_t *enc_ids, size_t n_enc,
 int orc_run_batch(const void *model, const uint32_t *ids,
                   const uint64_t *offsets, size_t n_req, size_t max_new,
                   const uint64_t *mask_bits, int stop_on_eos, uint32_t *out_ids,
-                  uint32_t *out_lens, float *margins, int n_threads);
+                  uint32_t *out_lens, float *margins, int n_threads, float *tops);
 
 /* KV-cache saturation semantics (attn.rs:53-67): pushes n_push rows into a
  * cache of max_len rows; returns the final len. */

@@ -47,7 +47,7 @@ def lib():
             "orc_model_config": (None, [P, P]),
             "orc_forward": (I, [P, P, S, P, S, P, P]),
             "orc_generate": (S, [P, P, S, S, P, I, P, P, P]),
-            "orc_run_batch": (I, [P, P, P, S, S, P, I, P, P, P, I]),
+            "orc_run_batch": (I, [P, P, P, S, S, P, I, P, P, P, I, P]),
             "orc_kv_cache_push_count": (S, [S, S]),
             "orc_encode_contrastive": (S, [P, P, S, P]),
             "orc_contrastive_dim": (S, [P]),
@@ -195,16 +195,19 @@ class Model:
         res = (out[:n], marg[:n])
         return res + (lg[:n],) if want_logits else res
 
-    def run_batch(self, ids, offsets, max_new, mask_bits=None, stop_on_eos=False, n_threads=1):
+    def run_batch(self, ids, offsets, max_new, mask_bits=None, stop_on_eos=False, n_threads=1, want_tops=False):
+        """-> (ids [n, max_new], lens [n], top-2 margins [n, max_new][, top
+        masked logit of each step [n, max_new] when want_tops])."""
         ids = np.ascontiguousarray(ids, np.uint32)
         offsets = np.ascontiguousarray(offsets, np.uint64)
         n_req = offsets.size - 1
         out = np.zeros((n_req, max_new), np.uint32)
         lens = np.zeros(n_req, np.uint32)
         marg = np.zeros((n_req, max_new), np.float32)
+        tops = np.zeros((n_req, max_new), np.float32) if want_tops else None
         mb = None if mask_bits is None else np.ascontiguousarray(mask_bits, np.uint64)
         rc = lib().orc_run_batch(self.h, _p(ids), _p(offsets), n_req, max_new, _p(mb), int(stop_on_eos),
-                                 _p(out), _p(lens), _p(marg), n_threads)
+                                 _p(out), _p(lens), _p(marg), n_threads, _p(tops))
         if rc != 0:
             raise ValueError("invalid request")
-        return out, lens, marg
+        return (out, lens, marg, tops) if want_tops else (out, lens, marg)

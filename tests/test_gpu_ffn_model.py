@@ -87,7 +87,7 @@ def test_ffn_batched_decode(ffn_model):
     for r in (0, 91, 191):
         rid, rmarg, rlg = ref.generate(prompts[r], steps, want_logits=True)
         assert close(lg[r, 0], rlg[0]), float(np.max(np.abs(lg[r, 0] - rlg[0])))
-        for s in range(steps):
-            if rmarg[s] <= tol:
+        for s in range(steps):  # the sequences may part only at a tie-level step
+            if out[r, s] != rid[s]:
+                assert rmarg[s] <= tol, (r, s)
                 break
-            assert out[r, s] == rid[s], (r, s)

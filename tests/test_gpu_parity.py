@@ -5,8 +5,8 @@ RTOL * |ref| with RTOL = 1e-3, ATOL = 1e-4; intermediate activations (encoder
 hidden, matmul and MLP outputs) the same with ATOL scaled by the tensor's RMS
 when that exceeds 1 (f32 rounding error grows with the magnitude of the sum,
 not of each element); greedy and constrained token ids identical wherever the
-oracle's top-2 margin exceeds the logit tolerance (after a tie-level
-divergence the sequences legitimately differ, so comparison stops there).
+oracle's top-2 margin exceeds the logit tolerance (the sequences may part
+only at a tie-level step, and legitimately differ after it).
 """
 import json
 import os
@@ -56,13 +56,12 @@ def close_act(got, ref):
 
 
 def tokens_match(gpu_ids, ref_ids, ref_margins, tol_margin):
-    """Exact match up to the first step whose oracle margin is within the
-    logit tolerance (a tie the tolerance cannot resolve)."""
+    """Exact match, except that the sequences may part at a step whose
+    oracle top-2 margin is within the logit tolerance (a tie the tolerance
+    cannot resolve); after that step they legitimately differ."""
     for s, (g, r) in enumerate(zip(gpu_ids, ref_ids)):
-        if ref_margins[s] <= tol_margin:
-            return True
         if g != r:
-            return False
+            return ref_margins[s] <= tol_margin
     return True
 
 
@@ -466,3 +465,22 @@ def test_ffn_plan_vs_oracle(act, T):
             plan.forward(xd.data_ptr(), 257, act, out.data_ptr())
     finally:
         plan.close()
+
+
+def test_one_row_tile_batch_vs_oracle(full):
+    # 128 requests: every decode GEMM has a single 128-row tile, so the
+    # projections and the head's mask + argmax epilogue run as split-K
+    # clusters reduced through distributed shared memory.
+    eng, ref = full
+    ids_in, off = wl.random_prompts(128, 8, 70, 8192, seed=19)
+    prompts = [ids_in[off[i]:off[i + 1]] for i in range(128)]
+    steps = 4
+    masks = wl.random_masks(128, steps, 8192, 0.05, seed=20)
+    ids, lens, lg = eng.run_batch_ids(prompts, steps, mask_bits=masks, want_logits=True)
+    again = eng.run_batch_ids(prompts, steps, mask_bits=masks, want_logits=True)
+    assert np.array_equal(again[2], lg)  # the split-K reduction order is fixed
+    tol = 2 * (ATOL + RTOL * 10.0)
+    for r in (0, 64, 127):
+        rid, rmarg, rlg = ref.generate(prompts[r], steps, mask_bits=masks[r], want_logits=True)
+        assert tokens_match(ids[r], rid, rmarg, tol), r
+        assert close(lg[r, 0], rlg[0]), max_excess(lg[r, 0], rlg[0])

@@ -41,6 +41,7 @@
 #include <cudaTypedefs.h>
 
 #include <cstdlib>
+#include <cstring>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -310,11 +311,100 @@ __device__ __forceinline__ void epi_tile(const TcEpi &e, int M, int N, int m, ui
   if (amax && m < M) atomicMax(e.o.keys + m, best);
 }
 
+// Whether the epilogue `epi` writes through the TMA output map when one is
+// given: the f32 outputs of the plain store, the gated residual (as a
+// reduce-add of gate * acc) and the k-norm.
+__device__ __forceinline__ bool epi_uses_tma(int epi) {
+  return epi == EPI_STORE || epi == EPI_RESID || epi == EPI_KNORM;
+}
+
+// TMA output path of the store / gated-residual / k-norm epilogues for one
+// warp's 32 rows (tile rows m0.., TMEM lane quarter at `base`), accumulator
+// columns [c0, c1), output column = n_base + accumulator column.  Every
+// 32 x 32 f32 box is staged in the warp's 4 KB buffer `stg` in the 128-byte
+// swizzled layout of the map (row r's 16-byte chunk j at r * 128 + ((j ^
+// (r & 7)) << 4): one row per lane touches every bank once) and written by
+// one TMA store issued by lane 0; the residual adds gate * acc to y with a
+// TMA reduce-add (each element once, so the result is deterministic).  A
+// thread storing its own row directly scatters each warp instruction over
+// 32 rows and reaches a fraction of the SM's store bandwidth.  Rows past M
+// and columns past the map's extent are not written.  The bulk group is
+// drained (read) before `stg` is reused, and completely before the CTA
+// exits (tma_epi_drain).
+__device__ __forceinline__ void epi_tile_tma(const TcEpi &e, const CUtensorMap *map, int N, int m0, int lane,
+                                             uint32_t base, int c0, int c1, int n_base, uint8_t *stg) {
+  const MatmulOut &o = e.o;
+  const bool knorm = o.epi == EPI_KNORM, resid = o.epi == EPI_RESID;
+  const int cnt = knorm ? 64 : 32;
+  for (int c = c0; c < c1; c += cnt) {
+    float v[64];
+    tmem_ld32(base + c, v);
+    if (knorm) tmem_ld32(base + c + 32, v + 32);
+    const int n0 = n_base + c;
+    if (n0 >= N) continue;  // warp-uniform
+    if (knorm) {
+      const int blk = n0 / (o.kv_block ? o.kv_block : o.col_block);
+      if ((blk & 1) == 0) {  // K block: ZCRMSNorm of the 64-column head (norm.rs:23-30)
+        const float4 *sc = reinterpret_cast<const float4 *>(o.vec + (int64_t)(blk >> 1) * 64);
+        float ss = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 64; ++j) ss += v[j] * v[j];
+        const float inv = 1.0f / sqrtf(ss / 64.0f + 1e-6f);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const float4 s4 = __ldg(sc + j);
+          v[4 * j + 0] = ((1.0f + s4.x) * v[4 * j + 0]) * inv;
+          v[4 * j + 1] = ((1.0f + s4.y) * v[4 * j + 1]) * inv;
+          v[4 * j + 2] = ((1.0f + s4.z) * v[4 * j + 2]) * inv;
+          v[4 * j + 3] = ((1.0f + s4.w) * v[4 * j + 3]) * inv;
+        }
+      }
+    } else if (resid) {  // layers.rs:70-74: x += gate * out
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = o.gate * v[j];
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      if (h * 32 >= cnt) break;
+      if (lane == 0) bulk_wait_read_all();  // the previous box has left `stg`
+      __syncwarp();
+      uint8_t *row = stg + lane * 128;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        *reinterpret_cast<float4 *>(row + ((j ^ (lane & 7)) << 4)) =
+            make_float4(v[32 * h + 4 * j], v[32 * h + 4 * j + 1], v[32 * h + 4 * j + 2], v[32 * h + 4 * j + 3]);
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        const int n = n0 + 32 * h;
+        if (o.col_block) {
+          if (resid)
+            tma_reduce_add_3d(map, stg, n % o.col_block, m0, n / o.col_block);
+          else
+            tma_store_3d(map, stg, n % o.col_block, m0, n / o.col_block);
+        } else if (resid) {
+          tma_reduce_add_2d(map, stg, n, m0);
+        } else {
+          tma_store_2d(map, stg, n, m0);
+        }
+        bulk_commit();
+      }
+    }
+  }
+}
+
+// Before the CTA leaves: every TMA output store of this warp has completed.
+__device__ __forceinline__ void tma_epi_drain(int lane) {
+  if (lane == 0) bulk_wait_all();
+  __syncwarp();
+}
+
 template <int BN, int TC_STAGES>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
-                   const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl, int M, int N,
-                   int Kp, TcEpi e, int *err, int b_lo_zero) {
+                   const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl,
+                   const __grid_constant__ CUtensorMap tmY, int M, int N, int Kp, TcEpi e, int *err, int b_lo_zero,
+                   int y_tma) {
   constexpr int A_BYTES = TC_BM * TC_BK * 2, B_BYTES = BN * TC_BK * 2;
   constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
   constexpr uint32_t IDESC = umma_idesc(TC_BM, BN);
@@ -438,6 +528,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     // ── epilogue: warpgroup `half` takes columns [half * BN/2, (half + 1) * BN/2) ──
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(TC_REG_EPILOGUE));
     const int q = warp & 3, half = (warp - 4) >> 2;
+    const bool tma_out = y_tma && epi_uses_tma(e.o.epi);
+    uint8_t *stg = smem + TC_STAGES * STAGE_BYTES + 1024 + (warp - 4) * 4096;  // 1024-byte aligned
     int i = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
       const int buf = i & 1;
@@ -446,10 +538,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const int mt = t / num_n, nt = t - mt * num_n;
       const int m = mt * TC_BM + q * 32 + lane;
       const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
-      epi_tile(e, M, N, m, base, half * (BN / 2), (half + 1) * (BN / 2), nt * BN);
+      if (tma_out)
+        epi_tile_tma(e, &tmY, N, m - lane, lane, base, half * (BN / 2), (half + 1) * (BN / 2), nt * BN, stg);
+      else
+        epi_tile(e, M, N, m, base, half * (BN / 2), (half + 1) * (BN / 2), nt * BN);
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       mbar_arrive(&tempty[buf]);
     }
+    if (tma_out) tma_epi_drain(lane);
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
@@ -473,8 +569,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 template <int STAGES>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
-                        const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl, int M,
-                        int N, int Kp, TcEpi e, int *err, int b_lo_zero) {
+                        const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl,
+                        const __grid_constant__ CUtensorMap tmY, int M, int N, int Kp, TcEpi e, int *err,
+                        int b_lo_zero, int y_tma) {
   constexpr int HALF = 128, BN = 256;
   constexpr int A_BYTES = HALF * TC_BK * 2, B_BYTES = HALF * TC_BK * 2;
   constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
@@ -589,6 +686,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     // ── epilogue (both CTAs): warpgroup `half` takes 128 of the 256 columns ──
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(TC_REG_EPILOGUE));
     const int q = warp & 3, half = (warp - 4) >> 2;
+    const bool tma_out = y_tma && epi_uses_tma(e.o.epi);
+    uint8_t *stg = smem + STAGES * STAGE_BYTES + 1024 + (warp - 4) * 4096;  // 1024-byte aligned
     int i = 0;
     for (int t = pair; t < tiles; t += npairs, ++i) {
       const int buf = i & 1;
@@ -597,11 +696,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const int mt = t / num_n, nt = t - mt * num_n;
       const int m = mt * 2 * HALF + (int)rank * HALF + q * 32 + lane;
       const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
-      epi_tile(e, M, N, m, base, half * (BN / 2), (half + 1) * (BN / 2), nt * BN);
+      if (tma_out)
+        epi_tile_tma(e, &tmY, N, m - lane, lane, base, half * (BN / 2), (half + 1) * (BN / 2), nt * BN, stg);
+      else
+        epi_tile(e, M, N, m, base, half * (BN / 2), (half + 1) * (BN / 2), nt * BN);
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(&tempty[buf], 0);  // the leader's barrier
     }
+    if (tma_out) tma_epi_drain(lane);
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
@@ -929,15 +1032,18 @@ int tc_sm_count() {
   return n[dev] > 0 ? n[dev] : 148;
 }
 
+// Operand ring, barriers (under 1 KB), then eight 4 KB TMA output staging
+// buffers (one per epilogue warp, 1024-byte aligned for the 128-byte swizzle).
+constexpr size_t kTmaStageBytes = 1024 + 8 * 4096;
 constexpr size_t tc_smem_bytes(int BN, int stages) {
-  return 1024 + (size_t)stages * (2 * TC_BM * TC_BK * 2 + 2 * BN * TC_BK * 2) + 256;
+  return 1024 + (size_t)stages * (2 * TC_BM * TC_BK * 2 + 2 * BN * TC_BK * 2) + kTmaStageBytes;
 }
 static_assert(tc_smem_bytes(128, 3) <= 232448 && tc_smem_bytes(256, 2) <= 232448,
               "exceeds the 227 KB of dynamic shared memory per block");
 constexpr int TC_PAIR_STAGES = 3;
-constexpr size_t tc_smem_pair_bytes() { return 1024 + (size_t)TC_PAIR_STAGES * (4 * 128 * TC_BK * 2) + 256; }
+constexpr size_t tc_smem_pair_bytes() { return 1024 + (size_t)TC_PAIR_STAGES * (4 * 128 * TC_BK * 2) + kTmaStageBytes; }
 static_assert(tc_smem_pair_bytes() <= 232448, "exceeds the 227 KB of dynamic shared memory per block");
-constexpr size_t tc_smem_splitk_bytes() { return tc_smem_bytes(128, 3); }
+constexpr size_t tc_smem_splitk_bytes() { return 1024 + (size_t)3 * (4 * 128 * TC_BK * 2) + 256; }
 static_assert(tc_smem_splitk_bytes() <= 232448, "exceeds the 227 KB of dynamic shared memory per block");
 
 // NEEDLE_NO_SPLITK=1 keeps every GEMM on the persistent kernels (for
@@ -1046,6 +1152,42 @@ cudaError_t tc_split_rows(const float *x, int64_t ldx, int M, int K, int Kp, voi
   return cudaGetLastError();
 }
 
+namespace {
+// TMA map of the f32 output of a store / residual / k-norm epilogue: 32 x 32
+// boxes, 128-byte swizzle; 3-D ({col_block, M, N / col_block}) when the
+// columns are split into blocks.  False when the layout does not allow one
+// (the epilogue then stores per thread).
+bool tma_map_out(const MatmulOut &o, int M, int N, CUtensorMap *map) {
+  auto fn = encode_fn();
+  if (!fn || !o.y || ((uintptr_t)o.y % 16) || (o.ldy % 4) || M <= 0) return false;
+  cuuint32_t box[3] = {32, 32, 1}, es[3] = {1, 1, 1};
+  CUresult r;
+  if (o.col_block) {
+    if ((o.col_block % 32) || (N % o.col_block) || (o.block_stride % 4)) return false;
+    cuuint64_t dims[3] = {(cuuint64_t)o.col_block, (cuuint64_t)M, (cuuint64_t)(N / o.col_block)};
+    cuuint64_t strides[2] = {(cuuint64_t)o.ldy * 4, (cuuint64_t)o.block_stride * 4};
+    r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, o.y, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else {
+    cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)M};
+    cuuint64_t strides[1] = {(cuuint64_t)o.ldy * 4};
+    r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, o.y, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
+  return r == CUDA_SUCCESS;
+}
+
+// NEEDLE_NO_TMA_STORE=1 keeps every epilogue on per-thread stores (for
+// comparisons; the residual then adds with one fused multiply-add).
+bool tma_store_disabled() {
+  static const bool off = [] {
+    const char *v = std::getenv("NEEDLE_NO_TMA_STORE");
+    return v && *v && *v != '0';
+  }();
+  return off;
+}
+}  // namespace
+
 cudaError_t tc_matmul(const TcPlanes &A, int M, const TcPlanes &B, int N, const MatmulOut &o, int *err,
                       cudaStream_t st, bool b_lo_zero) {
   if (M <= 0 || N <= 0) return cudaSuccess;
@@ -1076,6 +1218,12 @@ cudaError_t tc_matmul(const TcPlanes &A, int M, const TcPlanes &B, int N, const 
   }
   if (o.epi == EPI_ACT && (N & 1)) return cudaErrorInvalidValue;
   TcEpi e{o, N};
+  alignas(64) CUtensorMap ymap;
+  std::memset(&ymap, 0, sizeof(ymap));
+  const int y_tma = (o.epi == EPI_STORE || o.epi == EPI_RESID || o.epi == EPI_KNORM) && !tma_store_disabled() &&
+                            tma_map_out(o, M, N, &ymap)
+                        ? 1
+                        : 0;
   // setmaxnreg redistributes exactly the registers of a 168-register launch;
   // any other count would leave the increase waiting for registers that
   // never come, so such a build is refused here.
@@ -1116,12 +1264,12 @@ cudaError_t tc_matmul(const TcPlanes &A, int M, const TcPlanes &B, int N, const 
     at[0].val.clusterDim.z = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<TC_PAIR_STAGES>, *ah, *al, *bh, *bl, M, N, A.Kp, e, err,
-                              b_lo_zero ? 1 : 0);
+    return cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<TC_PAIR_STAGES>, *ah, *al, *bh, *bl, ymap, M, N, A.Kp, e,
+                              err, b_lo_zero ? 1 : 0, y_tma);
   }
   if (tiles256 >= 2 * sms)
-    return launch(tc_gemm_kernel<256, 2>, dim3(sms), dim3(TC_THREADS), tc_smem_bytes(256, 2), st, *ah, *al, *bh, *bl, M,
-                  N, A.Kp, e, err, b_lo_zero ? 1 : 0);
+    return launch(tc_gemm_kernel<256, 2>, dim3(sms), dim3(TC_THREADS), tc_smem_bytes(256, 2), st, *ah, *al, *bh, *bl,
+                  ymap, M, N, A.Kp, e, err, b_lo_zero ? 1 : 0, y_tma);
   const int tiles = num_m * ((N + 127) / 128);
   // clusters of 2, 4 and 8 split-K CTAs this device holds at once (0: the
   // split-K kernels are unavailable)
@@ -1157,7 +1305,7 @@ cudaError_t tc_matmul(const TcPlanes &A, int M, const TcPlanes &B, int N, const 
   if (S == 4) return launch_splitk<4>(ah, al, bh, bl, M, N, A.Kp, e, err, b_lo_zero ? 1 : 0, tiles, st);
   if (S == 2) return launch_splitk<2>(ah, al, bh, bl, M, N, A.Kp, e, err, b_lo_zero ? 1 : 0, tiles, st);
   return launch(tc_gemm_kernel<128, 3>, dim3(tiles < sms ? tiles : sms), dim3(TC_THREADS), tc_smem_bytes(128, 3), st,
-                *ah, *al, *bh, *bl, M, N, A.Kp, e, err, b_lo_zero ? 1 : 0);
+                *ah, *al, *bh, *bl, ymap, M, N, A.Kp, e, err, b_lo_zero ? 1 : 0, y_tma);
 }
 
 cudaError_t init_tc_kernels() {

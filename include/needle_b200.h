@@ -230,9 +230,15 @@ int needle_ffn_forward(const float *x, size_t T, size_t d_model, size_t d_ff, co
  *     loads the library until the process exits); T * d_ff above that is
  *     rejected with an error; nothing is allocated and the matmuls run on the
  *     CUDA cores;
- *   - the first call on each device looks up that array's device address
- *     (cudaGetSymbolAddress) and sets kernel attributes; make that first call
- *     before any stream capture;
+ *   - every call looks up that array's device address on the current
+ *     device (cudaGetSymbolAddress); the first call on each device also sets
+ *     kernel attributes, so make that first call before any stream capture,
+ *     and none after a cudaDeviceReset of that device;
+ *   - up to 8 tokens a block holds every token's input row in shared
+ *     memory (2 floats per input element of the down projection), which
+ *     must fit in 200 KB with the block's buffers, else the call fails and
+ *     says so: d_ff up to 2,560 at 5-8 tokens and 5,248 at 3-4, d_model up
+ *     to 5,376 at 8 tokens;
  *   - every call shares the one array, which keeps the last call's contents:
  *     calls whose work overlaps on the GPU (different streams, or threads
  *     without ordering) race on it and must be serialised by the caller. */

@@ -12,6 +12,7 @@
 // nothing.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <mutex>
 #include <string>
 
@@ -28,33 +29,31 @@ constexpr size_t kNoAllocHiddenFloats = size_t(1) << 20;
 
 static __device__ __align__(256) float g_ffn_hidden[kNoAllocHiddenFloats];
 
-// Device address of g_ffn_hidden for each device.  The host-side name of the
-// array is only a stand-in, not a device address, so each device's address
-// is obtained once with cudaGetSymbolAddress while that device is current.
+// The host-side name of g_ffn_hidden is only a stand-in, not a device
+// address: each call looks up the current device's address with
+// cudaGetSymbolAddress (cheap, allocates nothing), so an address never
+// outlives the context it came from.  Kernel attributes are set once per
+// device.
 std::mutex g_mu;
-float *g_hidden_dev[64] = {nullptr};
 bool g_kernels_ready[64] = {false};
 
 bool setup_device(int dev, float **hidden) {
-  std::lock_guard<std::mutex> lock(g_mu);
-  if (!g_hidden_dev[dev]) {
-    void *p = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&p, g_ffn_hidden);
-    if (e != cudaSuccess) {
-      ndl::capi_set_last_error(std::string("cudaGetSymbolAddress failed: ") + cudaGetErrorString(e));
-      return false;
-    }
-    g_hidden_dev[dev] = (float *)p;
+  void *p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_ffn_hidden);
+  if (e != cudaSuccess) {
+    ndl::capi_set_last_error(std::string("cudaGetSymbolAddress failed: ") + cudaGetErrorString(e));
+    return false;
   }
+  std::lock_guard<std::mutex> lock(g_mu);
   if (!g_kernels_ready[dev]) {
-    cudaError_t e = ndl::init_kernels();
+    e = ndl::init_kernels();
     if (e != cudaSuccess) {
       ndl::capi_set_last_error(std::string("kernel set-up failed: ") + cudaGetErrorString(e));
       return false;
     }
     g_kernels_ready[dev] = true;
   }
-  *hidden = g_hidden_dev[dev];
+  *hidden = (float *)p;
   return true;
 }
 
@@ -97,14 +96,22 @@ extern "C" int needle_ffn_forward_noalloc(const float *x, size_t T, size_t d_mod
   a.ldy = (int64_t)d_ff;
   a.epi = EPI_ACT;
   a.act = activation;
-  cudaError_t e = int4_matmul(x, (int64_t)d_model, (int)T, gu, a, st);
-  if (e == cudaSuccess) {
-    Int4Weight dn{down_data, down_scales, (int)d_ff, (int)d_model, G2, gs2};
-    MatmulOut o;
-    o.y = out;
-    o.ldy = (int64_t)d_model;
-    e = int4_matmul(hidden, (int64_t)d_ff, (int)T, dn, o, st);
+  Int4Weight dn{down_data, down_scales, (int)d_ff, (int)d_model, G2, gs2};
+  MatmulOut o;
+  o.y = out;
+  o.ldy = (int64_t)d_model;
+  // up to 8 tokens the matvec kernels hold x in shared memory: refuse what
+  // does not fit with the reason, not a bare launch error
+  const size_t need = std::max(int4_matmul_smem((int)T, gu, a), int4_matmul_smem((int)T, dn, o));
+  if (need > (size_t)kMaxDynSmem) {
+    capi_set_last_error("needle_ffn_forward_noalloc: " + std::to_string(T) + " tokens at d_model " +
+                        std::to_string(d_model) + ", d_ff " + std::to_string(d_ff) + " need " + std::to_string(need) +
+                        " bytes of shared memory per block; the limit is " + std::to_string(kMaxDynSmem) +
+                        " (up to 8 tokens a block holds every token's input row)");
+    return -1;
   }
+  cudaError_t e = int4_matmul(x, (int64_t)d_model, (int)T, gu, a, st);
+  if (e == cudaSuccess) e = int4_matmul(hidden, (int64_t)d_ff, (int)T, dn, o, st);
   if (e != cudaSuccess) {
     capi_set_last_error(std::string("CUDA error: ") + cudaGetErrorString(e));
     return -1;

@@ -343,123 +343,186 @@ __global__ void __launch_bounds__(256) gemv_kernel(const float *__restrict__ x, 
   }
 }
 
-// Decode matvec for M <= 8 rows on 16-byte weight loads.  CTA = 256
-// threads: CX column threads x (256 / CX) pair slices.  Each thread owns 16
-// consecutive output columns (one 16-byte load per pair row: 16 packed
-// bytes) and a contiguous run of pair rows; nibbles are unpacked in
-// registers, slices are reduced with warp shuffles and then across the 8
-// warps in shared memory.  The first batch of weight and scale loads is
-// issued before griddepcontrol.wait, so under programmatic dependent launch
-// it overlaps the previous kernel in the stream; x is read (and y written)
-// only after the wait.  Requires N % 16 == 0 and 16-byte aligned weights and
-// scales.
+// Matvec for M <= 8 rows on 16-byte weight loads (decode with few requests,
+// and the standalone INT4 matmul).  CTA = 256 threads = CX column threads x
+// KS = 256 / CX pair-row slices.  Each thread owns 16 consecutive output
+// columns (one 16-byte load per pair row) over a contiguous run of pair
+// rows, fetched with cp.async into its own slots of a shared-memory ring 8
+// pair rows ahead, so that loads stay in flight without holding registers.
+//
+// Unpack: the nibbles of a 32-bit word (4 columns, low nibble = row 2p, high
+// = row 2p+1) are XORed with 8 once, so nibble u' = q + 8 in [0, 15].  One
+// LOP3 then turns the nibble at bit s (s <= 12) into the float
+// 2^23 + u' * 2^s ((w & (0xF << s)) | 0x4B000000); one packed subtract of
+// (2^23 + 8 * 2^s) leaves q * 2^s exactly, and packed multiplies by x * 2^-s
+// (an exact power-of-two scaling) give the products q * x.  The upper
+// half-word takes one shift.  The terms are those of matvec_avx2
+// (quant.rs:209-297): (lo * x0 + hi * x1) * scale per pair row and column,
+// in f32; for a single row the pair terms of a 32-row scale group are
+// summed first and scaled once (another summation order, same terms).
+// About 4.5 instructions per weight byte with packed f32x2 arithmetic.
+//
+// Under programmatic dependent launch the first weight and scale loads are
+// issued before griddepcontrol.wait (no kernel of the stream writes
+// weights); x is read, and y written, after it.  Requires N % 16 == 0 and
+// 16-byte aligned weights and scales.
+// q * 2^s of the nibble (XORed with 8) at bit s of w, exactly: bias = 2^23 + 8 * 2^s.
+__device__ __forceinline__ float q4_at(uint32_t w, uint32_t mask, float bias) {
+  return __uint_as_float((w & mask) | 0x4B000000u) - bias;
+}
+
 template <int MR, int CX>
-__global__ void __launch_bounds__(256) gemv16_kernel(const float *__restrict__ x, int64_t ldx, int M, int K,
-                                                     Int4Weight W, EpiCtx e) {
-  constexpr int PY = 256 / CX;  // pair slices per CTA
+__global__ void __launch_bounds__(256, MR <= 2 ? 2 : 1) gemv_q4_kernel(const float *__restrict__ x, int64_t ldx,
+                                                                        int M, int K, Int4Weight W, EpiCtx e) {
+  constexpr int KS = 256 / CX;  // pair-row slices per CTA
   constexpr int NC = 16 * CX;   // columns per CTA
-  constexpr int PF = MR >= 4 ? 4 : 8;  // pair rows loaded per batch
+  constexpr int D = 8;          // pair rows in flight per thread (shared-memory ring)
   extern __shared__ __align__(16) float sm[];
   asm volatile("griddepcontrol.launch_dependents;");
-  const int N = W.N, Kp = W.G * W.gs, npairs = Kp >> 1;
-  const int tid = threadIdx.x, tx = tid % CX, ty = tid / CX;
+  const int N = W.N, Kp = W.G * W.gs, npairs = Kp >> 1, gp = W.gs >> 1;  // gp: pair rows per scale group
+  const int tid = threadIdx.x, tx = tid % CX, ks = tid / CX;
   const int n0 = blockIdx.x * NC, n = n0 + 16 * tx;
   const bool col_ok = n < N;
-  const int pp = (npairs + PY - 1) / PY;
-  const int p_beg = min(npairs, ty * pp), p_end = min(npairs, p_beg + pp);
-  float *xs = sm;                                   // [M][Kp]
-  float *red = sm + (((size_t)M * Kp + 3) & ~(size_t)3);  // [8 warps][MR][NC], 16-byte aligned
+  const int pp = (npairs + KS - 1) / KS;
+  const int p_beg = min(npairs, ks * pp), p_end = min(npairs, p_beg + pp);
+  uint4 *ring = reinterpret_cast<uint4 *>(sm);               // [D][256]: this thread's 16 bytes at [slot][tid]
+  float4 *xq = reinterpret_cast<float4 *>(sm) + D * 256;      // [MR][npairs]: (x0, x0 / 256, x1 / 16, x1 / 4096)
+  float *red = reinterpret_cast<float *>(xq + MR * npairs);  // reduction buffer
 
-  uint4 wb[PF];
-  auto load_batch = [&](int pb) {
+  // cp.async of pair row pi into slot (pi - p_beg) % D; one commit group per
+  // call (empty past the slice), so group counts stay uniform.
+  const uint32_t ring0 = (uint32_t)__cvta_generic_to_shared(ring + tid);
+  const uint8_t *wcol = W.w + n;
+  auto issue = [&](int pi, int slot) {
+    if (col_ok && pi < p_end)
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(ring0 + slot * 4096u), "l"(wcol + (int64_t)pi * N)
+                   : "memory");
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  float sc[16], scn[16];  // this and the next scale group
+  auto load_scales = [&](int g, float *dst) {
+    const float4 *sp = reinterpret_cast<const float4 *>(W.s + (int64_t)g * N + n);
+    const bool ok = col_ok && g * gp < p_end;
 #pragma unroll
-    for (int i = 0; i < PF; ++i) {
-      const int pi = pb + i;
-      wb[i] = (col_ok && pi < p_end) ? __ldg(reinterpret_cast<const uint4 *>(W.w + (int64_t)pi * N + n))
-                                     : make_uint4(0u, 0u, 0u, 0u);
+    for (int q = 0; q < 4; ++q) {
+      const float4 v = ok ? __ldg(sp + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+      dst[4 * q] = v.x;
+      dst[4 * q + 1] = v.y;
+      dst[4 * q + 2] = v.z;
+      dst[4 * q + 3] = v.w;
     }
   };
-  float sc[16];
-  int gcur = -1;
-  auto load_scales = [&](int g) {
-    if (col_ok) {
-      const float4 *sp = reinterpret_cast<const float4 *>(W.s + (int64_t)g * N + n);
+  int g = p_beg < p_end ? p_beg / gp : 0;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        float4 v = __ldg(sp + q);
-        sc[4 * q] = v.x;
-        sc[4 * q + 1] = v.y;
-        sc[4 * q + 2] = v.z;
-        sc[4 * q + 3] = v.w;
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 16; ++j) sc[j] = 0.0f;
-    }
-    gcur = g;
-  };
-  load_batch(p_beg);
-  if (p_beg < p_end) load_scales((2 * p_beg) / W.gs);
+  for (int d = 0; d < D - 1; ++d) issue(p_beg + d, d);
+  load_scales(g, sc);
+  load_scales(g + 1, scn);
 
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  for (int i = tid; i < M * Kp; i += 256) {
-    int m = i / Kp, k = i - m * Kp;
-    xs[i] = k < K ? x[(int64_t)m * ldx + k] : 0.0f;
+  for (int i = tid; i < MR * npairs; i += 256) {
+    const int m = i / npairs, p = i - m * npairs;
+    float x0 = 0.0f, x1 = 0.0f;
+    if (m < M) {
+      if (2 * p < K) x0 = x[(int64_t)m * ldx + 2 * p];
+      if (2 * p + 1 < K) x1 = x[(int64_t)m * ldx + 2 * p + 1];
+    }
+    xq[i] = make_float4(x0, x0 * 0.00390625f, x1 * 0.0625f, x1 * 0.000244140625f);
   }
   __syncthreads();
 
-  float acc[MR][16];
+  // one row: per-group sums of (lo * x0 + hi * x1), times the group's scale
+  // when the group ends (one scale FMA per 16 pair rows); more rows: scale
+  // per pair row (fewer registers)
+  constexpr bool kGroupSums = MR == 1;
+  float acc[MR][16], inner[kGroupSums ? MR : 1][16];
 #pragma unroll
   for (int m = 0; m < MR; ++m)
 #pragma unroll
     for (int j = 0; j < 16; ++j) acc[m][j] = 0.0f;
-
-  for (int p = p_beg; p < p_end; p += PF) {
-    if (p != p_beg) load_batch(p);
 #pragma unroll
-    for (int i = 0; i < PF; ++i) {
-      const int pi = p + i;
-      if (pi < p_end) {
-        const int g = (2 * pi) / W.gs;
-        if (g != gcur) load_scales(g);
-        const uint32_t wd[4] = {wb[i].x, wb[i].y, wb[i].z, wb[i].w};
-        float lo[16], hi[16];
+  for (int m = 0; m < (kGroupSums ? MR : 1); ++m)
+#pragma unroll
+    for (int j = 0; j < 16; ++j) inner[m][j] = 0.0f;
+  auto flush = [&]() {
+    if constexpr (kGroupSums) {
+#pragma unroll
+      for (int m = 0; m < MR; ++m)
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-          const uint32_t b = (wd[j >> 2] >> (8 * (j & 3))) & 0xFFu;
-          lo[j] = (float)sign_extend4(b & 0xFu);
-          hi[j] = (float)sign_extend4(b >> 4);
+          acc[m][j] = fmaf(inner[m][j], sc[j], acc[m][j]);
+          inner[m][j] = 0.0f;
         }
+    }
+  };
+
+  int slot = 0, gend = (g + 1) * gp;
+#pragma unroll 2
+  for (int pi = p_beg; pi < p_end; ++pi) {
+    asm volatile("cp.async.wait_group %0;" ::"n"(D - 2) : "memory");  // row pi has landed
+    const uint4 cw = ring[slot * 256 + tid];
+    issue(pi + D - 1, slot == 0 ? D - 1 : slot - 1);  // into the slot row pi - 1 left
+    slot = slot == D - 1 ? 0 : slot + 1;
+    {
+      if (pi >= gend) {  // next scale group
+        flush();
+        ++g;
+        gend += gp;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) sc[j] = scn[j];
+        load_scales(g + 1, scn);
+      }
+      float4 xv[MR];
+#pragma unroll
+      for (int m = 0; m < MR; ++m) xv[m] = xq[m * npairs + pi];
+      const uint32_t wd[4] = {cw.x ^ 0x88888888u, cw.y ^ 0x88888888u, cw.z ^ 0x88888888u, cw.w ^ 0x88888888u};
+#pragma unroll
+      for (int wq = 0; wq < 4; ++wq) {
+        const uint32_t wl = wd[wq], wu = wd[wq] >> 16;
+        // columns 4wq .. 4wq+3: low nibbles at bits 0 / 8, high at 4 / 12 of each half-word
+        const float lo[4] = {q4_at(wl, 0xFu, 8388616.0f), q4_at(wl, 0xF00u, 8390656.0f), q4_at(wu, 0xFu, 8388616.0f),
+                             q4_at(wu, 0xF00u, 8390656.0f)};
+        const float hi[4] = {q4_at(wl, 0xF0u, 8388736.0f), q4_at(wl, 0xF000u, 8421376.0f),
+                             q4_at(wu, 0xF0u, 8388736.0f), q4_at(wu, 0xF000u, 8421376.0f)};
 #pragma unroll
         for (int m = 0; m < MR; ++m) {
-          if (m < M) {
-            const float x0 = xs[m * Kp + 2 * pi], x1 = xs[m * Kp + 2 * pi + 1];
+          // x pre-scaled per nibble position: (x0, x0 / 256, x1 / 16, x1 / 4096)
+          const float xl[4] = {xv[m].x, xv[m].y, xv[m].x, xv[m].y}, xh[4] = {xv[m].z, xv[m].w, xv[m].z, xv[m].w};
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              // per-pair term in the order of matvec_avx2: (lo*x0 + hi*x1) * scale
-              const float t = fmaf(hi[j], x1, lo[j] * x0);
-              acc[m][j] += t * sc[j];
+          for (int c = 0; c < 4; ++c) {
+            if constexpr (kGroupSums) {
+              inner[m][4 * wq + c] = fmaf(hi[c], xh[c], fmaf(lo[c], xl[c], inner[m][4 * wq + c]));
+            } else {  // (lo * x0 + hi * x1) * scale, as matvec_avx2 orders it
+              acc[m][4 * wq + c] = fmaf(fmaf(hi[c], xh[c], lo[c] * xl[c]), sc[4 * wq + c], acc[m][4 * wq + c]);
             }
           }
         }
       }
     }
   }
-  // Reduce the slices of this warp (lanes with equal tx), then across warps.
-#pragma unroll
-  for (int off = CX; off < 32; off <<= 1)
-#pragma unroll
-    for (int m = 0; m < MR; ++m)
-#pragma unroll
-      for (int j = 0; j < 16; ++j) acc[m][j] += __shfl_xor_sync(0xffffffffu, acc[m][j], off);
+  flush();
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+
+  // Reduce the pair-row slices: lanes of one warp that share columns (CX <
+  // 32) by shuffles, then the R partial rows in shared memory in a fixed order.
+  constexpr int R = CX >= 32 ? KS : 8;
   const int warp = tid >> 5, lane = tid & 31;
-  if (lane < CX) {
+  float (&a)[MR][16] = acc;
+  if constexpr (CX < 32) {
+#pragma unroll
+    for (int off = CX; off < 32; off <<= 1)
+#pragma unroll
+      for (int m = 0; m < MR; ++m)
+#pragma unroll
+        for (int j = 0; j < 16; ++j) a[m][j] += __shfl_xor_sync(0xffffffffu, a[m][j], off);
+  }
+  const int rslot = CX >= 32 ? ks : warp;
+  if (CX >= 32 || lane < CX) {
 #pragma unroll
     for (int m = 0; m < MR; ++m)
 #pragma unroll
       for (int j = 0; j < 16; j += 4)
-        *reinterpret_cast<float4 *>(red + (warp * MR + m) * NC + 16 * lane + j) =
-            make_float4(acc[m][j], acc[m][j + 1], acc[m][j + 2], acc[m][j + 3]);
+        *reinterpret_cast<float4 *>(red + (rslot * MR + m) * NC + 16 * tx + j) =
+            make_float4(a[m][j], a[m][j + 1], a[m][j + 2], a[m][j + 3]);
   }
   __syncthreads();
   for (int i = tid; i < M * (NC / 4); i += 256) {
@@ -468,12 +531,12 @@ __global__ void __launch_bounds__(256) gemv16_kernel(const float *__restrict__ x
     if (nn < N) {
       float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-      for (int w = 0; w < 8; ++w) {
-        const float4 r = *reinterpret_cast<const float4 *>(red + (w * MR + m) * NC + 4 * c4);
-        v[0] += r.x;
-        v[1] += r.y;
-        v[2] += r.z;
-        v[3] += r.w;
+      for (int r = 0; r < R; ++r) {
+        const float4 t = *reinterpret_cast<const float4 *>(red + (r * MR + m) * NC + 4 * c4);
+        v[0] += t.x;
+        v[1] += t.y;
+        v[2] += t.z;
+        v[3] += t.w;
       }
       store4(e, m, nn, v[0], v[1], v[2], v[3], false);
     }
@@ -481,11 +544,16 @@ __global__ void __launch_bounds__(256) gemv16_kernel(const float *__restrict__ x
 }
 
 template <int MR, int CX>
-cudaError_t launch_gemv16(const float *x, int64_t ldx, int M, const Int4Weight &W, const EpiCtx &e, bool pdl,
-                          cudaStream_t stream) {
+size_t gemv_q4_smem(int Kp) {
+  constexpr int KS = 256 / CX, R = CX >= 32 ? KS : 8;
+  return (size_t)8 * 256 * 16 + (size_t)MR * (Kp / 2) * 16 + (size_t)R * MR * 16 * CX * 4;
+}
+
+template <int MR, int CX>
+cudaError_t launch_gemv_q4(const float *x, int64_t ldx, int M, const Int4Weight &W, const EpiCtx &e, bool pdl,
+                           cudaStream_t stream) {
   constexpr int NC = 16 * CX;
-  const int Kp = W.G * W.gs;
-  const size_t sm = ((((size_t)M * Kp + 3) & ~(size_t)3) + (size_t)8 * MR * NC) * sizeof(float);
+  const size_t sm = gemv_q4_smem<MR, CX>(W.G * W.gs);
   if (sm > (size_t)kMaxDynSmem) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((W.N + NC - 1) / NC);
@@ -497,16 +565,49 @@ cudaError_t launch_gemv16(const float *x, int64_t ldx, int M, const Int4Weight &
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, gemv16_kernel<MR, CX>, x, ldx, M, W.K, W, e);
+  return cudaLaunchKernelEx(&cfg, gemv_q4_kernel<MR, CX>, x, ldx, M, W.K, W, e);
 }
 
-template <int CX>
-cudaError_t dispatch_gemv16(const float *x, int64_t ldx, int M, const Int4Weight &W, const EpiCtx &e, bool pdl,
-                            cudaStream_t stream) {
-  if (M <= 1) return launch_gemv16<1, CX>(x, ldx, M, W, e, pdl, stream);
-  if (M <= 2) return launch_gemv16<2, CX>(x, ldx, M, W, e, pdl, stream);
-  if (M <= 4) return launch_gemv16<4, CX>(x, ldx, M, W, e, pdl, stream);
-  return launch_gemv16<8, CX>(x, ldx, M, W, e, pdl, stream);
+// Column threads per CTA: 1024 columns a CTA for wide matrices (long runs of
+// pair rows per thread, few reductions), narrower CTAs (more pair-row
+// slices, down to 32 columns) while the grid would not cover the SMs.
+int gemv_q4_cx(int MR, int N) {
+  const int cols16 = N / 16;
+  if (MR <= 2 && cols16 >= 64 * 296) return 64;
+  if (MR <= 2 && cols16 >= 32 * 296) return 32;
+  if (cols16 >= 16 * 148) return 16;
+  if (cols16 >= 8 * 148) return 8;
+  if (cols16 >= 4 * 148) return 4;
+  return 2;
+}
+
+template <int MR>
+cudaError_t dispatch_gemv_q4(const float *x, int64_t ldx, int M, const Int4Weight &W, const EpiCtx &e, bool pdl,
+                             cudaStream_t stream) {
+  switch (gemv_q4_cx(MR, W.N)) {
+    case 64:
+      if constexpr (MR <= 2) return launch_gemv_q4<MR, 64>(x, ldx, M, W, e, pdl, stream);
+      break;
+    case 32:
+      if constexpr (MR <= 2) return launch_gemv_q4<MR, 32>(x, ldx, M, W, e, pdl, stream);
+      break;
+    case 16:
+      return launch_gemv_q4<MR, 16>(x, ldx, M, W, e, pdl, stream);
+    case 8:
+      return launch_gemv_q4<MR, 8>(x, ldx, M, W, e, pdl, stream);
+    case 4:
+      return launch_gemv_q4<MR, 4>(x, ldx, M, W, e, pdl, stream);
+    default:
+      break;
+  }
+  return launch_gemv_q4<MR, 2>(x, ldx, M, W, e, pdl, stream);
+}
+
+// The 16-byte-load matvec serves M <= 8 rows of a plain (unpaired) weight
+// whose columns come in 16s, with 16-byte aligned data and scales.
+bool gemv_q4_fits(int M, const Int4Weight &W, const MatmulOut &o) {
+  return M <= 8 && !W.w2 && o.epi != EPI_KNORM && (W.N % 16) == 0 && ((uintptr_t)W.w % 16) == 0 &&
+         ((uintptr_t)W.s % 16) == 0;
 }
 
 __global__ void quantize_kernel(const float *__restrict__ w, int K, int N, int gs, int G, uint8_t *data,
@@ -558,10 +659,16 @@ __global__ void dequantize_kernel(const uint8_t *__restrict__ data, const float 
 cudaError_t init_matmul_kernels() {
   cudaError_t e = cudaSuccess;
   for (const void *f : {(const void *)tile_kernel, (const void *)gemv_kernel<8>, (const void *)gemv_kernel<16>,
-                        (const void *)gemv16_kernel<1, 2>, (const void *)gemv16_kernel<2, 2>,
-                        (const void *)gemv16_kernel<4, 2>, (const void *)gemv16_kernel<8, 2>,
-                        (const void *)gemv16_kernel<1, 4>, (const void *)gemv16_kernel<2, 4>,
-                        (const void *)gemv16_kernel<4, 4>, (const void *)gemv16_kernel<8, 4>}) {
+                        (const void *)gemv_q4_kernel<1, 8>, (const void *)gemv_q4_kernel<1, 16>,
+                        (const void *)gemv_q4_kernel<1, 32>, (const void *)gemv_q4_kernel<1, 64>,
+                        (const void *)gemv_q4_kernel<2, 8>, (const void *)gemv_q4_kernel<2, 16>,
+                        (const void *)gemv_q4_kernel<2, 32>, (const void *)gemv_q4_kernel<2, 64>,
+                        (const void *)gemv_q4_kernel<4, 8>, (const void *)gemv_q4_kernel<4, 16>,
+                        (const void *)gemv_q4_kernel<8, 8>, (const void *)gemv_q4_kernel<8, 16>,
+                        (const void *)gemv_q4_kernel<1, 2>, (const void *)gemv_q4_kernel<1, 4>,
+                        (const void *)gemv_q4_kernel<2, 2>, (const void *)gemv_q4_kernel<2, 4>,
+                        (const void *)gemv_q4_kernel<4, 2>, (const void *)gemv_q4_kernel<4, 4>,
+                        (const void *)gemv_q4_kernel<8, 2>, (const void *)gemv_q4_kernel<8, 4>}) {
     cudaError_t r = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
     if (r != cudaSuccess) e = r;
   }
@@ -583,11 +690,11 @@ cudaError_t int4_matmul(const float *x, int64_t ldx, int M, const Int4Weight &W,
   if (o.epi == EPI_ACT && ((W.N & 1) || o.planes[0])) return cudaErrorInvalidValue;  // planes: tensor-core only
   EpiCtx e{o, W.N};
   const int Kp = W.G * W.gs;
-  if (M <= 8 && !W.w2 && o.epi != EPI_KNORM && (W.N % 16) == 0 && ((uintptr_t)W.w % 16) == 0 &&
-      ((uintptr_t)W.s % 16) == 0) {
-    // 128 or more CTAs where the width allows, else 32-column CTAs
-    if (W.N / 64 >= 96) return dispatch_gemv16<4>(x, ldx, M, W, e, pdl, stream);
-    return dispatch_gemv16<2>(x, ldx, M, W, e, pdl, stream);
+  if (gemv_q4_fits(M, W, o)) {
+    if (M <= 1) return dispatch_gemv_q4<1>(x, ldx, M, W, e, pdl, stream);
+    if (M <= 2) return dispatch_gemv_q4<2>(x, ldx, M, W, e, pdl, stream);
+    if (M <= 4) return dispatch_gemv_q4<4>(x, ldx, M, W, e, pdl, stream);
+    return dispatch_gemv_q4<8>(x, ldx, M, W, e, pdl, stream);
   }
   if (M <= 8) {
     if (o.epi == EPI_KNORM || W.N > 1024) {
@@ -609,6 +716,20 @@ cudaError_t int4_matmul(const float *x, int64_t ldx, int M, const Int4Weight &W,
   if (grid.y > 65535) return cudaErrorInvalidConfiguration;
   tile_kernel<<<grid, 256, sm, stream>>>(x, ldx, M, W.K, W, e, xvec, yvec);
   return cudaGetLastError();
+}
+
+size_t int4_matmul_smem(int M, const Int4Weight &W, const MatmulOut &o) {
+  if (M <= 0 || W.N <= 0 || W.G <= 0 || W.gs <= 0) return 0;
+  const int Kp = W.G * W.gs;
+  if (gemv_q4_fits(M, W, o)) {
+    const int MR = M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8, CX = gemv_q4_cx(MR, W.N);
+    const int R = CX >= 32 ? 256 / CX : 8;
+    return (size_t)8 * 256 * 16 + (size_t)MR * (Kp / 2) * 16 + (size_t)R * MR * 16 * CX * 4;
+  }
+  if (M <= 8)
+    return (o.epi == EPI_KNORM || W.N > 1024) ? ((size_t)M * Kp + (size_t)16 * M * 64) * sizeof(float)
+                                               : ((size_t)M * Kp + (size_t)32 * M * 32) * sizeof(float);
+  return (size_t)2 * TBK * (XS + TBN) * sizeof(float);
 }
 
 cudaError_t int4_quantize(const float *w, int K, int N, uint8_t *data, float *scales, cudaStream_t st) {

@@ -94,6 +94,10 @@ struct MatmulOut {
 // Y[M, N] (epilogue) X[M, K] @ W.  x row stride ldx (floats).
 cudaError_t int4_matmul(const float *x, int64_t ldx, int M, const Int4Weight &W, const MatmulOut &o,
                         cudaStream_t stream, bool pdl = false);
+// Dynamic shared memory (bytes) int4_matmul requests for these arguments;
+// above kMaxDynSmem it refuses the call (cudaErrorInvalidValue).  Up to 8
+// rows it holds x: M * (K rounded up to the group) floats and more.
+size_t int4_matmul_smem(int M, const Int4Weight &W, const MatmulOut &o);
 
 // ── tensor-core path (tc_gemm.cu) ──
 // A pair of bf16 planes (hi, lo) of a [rows][Kp] K-contiguous operand, with

@@ -56,8 +56,51 @@ def test_noalloc_matches_allocating_entry_point_twice():
         assert close_act(got, ref)
 
 
+@pytest.mark.parametrize("T,act", [(1, 0), (1, 2), (8, 1), (8, 0)])
+def test_noalloc_few_tokens(T, act):
+    # up to 8 tokens the block runs on the matvec kernels (gate and up
+    # interleaved, the activation in the epilogue)
+    got, ref = run_both(T, act, 10 + T + act)
+    assert not np.isnan(got).any()
+    assert close_act(got, ref)
+
+
+def test_noalloc_allocates_nothing():
+    # The call must take nothing from the device's stream-ordered pool (the
+    # allocator needle_ffn_forward uses): reset the pool's high-water mark,
+    # call twice, and the mark must not have moved past the memory in use.
+    rt = pytest.importorskip("cuda.bindings.runtime")
+    drv = pytest.importorskip("cuda.bindings.driver")
+    T, d, ff = 64, 512, 2048
+    rng = np.random.default_rng(3)
+    x = dev(rng.standard_normal((T, d)).astype(np.float32))
+    w = [[dev(a) for a in wl.random_int4(rng, d if i < 2 else ff, ff if i < 2 else d)] for i in range(3)]
+    ptrs = [[t.data_ptr() for t in pair] for pair in w]
+    out = torch.empty((T, d), device="cuda")
+    nb.ffn_forward_noalloc(x.data_ptr(), T, d, ff, ptrs[0], ptrs[1], ptrs[2], 0, out.data_ptr())
+    torch.cuda.synchronize()
+    err, pool = rt.cudaDeviceGetDefaultMemPool(torch.cuda.current_device())
+    assert err == rt.cudaError_t.cudaSuccess
+    used_high = rt.cudaMemPoolAttr.cudaMemPoolAttrUsedMemHigh
+    used_now = rt.cudaMemPoolAttr.cudaMemPoolAttrUsedMemCurrent
+    (err,) = rt.cudaMemPoolSetAttribute(pool, used_high, drv.cuuint64_t(0))  # 0 resets the mark to current use
+    assert err == rt.cudaError_t.cudaSuccess
+    free0 = torch.cuda.mem_get_info()[0]
+    for _ in range(2):
+        nb.ffn_forward_noalloc(x.data_ptr(), T, d, ff, ptrs[0], ptrs[1], ptrs[2], 0, out.data_ptr())
+    torch.cuda.synchronize()
+    err, high = rt.cudaMemPoolGetAttribute(pool, used_high)
+    err2, now = rt.cudaMemPoolGetAttribute(pool, used_now)
+    assert err == err2 == rt.cudaError_t.cudaSuccess
+    assert int(high) == int(now)
+    assert torch.cuda.mem_get_info()[0] == free0
+
+
 def test_noalloc_rejects_oversize():
     x = torch.zeros(1, device="cuda")
     p = x.data_ptr()
     with pytest.raises(nb.NeedleError, match="exceeds the fixed hidden buffer"):
         nb.ffn_forward_noalloc(p, 513, 512, 2048, [p, p], [p, p], [p, p], 0, p)
+    # few tokens over a wide hidden layer: the shared-memory limit, named
+    with pytest.raises(nb.NeedleError, match="shared memory"):
+        nb.ffn_forward_noalloc(p, 8, 512, 8192, [p, p], [p, p], [p, p], 0, p)

@@ -456,6 +456,42 @@ def op_suite(args, nb, wl, torch, np, pk, eng, blob):
     return out
 
 
+def profile_ops(nb, wl, torch, np):
+    """One untimed launch of each INT4-path kernel, for ncu: the matvec over
+    2048 x 512 columns side by side (its streaming rate) and over 2048
+    columns (config 0), the tensor-core matmul at 512 rows (split-K clusters)
+    and 4096 rows (persistent, TMA epilogue) for (N, K) = (512, 512), and the
+    MLP block plan over 256 tokens."""
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
+    K = 512
+    x, packed, scales = wl.int4_case(1, 2048, K, seed=0)
+    for R in (512, 1):
+        W = dev(np.tile(packed.reshape(K // 2, 2048), (1, R)))
+        S = dev(np.tile(scales, (1, R)))
+        Y = torch.empty((1, 2048 * R), device="cuda")
+        nb.int4_matmul(dev(x).data_ptr(), 1, K, W.data_ptr(), S.data_ptr(), 2048 * R, K // 32, Y.data_ptr())
+        torch.cuda.synchronize()
+    for M in (512, 4096):
+        x, packed, scales = wl.int4_case(M, 512, K, seed=M)
+        Wd, Sd, Xd = dev(packed), dev(scales), dev(x)
+        Yd = torch.empty((M, 512), device="cuda")
+        plan = nb.Int4Plan(Wd.data_ptr(), Sd.data_ptr(), K, 512, K // 32, M)
+        plan.matmul(Xd.data_ptr(), M, Yd.data_ptr())
+        plan.status()
+        plan.close()
+    rng = np.random.default_rng(2)
+    g, u, dn = wl.random_int4(rng, 512, 2048), wl.random_int4(rng, 512, 2048), wl.random_int4(rng, 2048, 512)
+    gd, ud, dd = [dev(a) for a in g], [dev(a) for a in u], [dev(a) for a in dn]
+    xd, od = dev(rng.standard_normal((256, 512)).astype(np.float32)), torch.empty((256, 512), device="cuda")
+    plan = nb.FfnPlan(512, 2048, [a.data_ptr() for a in gd], [a.data_ptr() for a in ud], [a.data_ptr() for a in dd],
+                      max_t=256)
+    plan.forward(xd.data_ptr(), 256, 0, od.data_ptr())
+    plan.status()
+    plan.close()
+    print(json.dumps({"profile_ops": True}), flush=True)
+    return 0
+
+
 class Clocks:
     """nvidia-smi sampler for the timed region."""
 
@@ -518,6 +554,8 @@ def main():
     ap.add_argument("--no-weak", action="store_true", help="skip the weak-scaled line at more than one rank")
     ap.add_argument("--profile-run", action="store_true",
                     help="one untimed run of the workload and exit (for ncu launch lists)")
+    ap.add_argument("--profile-ops", action="store_true",
+                    help="one untimed launch of each INT4-path kernel and exit (for ncu)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl != "reference":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
@@ -547,6 +585,8 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    if args.profile_ops:
+        return profile_ops(nb, wl, torch, np)
     per_gpu = args.requests_per_gpu or None
     blob, ids, off, masks, n_total = workload(args, wl, nb, rank, world, per_gpu)
     n_req = off.size - 1

@@ -1074,7 +1074,8 @@ bool Batch::decode_step(std::string &err, bool capture, int att_rows) {
     o.splitk_ws = splitk_ws_;
     NDL_LK(tc_matmul(*hp, B, m.emb_tc, c.vocab_size, o, m.kerr, st, m.emb_bf16_exact));
   } else {
-    NDL_LK(head_argmax(h_, B, m.emb, c.vocab_size, d, mask_, W_, logits_, spec_.max_new, pos_, keys_, st));
+    NDL_LK(head_argmax(h_, B, m.emb, c.vocab_size, d, mask_, W_, logits_, spec_.max_new, pos_, keys_, st,
+                       m.emb_bf16_exact && m.emb_tc_ready ? m.emb_hi : nullptr, m.emb_tc.Kp));
   }
   if (!tend(ev, 2.0 * B * c.vocab_size * (double)d,
             (double)c.vocab_size * d * 4 + (double)B * d * 4 + (mask_ ? (double)B * W_ * 8 : 0.0), err))

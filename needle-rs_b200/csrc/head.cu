@@ -96,6 +96,87 @@ __global__ void __launch_bounds__(256) head_gemv_kernel(const float *__restrict_
   }
 }
 
+// Small batch over the bf16 copy of the embedding, used when every value of
+// the embedding is exactly a bf16 (as the shipped checkpoints store it):
+// the same products as over the f32 copy, from half the bytes.  One warp
+// per 4 vocabulary rows; each lane loads CPL 16-byte chunks (8 values) of
+// every row, all of the warp's loads issued before the first is used.
+template <int CPL>
+__global__ void __launch_bounds__(256) head_gemv_bf16_kernel(const float *__restrict__ h, int B,
+                                                             const uint16_t *__restrict__ emb, int64_t ld, int V,
+                                                             int d, HeadIO io, unsigned long long *keys) {
+  extern __shared__ __align__(16) float hs[];  // [B][d]
+  __shared__ unsigned long long best_s[8][HB_MAX];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int v0 = (blockIdx.x * 8 + warp) * H_ROWS_PER_WARP;
+  uint4 ev[H_ROWS_PER_WARP][CPL];
+#pragma unroll
+  for (int r = 0; r < H_ROWS_PER_WARP; ++r)
+#pragma unroll
+    for (int j = 0; j < CPL; ++j)
+      ev[r][j] = v0 + r < V ? __ldg(reinterpret_cast<const uint4 *>(emb + (int64_t)(v0 + r) * ld) + lane + 32 * j)
+                            : make_uint4(0u, 0u, 0u, 0u);
+  for (int i = tid; i < B * d; i += 256) hs[i] = h[i];
+  __syncthreads();
+  unsigned long long best[HB_MAX];
+#pragma unroll
+  for (int b = 0; b < HB_MAX; ++b) best[b] = 0ull;
+#pragma unroll
+  for (int r = 0; r < H_ROWS_PER_WARP; ++r) {
+    const int v = v0 + r;
+    if (v >= V) break;
+    float part[HB_MAX];
+#pragma unroll
+    for (int b = 0; b < HB_MAX; ++b) part[b] = 0.0f;
+#pragma unroll
+    for (int j = 0; j < CPL; ++j) {
+      const uint32_t w[4] = {ev[r][j].x, ev[r][j].y, ev[r][j].z, ev[r][j].w};
+      float e[8];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {  // bf16 -> f32 is exact: the bits move up
+        e[2 * q] = __uint_as_float(w[q] << 16);
+        e[2 * q + 1] = __uint_as_float(w[q] & 0xFFFF0000u);
+      }
+      const int c = 8 * (lane + 32 * j);
+#pragma unroll
+      for (int b = 0; b < HB_MAX; ++b) {
+        if (b < B) {
+          const float4 h0 = *reinterpret_cast<const float4 *>(hs + b * d + c);
+          const float4 h1 = *reinterpret_cast<const float4 *>(hs + b * d + c + 4);
+          part[b] = fmaf(h0.x, e[0], part[b]);
+          part[b] = fmaf(h0.y, e[1], part[b]);
+          part[b] = fmaf(h0.z, e[2], part[b]);
+          part[b] = fmaf(h0.w, e[3], part[b]);
+          part[b] = fmaf(h1.x, e[4], part[b]);
+          part[b] = fmaf(h1.y, e[5], part[b]);
+          part[b] = fmaf(h1.z, e[6], part[b]);
+          part[b] = fmaf(h1.w, e[7], part[b]);
+        }
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < HB_MAX; ++b) {
+      if (b < B) {
+        const float lg = warp_sum(part[b]);
+        const float mv = masked(lg, io.mrow(b), v);
+        float *lr = io.lrow(b, V);
+        if (lr && lane == 0) lr[v] = mv;
+        const unsigned long long k = argmax_key(mv, (uint32_t)v);
+        best[b] = k > best[b] ? k : best[b];
+      }
+    }
+  }
+  if (lane == 0)
+#pragma unroll
+    for (int b = 0; b < HB_MAX; ++b) best_s[warp][b] = best[b];
+  __syncthreads();
+  if (tid < B) {
+    unsigned long long k = 0ull;
+    for (int w = 0; w < 8; ++w) k = best_s[w][tid] > k ? best_s[w][tid] : k;
+    atomicMax(keys + tid, k);
+  }
+}
+
 // Large batch: 128 (requests) x 128 (vocab) tile, BK = 32, 8x8 per thread.
 constexpr int HBM_ = 128, HBN = 128, HBK = 32, HXS = 132;
 
@@ -248,7 +329,8 @@ cudaError_t init_kernels() {
 }
 
 cudaError_t head_argmax(const float *h, int B, const float *emb, int V, int d, const uint64_t *mask, int mask_words,
-                        float *logits, int max_new, const int32_t *pos, unsigned long long *keys, cudaStream_t st) {
+                        float *logits, int max_new, const int32_t *pos, unsigned long long *keys, cudaStream_t st,
+                        const void *emb_bf16, int64_t ld_bf16) {
   HeadIO io{mask, mask_words, logits, max_new, pos};
   if (B <= 0) return cudaSuccess;
   if (d & 3) return cudaErrorInvalidValue;
@@ -256,6 +338,16 @@ cudaError_t head_argmax(const float *h, int B, const float *emb, int V, int d, c
     size_t sm = (size_t)B * d * sizeof(float);
     if (sm > (size_t)kMaxDynSmem) return cudaErrorInvalidValue;
     int rows_per_cta = 8 * H_ROWS_PER_WARP;
+    const int cpl = d / 256;
+    if (emb_bf16 && d % 256 == 0 && cpl >= 1 && cpl <= 4 && ld_bf16 % 8 == 0 && ((uintptr_t)emb_bf16 % 16) == 0) {
+      const uint16_t *e = (const uint16_t *)emb_bf16;
+      const dim3 grid((V + rows_per_cta - 1) / rows_per_cta);
+      if (cpl == 1) head_gemv_bf16_kernel<1><<<grid, 256, sm, st>>>(h, B, e, ld_bf16, V, d, io, keys);
+      if (cpl == 2) head_gemv_bf16_kernel<2><<<grid, 256, sm, st>>>(h, B, e, ld_bf16, V, d, io, keys);
+      if (cpl == 3) head_gemv_bf16_kernel<3><<<grid, 256, sm, st>>>(h, B, e, ld_bf16, V, d, io, keys);
+      if (cpl == 4) head_gemv_bf16_kernel<4><<<grid, 256, sm, st>>>(h, B, e, ld_bf16, V, d, io, keys);
+      return cudaGetLastError();
+    }
     head_gemv_kernel<<<(V + rows_per_cta - 1) / rows_per_cta, 256, sm, st>>>(h, B, emb, V, d, io, keys);
     return cudaGetLastError();
   }

@@ -124,7 +124,7 @@ cudaError_t tc_split_rows(const float *x, int64_t ldx, int M, int K, int Kp, voi
 // (tcgen05, 3-term bf16 split, f32 accumulation).  *err is set if a bounded
 // wait inside the kernel expired.
 // b_lo_zero: B's lo plane is all zero (a bf16-exact operand such as the
-// embedding), so the hi*lo product is skipped.
+// embedding): the hi*lo product is skipped and the lo plane is not loaded.
 cudaError_t tc_matmul(const TcPlanes &A, int M, const TcPlanes &B, int N, const MatmulOut &o, int *err,
                       cudaStream_t st, bool b_lo_zero = false);
 cudaError_t init_tc_kernels();
@@ -247,7 +247,11 @@ cudaError_t decoder_cross_attention(const float *q, const float *q_norm, const f
 // `logits` is set, go to logits[(b*max_new + pos[b]) * V ...].  keys[b] must
 // be zero on entry and receives the packed (logit key, index) maximum.
 cudaError_t head_argmax(const float *h, int B, const float *emb, int V, int d, const uint64_t *mask, int mask_words,
-                        float *logits, int max_new, const int32_t *pos, unsigned long long *keys, cudaStream_t st);
+                        float *logits, int max_new, const int32_t *pos, unsigned long long *keys, cudaStream_t st,
+                        const void *emb_bf16 = nullptr, int64_t ld_bf16 = 0);
+// emb_bf16 (optional): the embedding as bf16 rows of stride ld_bf16, equal
+// to emb value for value (a bf16-exact embedding); small batches then read
+// it instead of the f32 copy.
 
 // After head_argmax, for request b at step s = pos[b]: next = index of
 // keys[b]; unless the request is done, append next to out_ids[b*max_new +

@@ -463,15 +463,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           for (int kb = 0; kb < nkb; ++kb) {
             if (!(ok = mbar_wait(&empty[stage], phase ^ 1, err))) break;
             uint8_t *st = smem + stage * STAGE_BYTES;
-            mbar_expect_tx(&full[stage], STAGE_BYTES);
+            mbar_expect_tx(&full[stage], b_lo_zero ? STAGE_BYTES - B_BYTES : STAGE_BYTES);
             tma_load_2d(st, &tmAh, &full[stage], kb * TC_BK, mt * TC_BM);
             tma_load_2d(st + A_BYTES, &tmAl, &full[stage], kb * TC_BK, mt * TC_BM);
   #pragma unroll
             for (int h = 0; h < BN / 128; ++h) {  // 128-row boxes, contiguous in shared memory
               tma_load_2d(st + 2 * A_BYTES + h * (B_BYTES * 128 / BN), &tmBh, &full[stage], kb * TC_BK,
                           nt * BN + 128 * h);
-              tma_load_2d(st + 2 * A_BYTES + B_BYTES + h * (B_BYTES * 128 / BN), &tmBl, &full[stage], kb * TC_BK,
-                          nt * BN + 128 * h);
+              if (!b_lo_zero)  // an all-zero lo plane is neither loaded nor multiplied
+                tma_load_2d(st + 2 * A_BYTES + B_BYTES + h * (B_BYTES * 128 / BN), &tmBl, &full[stage],
+                            kb * TC_BK, nt * BN + 128 * h);
             }
             if (++stage == TC_STAGES) {
               stage = 0;
@@ -628,13 +629,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int arow = mt * 2 * HALF + (int)rank * HALF, brow = nt * BN + (int)rank * HALF;
         for (int kb = 0; kb < nkb; ++kb) {
           if (!(ok = mbar_wait(&empty[stage], phase ^ 1, err))) break;
-          if (rank == 0) mbar_expect_tx(&full[stage], 2 * STAGE_BYTES);  // both CTAs' bytes
+          if (rank == 0)  // both CTAs' bytes
+            mbar_expect_tx(&full[stage], 2 * (b_lo_zero ? STAGE_BYTES - B_BYTES : STAGE_BYTES));
           const uint32_t fb = pair_leader_addr(&full[stage]);
           uint8_t *st = smem + stage * STAGE_BYTES;
           tma_load_2d_pair(st, &tmAh, fb, kb * TC_BK, arow);
           tma_load_2d_pair(st + A_BYTES, &tmAl, fb, kb * TC_BK, arow);
           tma_load_2d_pair(st + 2 * A_BYTES, &tmBh, fb, kb * TC_BK, brow);
-          tma_load_2d_pair(st + 2 * A_BYTES + B_BYTES, &tmBl, fb, kb * TC_BK, brow);
+          if (!b_lo_zero) tma_load_2d_pair(st + 2 * A_BYTES + B_BYTES, &tmBl, fb, kb * TC_BK, brow);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -830,9 +832,9 @@ __global__ void __launch_bounds__(TC_SPLITK_THREADS, 1)
     for (int kk = 0; kk < pre; ++kk) {  // fresh barriers: every stage is free
       const int kx = (kb0 + kk) * TC_BK;
       uint8_t *st = smem + kk * STAGE_BYTES;
-      mbar_expect_tx(&full[kk], STAGE_BYTES);
+      mbar_expect_tx(&full[kk], b_lo_zero ? STAGE_BYTES - B_BYTES : STAGE_BYTES);
       tma_load_2d(st + 2 * A_BYTES, &tmBh, &full[kk], kx, nt * BN);
-      tma_load_2d(st + 2 * A_BYTES + B_BYTES, &tmBl, &full[kk], kx, nt * BN);
+      if (!b_lo_zero) tma_load_2d(st + 2 * A_BYTES + B_BYTES, &tmBl, &full[kk], kx, nt * BN);
     }
     pdl_wait();
     for (int kk = 0; kk < pre; ++kk) {
@@ -848,11 +850,11 @@ __global__ void __launch_bounds__(TC_SPLITK_THREADS, 1)
       if (!(ok = mbar_wait(&empty[stage], phase ^ 1, err))) break;
       const int kx = (kb0 + kk) * TC_BK;
       uint8_t *st = smem + stage * STAGE_BYTES;
-      mbar_expect_tx(&full[stage], STAGE_BYTES);
+      mbar_expect_tx(&full[stage], b_lo_zero ? STAGE_BYTES - B_BYTES : STAGE_BYTES);
       tma_load_2d(st, &tmAh, &full[stage], kx, mt * TC_BM);
       tma_load_2d(st + A_BYTES, &tmAl, &full[stage], kx, mt * TC_BM);
       tma_load_2d(st + 2 * A_BYTES, &tmBh, &full[stage], kx, nt * BN);
-      tma_load_2d(st + 2 * A_BYTES + B_BYTES, &tmBl, &full[stage], kx, nt * BN);
+      if (!b_lo_zero) tma_load_2d(st + 2 * A_BYTES + B_BYTES, &tmBl, &full[stage], kx, nt * BN);
       if (++stage == STAGES) {
         stage = 0;
         phase ^= 1;

@@ -106,6 +106,9 @@ size_t int4_matmul_smem(int M, const Int4Weight &W, const MatmulOut &o);
 struct TcPlanes {
   alignas(64) unsigned char hi[128];  // CUtensorMap
   alignas(64) unsigned char lo[128];
+  // the same planes in boxes of 64 x 64 (B operands of 64-column tiles)
+  alignas(64) unsigned char hi64[128];
+  alignas(64) unsigned char lo64[128];
   int rows = 0, Kp = 0, box_rows = 0;
   const void *hi_ptr = nullptr, *lo_ptr = nullptr;
 };

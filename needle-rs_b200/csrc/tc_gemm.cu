@@ -177,13 +177,17 @@ __device__ __forceinline__ void epi_row(const TcEpi &e, int m, int n0, float *v)
 // ZCRMSNorm + RoPE for Q and K heads (attn.rs:218-235, 120-140), then either
 // bf16 hi/lo into the encoder attention planes or, for a decoder step, Q as
 // f32 and K, V appended to the self-attention caches.
-__device__ __forceinline__ void epi_qkv64(const TcEpi &e, int m, int n0, float *v) {
+// ZCRMSNorm + RoPE (attn.rs:218-235, 120-140) of the Q or K head in the 64
+// columns n0.. of row m, in place; V heads pass unchanged.  Returns the
+// plane pair (0 Q, 2 K, 4 V) and writes the head's index within it.
+__device__ __forceinline__ int qkv64_transform(const TcEpi &e, int m, int n0, float *v, int &head) {
   const MatmulOut &o = e.o;
   const int hh = n0 >> 6, H = o.heads_q, KVH = o.heads_kv;
-  int plane;
-  int64_t base;
-  const bool dec = o.epi == EPI_QKV_DEC;
-  if (hh < H + KVH) {
+  if (hh >= H + KVH) {
+    head = hh - H - KVH;
+    return 4;
+  }
+  {
     const float4 *sc = reinterpret_cast<const float4 *>(hh < H ? o.q_norm : o.k_norm);
     float ss = 0.0f;
 #pragma unroll
@@ -214,13 +218,18 @@ __device__ __forceinline__ void epi_qkv64(const TcEpi &e, int m, int n0, float *
         v[i + 32] = r;
       }
     }
-    plane = hh < H ? 0 : 2;
-    base = ((int64_t)(hh < H ? hh : hh - H) * o.slab + m) * 64;
-  } else {
-    plane = 4;
-    base = ((int64_t)(hh - H - KVH) * o.slab + m) * 64;
   }
-  if (dec) {
+  head = hh < H ? hh : hh - H;
+  return hh < H ? 0 : 2;
+}
+
+__device__ __forceinline__ void epi_qkv64(const TcEpi &e, int m, int n0, float *v) {
+  const MatmulOut &o = e.o;
+  const int hh = n0 >> 6, H = o.heads_q, KVH = o.heads_kv;
+  int head;
+  const int plane = qkv64_transform(e, m, n0, v, head);
+  const int64_t base = ((int64_t)head * o.slab + m) * 64;
+  if (o.epi == EPI_QKV_DEC) {
     float *dst;
     if (hh < H) {
       dst = o.y + (int64_t)m * o.ldy + hh * 64;
@@ -309,6 +318,80 @@ __device__ __forceinline__ void epi_tile(const TcEpi &e, int M, int N, int m, ui
     }
   }
   if (amax && m < M) atomicMax(e.o.keys + m, best);
+}
+
+// TMA maps of the six bf16 attention planes the encoder QKV epilogue writes
+// (Q hi, Q lo, K hi, K lo, V hi, V lo): each {64, rows, heads} with 32 x 64
+// boxes, 128-byte swizzle.
+struct QkvMaps {
+  CUtensorMap m[6];
+};
+
+// Plane pair (0 Q, 2 K, 4 V) and head within it of the 64 QKV columns n0..
+__device__ __forceinline__ int qkv64_plane(const MatmulOut &o, int n0, int &head) {
+  const int hh = n0 >> 6;
+  if (hh < o.heads_q) {
+    head = hh;
+    return 0;
+  }
+  if (hh < o.heads_q + o.heads_kv) {
+    head = hh - o.heads_q;
+    return 2;
+  }
+  head = hh - o.heads_q - o.heads_kv;
+  return 4;
+}
+
+// TMA output path of the encoder QKV epilogue for one warp's 32 rows (tile
+// rows m0.., TMEM lane quarter at `base`): per 64-column head, the per-row
+// norm + RoPE, then the head's 32 rows go to its bf16 hi and lo attention
+// planes as two 32 x 64 boxes, staged in the warp's 4 KB buffer with the
+// same swizzle as epi_tile_tma (one 128-byte row per lane).  Rows past M
+// are zero and clipped by the maps (their row extent is M).
+__device__ __forceinline__ void epi_tile_qkv_tma(const TcEpi &e, const QkvMaps &qm, int M, int N, int m0, int lane,
+                                                 uint32_t base, int c0, int c1, int n_base, uint8_t *stg) {
+  for (int c = c0; c < c1; c += 64) {
+    float v[64];
+    tmem_ld32(base + c, v);
+    tmem_ld32(base + c + 32, v + 32);
+    const int n0 = n_base + c;
+    if (n0 >= N) continue;  // warp-uniform
+    int head;
+    const int plane = qkv64_plane(e.o, n0, head);
+    if (m0 + lane < M) {
+      int h2;
+      qkv64_transform(e, m0 + lane, n0, v, h2);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 64; ++j) v[j] = 0.0f;
+    }
+    uint32_t hw[32], lw[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+      const float2 hf = __bfloat1622float2(h);
+      const __nv_bfloat162 lo = __floats2bfloat162_rn(v[2 * i] - hf.x, v[2 * i + 1] - hf.y);
+      hw[i] = *reinterpret_cast<const uint32_t *>(&h);
+      lw[i] = *reinterpret_cast<const uint32_t *>(&lo);
+    }
+#pragma unroll
+    for (int part = 0; part < 2; ++part) {
+      if (lane == 0) bulk_wait_read_all();  // the previous box has left `stg`
+      __syncwarp();
+      uint8_t *row = stg + lane * 128;
+      const uint32_t *w = part ? lw : hw;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        *reinterpret_cast<uint4 *>(row + ((j ^ (lane & 7)) << 4)) =
+            make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_3d(&qm.m[plane + part], stg, 0, m0, head);
+        bulk_commit();
+      }
+    }
+  }
 }
 
 // Whether the epilogue `epi` writes through the TMA output map when one is
@@ -403,8 +486,8 @@ template <int BN, int TC_STAGES>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
                    const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl,
-                   const __grid_constant__ CUtensorMap tmY, int M, int N, int Kp, TcEpi e, int *err, int b_lo_zero,
-                   int y_tma) {
+                   const __grid_constant__ CUtensorMap tmY, const __grid_constant__ QkvMaps tmQ, int M, int N, int Kp,
+                   TcEpi e, int *err, int b_lo_zero, int y_tma, int qkv_tma) {
   constexpr int A_BYTES = TC_BM * TC_BK * 2, B_BYTES = BN * TC_BK * 2;
   constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
   constexpr uint32_t IDESC = umma_idesc(TC_BM, BN);
@@ -529,7 +612,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     // ── epilogue: warpgroup `half` takes columns [half * BN/2, (half + 1) * BN/2) ──
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(TC_REG_EPILOGUE));
     const int q = warp & 3, half = (warp - 4) >> 2;
-    const bool tma_out = y_tma && epi_uses_tma(e.o.epi);
+    const bool tma_out = y_tma && epi_uses_tma(e.o.epi), qkv_out = qkv_tma && e.o.epi == EPI_QKV;
     uint8_t *stg = smem + TC_STAGES * STAGE_BYTES + 1024 + (warp - 4) * 4096;  // 1024-byte aligned
     int i = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
@@ -541,12 +624,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
       if (tma_out)
         epi_tile_tma(e, &tmY, N, m - lane, lane, base, half * (BN / 2), (half + 1) * (BN / 2), nt * BN, stg);
+      else if (qkv_out)
+        epi_tile_qkv_tma(e, tmQ, M, N, m - lane, lane, base, half * (BN / 2), (half + 1) * (BN / 2), nt * BN, stg);
       else
         epi_tile(e, M, N, m, base, half * (BN / 2), (half + 1) * (BN / 2), nt * BN);
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       mbar_arrive(&tempty[buf]);
     }
-    if (tma_out) tma_epi_drain(lane);
+    if (tma_out || qkv_out) tma_epi_drain(lane);
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
@@ -571,8 +656,8 @@ template <int STAGES>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
                         const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl,
-                        const __grid_constant__ CUtensorMap tmY, int M, int N, int Kp, TcEpi e, int *err,
-                        int b_lo_zero, int y_tma) {
+                        const __grid_constant__ CUtensorMap tmY, const __grid_constant__ QkvMaps tmQ, int M, int N,
+                        int Kp, TcEpi e, int *err, int b_lo_zero, int y_tma, int qkv_tma) {
   constexpr int HALF = 128, BN = 256;
   constexpr int A_BYTES = HALF * TC_BK * 2, B_BYTES = HALF * TC_BK * 2;
   constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
@@ -688,7 +773,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     // ── epilogue (both CTAs): warpgroup `half` takes 128 of the 256 columns ──
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(TC_REG_EPILOGUE));
     const int q = warp & 3, half = (warp - 4) >> 2;
-    const bool tma_out = y_tma && epi_uses_tma(e.o.epi);
+    const bool tma_out = y_tma && epi_uses_tma(e.o.epi), qkv_out = qkv_tma && e.o.epi == EPI_QKV;
     uint8_t *stg = smem + STAGES * STAGE_BYTES + 1024 + (warp - 4) * 4096;  // 1024-byte aligned
     int i = 0;
     for (int t = pair; t < tiles; t += npairs, ++i) {
@@ -700,13 +785,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
       if (tma_out)
         epi_tile_tma(e, &tmY, N, m - lane, lane, base, half * (BN / 2), (half + 1) * (BN / 2), nt * BN, stg);
+      else if (qkv_out)
+        epi_tile_qkv_tma(e, tmQ, M, N, m - lane, lane, base, half * (BN / 2), (half + 1) * (BN / 2), nt * BN, stg);
       else
         epi_tile(e, M, N, m, base, half * (BN / 2), (half + 1) * (BN / 2), nt * BN);
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(&tempty[buf], 0);  // the leader's barrier
     }
-    if (tma_out) tma_epi_drain(lane);
+    if (tma_out || qkv_out) tma_epi_drain(lane);
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
@@ -728,12 +815,12 @@ __device__ __forceinline__ int sk_off(int r, int c) { return r * kSkRs + c + 8 *
 
 // Epilogue of one (row, CW-column) unit of the reduced rows staged in
 // shared memory: CW = 64 for the epilogues that need whole 64-column heads,
-// 32 otherwise.  Unit u covers staged row u / (128 / CW) = tile row
-// row0 + that, columns (u % (128 / CW)) * CW.
-template <int CW>
+// 32 otherwise.  Unit u covers staged row u / (BN / CW) = tile row
+// row0 + that, columns (u % (BN / CW)) * CW of the BN-column tile.
+template <int BN, int CW>
 __device__ __forceinline__ void splitk_finish(const TcEpi &e, int M, int N, const float *stg, int row0, int mt,
                                               int nt, int u) {
-  constexpr int UPR = 128 / CW;
+  constexpr int UPR = BN / CW;
   const int rl = u / UPR, c0 = (u % UPR) * CW;
   const float4 *p4 = reinterpret_cast<const float4 *>(stg + sk_off(rl, c0));
   float v[CW];
@@ -745,7 +832,7 @@ __device__ __forceinline__ void splitk_finish(const TcEpi &e, int M, int N, cons
     v[4 * j + 2] = x.z;
     v[4 * j + 3] = x.w;
   }
-  const int m = mt * TC_BM + row0 + rl, n0 = nt * 128 + c0;
+  const int m = mt * TC_BM + row0 + rl, n0 = nt * BN + c0;
   if (m >= M || n0 >= N) return;
   if constexpr (CW == 64) {
     if (e.o.epi == EPI_KNORM)
@@ -761,29 +848,32 @@ __device__ __forceinline__ void splitk_finish(const TcEpi &e, int M, int N, cons
 }
 
 // Split-K GEMM for grids with few output tiles (decode-sized M): a cluster
-// of S CTAs shares one 128 x 128 output tile, CTA r of the cluster taking
+// of S CTAs shares one 128 x BN output tile (BN = 128, or 64 when the
+// narrower tiles still leave room for the split), CTA r of the cluster taking
 // k-blocks [r * nkb / S, (r + 1) * nkb / S).  Every SM ingests at most ~64
 // bytes per clock from L2, so a lone CTA walking all of K spends most of its
 // time waiting for operands; S CTAs load and multiply S slices at once.
 // Reduction through L2: every CTA writes its partial tile from TMEM to its
-// own 64 KB block of the caller's workspace (o.splitk_ws), one cluster
+// own block of the caller's workspace (o.splitk_ws), one cluster
 // barrier (release / acquire at cluster scope) orders those writes before
 // the reads, and CTA r sums the S partials of tile rows [r * 128 / S,
 // (r + 1) * 128 / S) in rank order and applies the epilogue.  Partial rows
 // move through shared memory so that every global access of a warp covers
-// one contiguous 512-byte row: a thread storing its own accumulator row
+// whole contiguous rows: a thread storing its own accumulator row
 // scatters each warp instruction over 32 rows and reaches a fraction of the
 // SM's bandwidth (distributed shared memory behaves the same way).
 // Under programmatic dependent launch the first weight tiles are requested
 // before the wait for the previous kernel; only the activation tiles wait.
 // Every mbarrier wait is bounded; a wait that gives up still reaches the
 // cluster barrier.
-template <int S>
+template <int S, int BN>
 __global__ void __launch_bounds__(TC_SPLITK_THREADS, 1)
     tc_gemm_splitk_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
                           const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl, int M,
                           int N, int Kp, TcEpi e, int *err, int b_lo_zero) {
-  constexpr int BN = 128, STAGES = 3;
+  constexpr int STAGES = 3;
+  static_assert(BN == 64 || BN == 128, "tile widths of the split-K kernel");
+  constexpr int LPR = BN / 4, RPI = 32 / LPR;  // lanes per 16-byte-chunked row, rows per warp instruction
   constexpr int A_BYTES = TC_BM * TC_BK * 2, B_BYTES = BN * TC_BK * 2;
   constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
   constexpr uint32_t IDESC = umma_idesc(TC_BM, BN);
@@ -799,7 +889,7 @@ __global__ void __launch_bounds__(TC_SPLITK_THREADS, 1)
   const int tile = blockIdx.x / S, num_n = (N + BN - 1) / BN;
   const int mt = tile / num_n, nt = tile - mt * num_n;
   const int kper = Kp / TC_BK / S, kb0 = (int)rank * kper;
-  float *tile_ws = e.o.splitk_ws + (size_t)tile * S * (128 * 128);
+  float *tile_ws = e.o.splitk_ws + (size_t)tile * S * (128 * BN);
   pdl_trigger();
 
   if (threadIdx.x == 0) {
@@ -914,10 +1004,11 @@ __global__ void __launch_bounds__(TC_SPLITK_THREADS, 1)
           for (int j = 0; j < 8; ++j) d4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
         }
         __syncwarp();
-        float4 *dst = reinterpret_cast<float4 *>(tile_ws + (size_t)rank * (128 * 128));
+        float4 *dst = reinterpret_cast<float4 *>(tile_ws + (size_t)rank * (128 * BN));
+        const int rl = lane / LPR, c4 = lane % LPR;
 #pragma unroll 4
-        for (int r = q * 32; r < q * 32 + 32; ++r)
-          __stcg(dst + r * 32 + lane, *reinterpret_cast<const float4 *>(stg + sk_off(r, 4 * lane)));
+        for (int r = q * 32; r < q * 32 + 32; r += RPI)
+          __stcg(dst + (r + rl) * LPR + c4, *reinterpret_cast<const float4 *>(stg + sk_off(r + rl, 4 * c4)));
       }
     }
   }
@@ -926,20 +1017,21 @@ __global__ void __launch_bounds__(TC_SPLITK_THREADS, 1)
 
   if (warp >= 4) {
     // ── reduction of tile rows [rank * ROWS, (rank + 1) * ROWS): warp q sums
-    // rows q, q + 4, ... over the S partials in rank order (lane = 4 columns,
-    // all 32 loads of a lane in flight at once), stages them, then every
-    // epilogue thread takes (row, column-block) units ──
-    constexpr int ROWS = TC_BM / S, RPW = ROWS / 4;  // RPW * S = 32 loads per lane
-    const int q = warp & 3, row0 = (int)rank * ROWS;
+    // its ROWS / 4 rows over the S partials in rank order (lane = 4 columns
+    // of a row, every load of a lane in flight at once), stages them, then
+    // every epilogue thread takes (row, column-block) units ──
+    constexpr int ROWS = TC_BM / S, RPW = ROWS / 4, IT = RPW / RPI;  // IT * S loads per lane
+    const int q = warp & 3, row0 = (int)rank * ROWS, rl = lane / LPR, c4 = lane % LPR;
     float *stg = reinterpret_cast<float *>(smem);
     const float4 *src = reinterpret_cast<const float4 *>(tile_ws);
-    float4 x[RPW][S];
+    float4 x[IT][S];
 #pragma unroll
-    for (int i = 0; i < RPW; ++i)
+    for (int i = 0; i < IT; ++i)
 #pragma unroll
-      for (int r = 0; r < S; ++r) x[i][r] = __ldcg(src + (size_t)r * (128 * 32) + (row0 + q + 4 * i) * 32 + lane);
+      for (int r = 0; r < S; ++r)
+        x[i][r] = __ldcg(src + (size_t)r * (128 * LPR) + (row0 + q * RPW + i * RPI + rl) * LPR + c4);
 #pragma unroll
-    for (int i = 0; i < RPW; ++i) {
+    for (int i = 0; i < IT; ++i) {
       float4 a = x[i][0];
 #pragma unroll
       for (int r = 1; r < S; ++r) {
@@ -948,7 +1040,7 @@ __global__ void __launch_bounds__(TC_SPLITK_THREADS, 1)
         a.z += x[i][r].z;
         a.w += x[i][r].w;
       }
-      *reinterpret_cast<float4 *>(stg + sk_off(q + 4 * i, 4 * lane)) = a;
+      *reinterpret_cast<float4 *>(stg + sk_off(q * RPW + i * RPI + rl, 4 * c4)) = a;
     }
     asm volatile("bar.sync 1, 128;" ::: "memory");  // the 4 epilogue warps
     const int epi = e.o.epi;
@@ -957,9 +1049,9 @@ __global__ void __launch_bounds__(TC_SPLITK_THREADS, 1)
 #pragma unroll 1
     for (int u = threadIdx.x - 128; u < units; u += 128) {
       if (wide)
-        splitk_finish<64>(e, M, N, stg, row0, mt, nt, u);
+        splitk_finish<BN, 64>(e, M, N, stg, row0, mt, nt, u);
       else
-        splitk_finish<32>(e, M, N, stg, row0, mt, nt, u);
+        splitk_finish<BN, 32>(e, M, N, stg, row0, mt, nt, u);
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -1072,7 +1164,7 @@ int splitk_factor(int tiles, int nkb, int sms, const int fits[3]) {
   return 1;
 }
 
-template <int S>
+template <int S, int BN>
 cudaError_t launch_splitk(const CUtensorMap *ah, const CUtensorMap *al, const CUtensorMap *bh, const CUtensorMap *bl,
                           int M, int N, int Kp, const TcEpi &e, int *err, int b_lo_zero, int tiles, cudaStream_t st) {
   cudaLaunchConfig_t cfg = {};
@@ -1093,7 +1185,7 @@ cudaError_t launch_splitk(const CUtensorMap *ah, const CUtensorMap *al, const CU
   }
   cfg.attrs = at;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, tc_gemm_splitk_kernel<S>, *ah, *al, *bh, *bl, M, N, Kp, e, err, b_lo_zero);
+  return cudaLaunchKernelEx(&cfg, tc_gemm_splitk_kernel<S, BN>, *ah, *al, *bh, *bl, M, N, Kp, e, err, b_lo_zero);
 }
 
 }  // namespace
@@ -1110,10 +1202,13 @@ cudaError_t tc_make_planes(const void *hi, const void *lo, int rows, int Kp, int
   cuuint64_t strides[1] = {(cuuint64_t)Kp * 2};
   cuuint32_t box[2] = {(cuuint32_t)TC_BK, (cuuint32_t)box_rows};
   cuuint32_t es[2] = {1, 1};
-  for (int s = 0; s < 2; ++s) {
-    CUresult r = fn(reinterpret_cast<CUtensorMap *>(s ? out.lo : out.hi), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(s ? lo : hi), dims,
-                    strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  cuuint32_t box64[2] = {(cuuint32_t)TC_BK, 64};
+  for (int s = 0; s < 4; ++s) {
+    unsigned char *m = s == 0 ? out.hi : s == 1 ? out.lo : s == 2 ? out.hi64 : out.lo64;
+    CUresult r = fn(reinterpret_cast<CUtensorMap *>(m), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                    const_cast<void *>((s & 1) ? lo : hi), dims, strides, s < 2 ? box : box64, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
   }
   out.rows = rows;
@@ -1179,6 +1274,24 @@ bool tma_map_out(const MatmulOut &o, int M, int N, CUtensorMap *map) {
   return r == CUDA_SUCCESS;
 }
 
+// TMA maps of the encoder QKV epilogue's six attention planes ({64, M, heads},
+// plane stride slab rows); false when the planes' layout does not allow them.
+bool tma_maps_qkv(const MatmulOut &o, int M, QkvMaps *qm) {
+  auto fn = encode_fn();
+  if (!fn || M <= 0 || o.slab < M) return false;
+  for (int p = 0; p < 6; ++p) {
+    if (!o.planes[p] || ((uintptr_t)o.planes[p] % 16)) return false;
+    cuuint64_t dims[3] = {64, (cuuint64_t)M, (cuuint64_t)(p < 2 ? o.heads_q : o.heads_kv)};
+    cuuint64_t strides[2] = {128, (cuuint64_t)o.slab * 128};
+    cuuint32_t box[3] = {64, 32, 1}, es[3] = {1, 1, 1};
+    if (fn(&qm->m[p], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, o.planes[p], dims, strides, box, es,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return false;
+  }
+  return true;
+}
+
 // NEEDLE_NO_TMA_STORE=1 keeps every epilogue on per-thread stores (for
 // comparisons; the residual then adds with one fused multiply-add).
 bool tma_store_disabled() {
@@ -1226,6 +1339,9 @@ cudaError_t tc_matmul(const TcPlanes &A, int M, const TcPlanes &B, int N, const 
                             tma_map_out(o, M, N, &ymap)
                         ? 1
                         : 0;
+  alignas(64) QkvMaps qmaps;
+  std::memset(&qmaps, 0, sizeof(qmaps));
+  const int qkv_tma = o.epi == EPI_QKV && !tma_store_disabled() && tma_maps_qkv(o, M, &qmaps) ? 1 : 0;
   // setmaxnreg redistributes exactly the registers of a 168-register launch;
   // any other count would leave the increase waiting for registers that
   // never come, so such a build is refused here.
@@ -1266,22 +1382,23 @@ cudaError_t tc_matmul(const TcPlanes &A, int M, const TcPlanes &B, int N, const 
     at[0].val.clusterDim.z = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<TC_PAIR_STAGES>, *ah, *al, *bh, *bl, ymap, M, N, A.Kp, e,
-                              err, b_lo_zero ? 1 : 0, y_tma);
+    return cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<TC_PAIR_STAGES>, *ah, *al, *bh, *bl, ymap, qmaps, M, N,
+                              A.Kp, e, err, b_lo_zero ? 1 : 0, y_tma, qkv_tma);
   }
   if (tiles256 >= 2 * sms)
     return launch(tc_gemm_kernel<256, 2>, dim3(sms), dim3(TC_THREADS), tc_smem_bytes(256, 2), st, *ah, *al, *bh, *bl,
-                  ymap, M, N, A.Kp, e, err, b_lo_zero ? 1 : 0, y_tma);
+                  ymap, qmaps, M, N, A.Kp, e, err, b_lo_zero ? 1 : 0, y_tma, qkv_tma);
   const int tiles = num_m * ((N + 127) / 128);
   // clusters of 2, 4 and 8 split-K CTAs this device holds at once (0: the
-  // split-K kernels are unavailable)
+  // split-K kernels are unavailable; both tile widths use the same shared
+  // memory, so they fit alike)
   static int fits[64][3];
   static bool probed[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !probed[dev]) {
-    const void *fs[3] = {(const void *)tc_gemm_splitk_kernel<2>, (const void *)tc_gemm_splitk_kernel<4>,
-                         (const void *)tc_gemm_splitk_kernel<8>};
+    const void *fs[3] = {(const void *)tc_gemm_splitk_kernel<2, 128>, (const void *)tc_gemm_splitk_kernel<4, 128>,
+                         (const void *)tc_gemm_splitk_kernel<8, 128>};
     for (int i = 0; i < 3; ++i) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(2 << i);
@@ -1300,14 +1417,32 @@ cudaError_t tc_matmul(const TcPlanes &A, int M, const TcPlanes &B, int N, const 
     cudaGetLastError();  // a failed query leaves no sticky error
     probed[dev] = true;
   }
-  int S = (o.splitk_ws && dev >= 0 && dev < 64 && !splitk_disabled()) ? splitk_factor(tiles, A.Kp / TC_BK, sms, fits[dev])
-                                                                       : 1;
-  if (tiles * S > sms || ((uintptr_t)o.splitk_ws % 16)) S = 1;  // the workspace holds one tile per SM
-  if (S == 8) return launch_splitk<8>(ah, al, bh, bl, M, N, A.Kp, e, err, b_lo_zero ? 1 : 0, tiles, st);
-  if (S == 4) return launch_splitk<4>(ah, al, bh, bl, M, N, A.Kp, e, err, b_lo_zero ? 1 : 0, tiles, st);
-  if (S == 2) return launch_splitk<2>(ah, al, bh, bl, M, N, A.Kp, e, err, b_lo_zero ? 1 : 0, tiles, st);
+  // 128 x 64 tiles when they still leave room for a split (half the partial
+  // bytes and 5/8 of the operand bytes per CTA, twice the CTAs), else 128 x 128
+  const bool can_split = o.splitk_ws && ((uintptr_t)o.splitk_ws % 16) == 0 && dev >= 0 && dev < 64 &&
+                         !splitk_disabled();
+  const int nkb = A.Kp / TC_BK, tiles64 = num_m * ((N + 63) / 64);
+  int S = 1, bn = 128;
+  if (can_split) {
+    S = splitk_factor(tiles64, nkb, sms, fits[dev]);
+    if (S > 1 && tiles64 * S <= sms) {
+      bn = 64;
+    } else {
+      S = splitk_factor(tiles, nkb, sms, fits[dev]);
+      if (tiles * S > sms) S = 1;  // the workspace holds one tile per SM
+    }
+  }
+  if (bn == 64) {
+    const auto *bh64 = reinterpret_cast<const CUtensorMap *>(B.hi64), *bl64 = reinterpret_cast<const CUtensorMap *>(B.lo64);
+    if (S == 8) return launch_splitk<8, 64>(ah, al, bh64, bl64, M, N, A.Kp, e, err, b_lo_zero ? 1 : 0, tiles64, st);
+    if (S == 4) return launch_splitk<4, 64>(ah, al, bh64, bl64, M, N, A.Kp, e, err, b_lo_zero ? 1 : 0, tiles64, st);
+    return launch_splitk<2, 64>(ah, al, bh64, bl64, M, N, A.Kp, e, err, b_lo_zero ? 1 : 0, tiles64, st);
+  }
+  if (S == 8) return launch_splitk<8, 128>(ah, al, bh, bl, M, N, A.Kp, e, err, b_lo_zero ? 1 : 0, tiles, st);
+  if (S == 4) return launch_splitk<4, 128>(ah, al, bh, bl, M, N, A.Kp, e, err, b_lo_zero ? 1 : 0, tiles, st);
+  if (S == 2) return launch_splitk<2, 128>(ah, al, bh, bl, M, N, A.Kp, e, err, b_lo_zero ? 1 : 0, tiles, st);
   return launch(tc_gemm_kernel<128, 3>, dim3(tiles < sms ? tiles : sms), dim3(TC_THREADS), tc_smem_bytes(128, 3), st,
-                *ah, *al, *bh, *bl, ymap, M, N, A.Kp, e, err, b_lo_zero ? 1 : 0, y_tma);
+                *ah, *al, *bh, *bl, ymap, qmaps, M, N, A.Kp, e, err, b_lo_zero ? 1 : 0, y_tma, qkv_tma);
 }
 
 cudaError_t init_tc_kernels() {
@@ -1319,8 +1454,9 @@ cudaError_t init_tc_kernels() {
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(tc_gemm_pair_kernel<TC_PAIR_STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)tc_smem_pair_bytes());
-  for (const void *f : {(const void *)tc_gemm_splitk_kernel<2>, (const void *)tc_gemm_splitk_kernel<4>,
-                        (const void *)tc_gemm_splitk_kernel<8>})
+  for (const void *f : {(const void *)tc_gemm_splitk_kernel<2, 128>, (const void *)tc_gemm_splitk_kernel<4, 128>,
+                        (const void *)tc_gemm_splitk_kernel<8, 128>, (const void *)tc_gemm_splitk_kernel<2, 64>,
+                        (const void *)tc_gemm_splitk_kernel<4, 64>, (const void *)tc_gemm_splitk_kernel<8, 64>})
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc_smem_splitk_bytes());
   return e;

@@ -895,8 +895,8 @@ bool Batch::prefill(std::string &err) {
         if (!tbegin(TIME_ENCODER_ATTENTION, false, ev, err)) return false;
         if (tc_attn_)
           NDL_LK(encoder_attention_tc(attn_planes_, ch.rel_off, ch.items, ch.n_items, pq ? nullptr : patt_,
-                                      pq ? tc_hi_ : nullptr, pq ? tc_lo_ : nullptr, pq ? pq->Kp : 0, m.ad,
-                                      m_->kerr, st));
+                                      pq ? tc_hi_ : nullptr, pq ? tc_lo_ : nullptr, pq ? pq->Kp : 0, rows,
+                                      m.ad, m_->kerr, st));
         else
           NDL_LK(encoder_attention(pqkv_, ch.rel_off, nr, ch.tmax, patt_, m.ad, st));
         double Tq = 0.0;  // sum of T^2 over the chunk's requests

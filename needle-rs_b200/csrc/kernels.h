@@ -159,10 +159,13 @@ cudaError_t qkv_post(const float *qkv, int rows, const int32_t *pos, const float
 // Bidirectional attention over the planes: items = int4 (request, 128-row
 // query tile, Q head, 0) against chunk-relative seq_off.  The result goes to
 // bf16 hi/lo planes [rows][ldp] (the O projection's input) when out_hi is
-// set, else to f32 out [rows][H*64].
+// set (out_rows rows; warps whose 32 rows lie inside one request write
+// through TMA boxes), else to f32 out [rows][H*64].
 cudaError_t encoder_attention_tc(const AttnPlanes &p, const int64_t *seq_off, const void *items, int n_items,
-                                 float *out, void *out_hi, void *out_lo, int ldp, AttnDims a, int *err,
+                                 float *out, void *out_hi, void *out_lo, int ldp, int out_rows, AttnDims a, int *err,
                                  cudaStream_t st);
+// NEEDLE_NO_TMA_STORE=1 in the environment: every epilogue stores per thread.
+bool tma_store_disabled();
 cudaError_t init_tc_attn_kernels();
 
 // Device packing / unpacking (quant.rs:63-155), bit-exact with the reference.

@@ -45,6 +45,8 @@
 #include <cuda.h>
 #include <cuda_bf16.h>
 
+#include <cstring>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "tc_common.cuh"
@@ -65,7 +67,8 @@ constexpr int AT_TILE = AT_BM * AT_HD * 2;  // one 128 x 64 bf16 plane tile: 16 
 constexpr int AT_Q = 0;                      // slot a hi, lo; slot b hi, lo
 constexpr int AT_KV = 4 * AT_TILE;           // 2 stages x (K hi, K lo, V hi, V lo)
 constexpr int AT_STAGE = 4 * AT_TILE;
-constexpr int AT_BAR = AT_KV + 2 * AT_STAGE;
+constexpr int AT_STG = AT_KV + 2 * AT_STAGE;  // 8 x 4 KB output staging, one per softmax warp
+constexpr int AT_BAR = AT_STG + 8 * 4096;
 constexpr size_t AT_SMEM = 1024 + AT_BAR + 256;
 constexpr float AT_RESCALE = 8.0f;  // log2 headroom before a row's reference point m is raised
 static_assert(AT_SMEM <= 232448, "exceeds the 227 KB of dynamic shared memory per block");
@@ -208,15 +211,16 @@ __device__ __forceinline__ void split2(float p0, float p1, uint32_t &hi, uint32_
 
 // P = 2^(s*c - m) for this thread's row of a 128-key tile held in sr,
 // written over the row's S columns 32 keys at a time (hi in a chunk's first
-// 16 columns, lo in the last 16).  Returns the row sum.  MASK: keys at kvalid
-// and beyond get probability 0.
+// 16 columns, lo in the last 16), for the first nch chunks.  Returns the row
+// sum.  MASK: keys at kvalid and beyond get probability 0.
 template <bool MASK>
-__device__ __forceinline__ float p_row(const uint32_t *sr, float c, float m, int kvalid, uint32_t tS) {
+__device__ __forceinline__ float p_row(const uint32_t *sr, float c, float m, int kvalid, int nch, uint32_t tS) {
   // even and odd keys summed in the two lanes of ps, in key order
   uint64_t ps = f2pack(0.0f, 0.0f);
   const uint64_t cc = f2pack(c, c), nm = f2pack(-m, -m);
 #pragma unroll
   for (int ch = 0; ch < 4; ++ch) {
+    if (ch >= nch) break;  // keys the PV MMAs of this tile do not read
     uint32_t hw[16], lw[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
@@ -266,8 +270,10 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     enc_attn_tc_kernel(const __grid_constant__ CUtensorMap tmQh, const __grid_constant__ CUtensorMap tmQl,
                        const __grid_constant__ CUtensorMap tmKh, const __grid_constant__ CUtensorMap tmKl,
                        const __grid_constant__ CUtensorMap tmVh, const __grid_constant__ CUtensorMap tmVl,
+                       const __grid_constant__ CUtensorMap tmOh, const __grid_constant__ CUtensorMap tmOl,
                        const int64_t *__restrict__ seq_off, const int4 *__restrict__ items, int n_items, int slab,
-                       float *out, __nv_bfloat16 *out_hi, __nv_bfloat16 *out_lo, int ldp, AttnDims a, int *err) {
+                       float *out, __nv_bfloat16 *out_hi, __nv_bfloat16 *out_lo, int ldp, int o_tma, AttnDims a,
+                       int *err) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *sm = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t *bars = (uint64_t *)(sm + AT_BAR);
@@ -352,7 +358,6 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       }
     } else if (warp == 1) {
       if (lane == 0) {  // ── MMA issuer ──
-        constexpr uint32_t ID_S = umma_idesc(AT_BM, AT_BN);
         constexpr uint32_t ID_PV2 = umma_idesc(AT_BM, 2 * AT_HD, true);  // P_hi x [V_hi | V_lo]
         constexpr uint32_t ID_PV = umma_idesc(AT_BM, AT_HD, true);       // P_lo x V_hi
         // per-slot phase counters (scalars: x is 0 or 1)
@@ -360,7 +365,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         uint32_t items0 = 0, items1 = 0;
         // S_x = Q_x K^T from stage st, once the slot's previous PV (which reads
         // P over S_x) has completed.
-        auto issue_s = [&](int x, int st) -> bool {
+        auto issue_s = [&](int x, int st, int ns) -> bool {
           const uint32_t waited = x ? pv_waited1 : pv_waited0;
           if ((x ? pv_issued1 : pv_issued0) > waited) {
             if (!mbar_wait(&pv_done[x], waited & 1, err)) return false;
@@ -369,22 +374,23 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
           uint8_t *kvs = sm + AT_KV + st * AT_STAGE;
           const uint32_t d = tmem + (uint32_t)(x * AT_BN);
+          const uint32_t id_s = umma_idesc(AT_BM, ns);  // the tile's first ns keys (a multiple of 16)
   #pragma unroll 1
           for (int ks = 0; ks < AT_HD / 16; ++ks) {
             const uint64_t adv = (uint64_t)((ks * 32) >> 4);
             const uint64_t qh = umma_desc(sm + AT_Q + 2 * x * AT_TILE) + adv;
             const uint64_t ql = umma_desc(sm + AT_Q + (2 * x + 1) * AT_TILE) + adv;
             const uint64_t kh = umma_desc(kvs) + adv, kl = umma_desc(kvs + AT_TILE) + adv;
-            umma_bf16(d, qh, kh, ID_S, ks ? 1u : 0u);
-            umma_bf16(d, qh, kl, ID_S, 1u);
-            umma_bf16(d, ql, kh, ID_S, 1u);
+            umma_bf16(d, qh, kh, id_s, ks ? 1u : 0u);
+            umma_bf16(d, qh, kl, id_s, 1u);
+            umma_bf16(d, ql, kh, id_s, 1u);
           }
           umma_commit(&s_full[x]);
           return true;
         };
         // O_x (+)= P_x V from stage st, once the softmax has written P_x (and,
         // on an item's first tile, the previous item's O_x has been read out).
-        auto issue_pv = [&](int x, int st, int j, bool last) -> bool {
+        auto issue_pv = [&](int x, int st, int j, bool last, int nks) -> bool {
           const uint32_t seen = x ? p_seen1 : p_seen0;
           if (!mbar_wait(&p_full[x], seen & 1, err)) return false;
           if (x) ++p_seen1; else ++p_seen0;
@@ -395,7 +401,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
           const uint32_t d = tmem + 256u + (uint32_t)(x * 2 * AT_HD);
           const uint32_t pbase = tmem + (uint32_t)(x * AT_BN);
   #pragma unroll 1
-          for (int ks = 0; ks < AT_BN / 16; ++ks) {
+          for (int ks = 0; ks < nks; ++ks) {
             // keys 16ks..16ks+15: chunk ks/2, hi at 32(ks/2) + 8(ks%2), lo 16 columns on
             const uint32_t ph = pbase + 32u * (ks >> 1) + 8u * (ks & 1), pl = ph + 16u;
             // V_lo sits one plane tile (AT_TILE bytes) after V_hi: the second MN atom
@@ -417,24 +423,28 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
           const AttnItem item = decode_item(items[w]);
           const int T = (int)(seq_off[item.req + 1] - seq_off[item.req]);
           const int nk = (T + AT_BN - 1) / AT_BN;
+          // keys of tile j that belong to the request, as S columns (a
+          // multiple of 16) and as 16-key PV steps
+          auto tile_ns = [&](int j) { return min(AT_BN, (T - j * AT_BN + 15) & ~15); };
           if (!(ok = mbar_wait(q_full, it & 1, err))) break;
           if (!(ok = mbar_wait(&kv_full[stage], phase, err))) break;
-          if (!(ok = issue_s(0, stage))) break;
-          if (item.two && !(ok = issue_s(1, stage))) break;
+          if (!(ok = issue_s(0, stage, tile_ns(0)))) break;
+          if (item.two && !(ok = issue_s(1, stage, tile_ns(0)))) break;
           if (nk == 1) umma_commit(q_empty);  // every S of the item issued
           for (int j = 0; j < nk && ok; ++j) {
             const int cur = stage;
             const int nxt = stage ^ 1;
             const uint32_t nph = stage == 1 ? phase ^ 1 : phase;
             const bool more = j + 1 < nk, last = j + 1 == nk;
-            if (!(ok = issue_pv(0, cur, j, last))) break;
+            const int nks = tile_ns(j) >> 4, ns1 = more ? tile_ns(j + 1) : 0;
+            if (!(ok = issue_pv(0, cur, j, last, nks))) break;
             if (more) {
               if (!(ok = mbar_wait(&kv_full[nxt], nph, err))) break;
-              if (!(ok = issue_s(0, nxt))) break;
+              if (!(ok = issue_s(0, nxt, ns1))) break;
             }
             if (item.two) {
-              if (!(ok = issue_pv(1, cur, j, last))) break;
-              if (more && !(ok = issue_s(1, nxt))) break;
+              if (!(ok = issue_pv(1, cur, j, last, nks))) break;
+              if (more && !(ok = issue_s(1, nxt, ns1))) break;
             }
             if (j + 2 == nk) umma_commit(q_empty);
             umma_commit(&kv_empty[cur]);  // every S and PV reading K_j / V_j issued before this commit
@@ -469,6 +479,10 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         ++s_seen;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const int kvalid = T - j * AT_BN;  // keys of this tile that belong to the request (>= 1)
+        // 32-key chunks the PV MMAs read (warp-uniform).  All 128 columns
+        // are loaded: those past the S MMA's columns hold stale values that
+        // the mask excludes.
+        const int nch = kvalid >= AT_BN ? 4 : (kvalid + 31) >> 5;
         uint32_t sr[128];
 #pragma unroll
         for (int q = 0; q < 4; ++q) tmem_ld32_raw(tS + 32 * q, sr + 32 * q);
@@ -490,7 +504,8 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
           corr = ex2(m - mt);  // 0 on the first tile (m = -inf)
           m = mt;
         }
-        const float psum = kvalid >= AT_BN ? p_row<false>(sr, c, m, kvalid, tS) : p_row<true>(sr, c, m, kvalid, tS);
+        const float psum =
+            kvalid >= AT_BN ? p_row<false>(sr, c, m, kvalid, 4, tS) : p_row<true>(sr, c, m, kvalid, nch, tS);
         l = l * corr + psum;
         // O_x *= corr (PV_x(j-1) completed before S_x(j) was issued).  The
         // tcgen05 loads and stores are warp-collective, so the whole warp
@@ -529,7 +544,36 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       for (int e = 0; e < 64; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) + __uint_as_float(ov[64 + e]));
       const int qt = x ? item.qt[1] : item.qt[0], head = x ? item.head[1] : item.head[0];
       const int qr = qt * AT_BM + r;
-      if (qr < T) {
+      const int row0 = qt * AT_BM + quarter * 32;  // the warp's first query row
+      if (o_tma && row0 + 32 <= T) {
+        // all 32 rows of the warp belong to the request: the hi and lo
+        // planes leave as two 32-row x 64-column TMA boxes, staged in the
+        // warp's 4 KB buffer with the 128-byte swizzle (16-byte chunk j of
+        // row r at r * 128 + ((j ^ (r & 7)) << 4))
+        const float inv = 1.0f / l;
+        uint8_t *stg = sm + AT_STG + (warp - 4) * 4096, *srow = stg + lane * 128;
+#pragma unroll
+        for (int part = 0; part < 2; ++part) {
+          if (lane == 0) bulk_wait_read_all();  // the warp's previous box has left stg
+          __syncwarp();
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            uint32_t hw[4], lw[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              split2(__uint_as_float(ov[8 * e + 2 * q]) * inv, __uint_as_float(ov[8 * e + 2 * q + 1]) * inv, hw[q],
+                     lw[q]);
+            *reinterpret_cast<uint4 *>(srow + ((e ^ (lane & 7)) << 4)) =
+                part ? make_uint4(lw[0], lw[1], lw[2], lw[3]) : make_uint4(hw[0], hw[1], hw[2], hw[3]);
+          }
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(part ? &tmOl : &tmOh, stg, head * AT_HD, (int)off + row0);
+            bulk_commit();
+          }
+        }
+      } else if (qr < T) {
         const float inv = 1.0f / l;
         if (out_hi) {  // bf16 hi/lo planes of the O projection's input
           const int64_t base = (off + qr) * (int64_t)ldp + head * AT_HD;
@@ -554,6 +598,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       }
     }
   }
+  if (warp >= 4 && o_tma && lane == 0) bulk_wait_all();  // this warp's output boxes written
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   if (warp == 1) {
@@ -586,7 +631,7 @@ cudaError_t qkv_post(const float *qkv, int rows, const int32_t *pos, const float
 }
 
 cudaError_t encoder_attention_tc(const AttnPlanes &p, const int64_t *seq_off, const void *items, int n_items,
-                                 float *out, void *out_hi, void *out_lo, int ldp, AttnDims a, int *err,
+                                 float *out, void *out_hi, void *out_lo, int ldp, int out_rows, AttnDims a, int *err,
                                  cudaStream_t st) {
   if (n_items <= 0) return cudaSuccess;
   if (a.HD != 64 || (a.H % a.KVH)) return cudaErrorInvalidValue;
@@ -607,10 +652,18 @@ cudaError_t encoder_attention_tc(const AttnPlanes &p, const int64_t *seq_off, co
     regs = fa.numRegs;
   }
   if (regs != AT_REG_LAUNCH) return cudaErrorInvalidKernelImage;
+  // output planes as TMA boxes of 32 rows x 64 columns, when they allow it
+  alignas(64) TcPlanes om;
+  std::memset(om.hi, 0, sizeof(om.hi));
+  std::memset(om.lo, 0, sizeof(om.lo));
+  const int o_tma = out_hi && out_rows > 0 && (ldp % 64) == 0 && !tma_store_disabled() &&
+                            tc_make_planes(out_hi, out_lo, out_rows, ldp, 32, om) == cudaSuccess
+                        ? 1
+                        : 0;
   auto M = [](const unsigned char *m) { return *reinterpret_cast<const CUtensorMap *>(m); };
-  enc_attn_tc_kernel<<<grid, AT_THREADS, AT_SMEM, st>>>(M(p.q.hi), M(p.q.lo), M(p.k.hi), M(p.k.lo), M(p.v.hi),
-                                                        M(p.v.lo), seq_off, (const int4 *)items, n_items, p.slab, out,
-                                                        (__nv_bfloat16 *)out_hi, (__nv_bfloat16 *)out_lo, ldp, a, err);
+  enc_attn_tc_kernel<<<grid, AT_THREADS, AT_SMEM, st>>>(
+      M(p.q.hi), M(p.q.lo), M(p.k.hi), M(p.k.lo), M(p.v.hi), M(p.v.lo), M(om.hi), M(om.lo), seq_off,
+      (const int4 *)items, n_items, p.slab, out, (__nv_bfloat16 *)out_hi, (__nv_bfloat16 *)out_lo, ldp, o_tma, a, err);
   return cudaGetLastError();
 }
 

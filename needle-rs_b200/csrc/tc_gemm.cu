@@ -1292,6 +1292,8 @@ bool tma_maps_qkv(const MatmulOut &o, int M, QkvMaps *qm) {
   return true;
 }
 
+}  // namespace
+
 // NEEDLE_NO_TMA_STORE=1 keeps every epilogue on per-thread stores (for
 // comparisons; the residual then adds with one fused multiply-add).
 bool tma_store_disabled() {
@@ -1301,7 +1303,6 @@ bool tma_store_disabled() {
   }();
   return off;
 }
-}  // namespace
 
 cudaError_t tc_matmul(const TcPlanes &A, int M, const TcPlanes &B, int N, const MatmulOut &o, int *err,
                       cudaStream_t st, bool b_lo_zero) {

@@ -15,15 +15,11 @@
 // warp 0 issues the TMA loads (the item's Q tiles, then K/V tiles of 128
 // keys through a 2-stage ring), warp 1 allocates TMEM and issues the MMAs
 // (the whole warp runs the issue loop and one elected lane issues each
-// tcgen05 instruction; warps 2-3 idle), and warpgroups 1 and 2 run the
-// softmax, slot a then slot b of every key tile: the two threads of a query
-// row (warps w and w + 4 read the same TMEM lanes) take its keys 0-63 and
-// 64-127, exchange their partial maxima through shared memory under a
-// named barrier of the warp pair, and keep partial row sums that are added
-// once per item.  The producer warpgroup hands its registers to them with
-// setmaxnreg.  TMEM: S_a
-// and S_b (128 columns each; P is written back over its own S), O_a and O_b
-// (128 columns each).  Per key tile j and slot x:
+// tcgen05 instruction; warps 2-3 idle), and warpgroups 1 / 2 run the
+// softmax of slot a / slot b (thread = one query row, all 128 keys of a tile
+// held in registers; the producer warpgroup hands its registers to them with
+// setmaxnreg).  TMEM: S_a and S_b (128 columns each; P is written back over
+// its own S), O_a and O_b (128 columns each).  Per key tile j and slot x:
 //   S_x = Q_x K_j^T      tcgen05.mma M128 N128 K16, A and B K-major in smem
 //   p = 2^(s*c - m)      c = hd^-0.5 * log2(e); m is raised only when a row's
 //                        maximum passes it by more than 8, so p <= 256; p and
@@ -41,13 +37,11 @@
 //                        when the row is written out.  O stays in TMEM and the
 //                        softmax warps rescale it there when m moves
 // The MMA warp issues S_a(0), S_b(0), then per tile PV_a(j), S_a(j+1),
-// PV_b(j), S_b(j+1): while the softmax warps work on one slot, the tensor
-// core works on the other.  A tile's MMAs and softmax cover only its keys
-// that belong to the request (S columns and PV steps in multiples of 16).  Each product is the 3-term split hi*hi + hi*lo +
+// PV_b(j), S_b(j+1): while one slot's warps run the softmax, the tensor core
+// works on the other slot.  Each product is the 3-term split hi*hi + hi*lo +
 // lo*hi (about 1e-6 relative), so the f32 reference is matched within the
 // logit tolerance.  Keys past the request's end get probability 0; query
-// rows past it are computed on neighbouring rows and never stored.  Output
-// rows of a warp pair that all belong to the request leave as TMA boxes.  Every TMA
+// rows past it are computed on neighbouring rows and never stored.  Every TMA
 // load fills only its own CTA's shared memory; every wait is bounded (error
 // flag, then unwind).
 #include <cuda.h>
@@ -66,18 +60,17 @@ using namespace tc;
 
 constexpr int AT_BM = 128, AT_BN = 128, AT_HD = 64, AT_THREADS = 384;
 // Registers a thread: launched at 168 (65,536 / 384, rounded down to 8),
-// then the producer warpgroup drops to 72 and the two softmax warpgroups
-// rise to 216: 128 x 72 + 256 x 216 = 384 x 168 = 64,512.
-constexpr int AT_REG_LAUNCH = 168, AT_REG_PRODUCER = 72, AT_REG_SOFTMAX = 216;
+// then the producer warpgroup drops to 56 and the two softmax warpgroups
+// rise to 224: 128 x 56 + 256 x 224 = 384 x 168 = 64,512.
+constexpr int AT_REG_LAUNCH = 168, AT_REG_PRODUCER = 56, AT_REG_SOFTMAX = 224;
 static_assert(128 * AT_REG_PRODUCER + 256 * AT_REG_SOFTMAX == AT_THREADS * AT_REG_LAUNCH,
               "the register split must add up to the launch's registers");
 constexpr int AT_TILE = AT_BM * AT_HD * 2;  // one 128 x 64 bf16 plane tile: 16 KB
 constexpr int AT_Q = 0;                      // slot a hi, lo; slot b hi, lo
 constexpr int AT_KV = 4 * AT_TILE;           // 2 stages x (K hi, K lo, V hi, V lo)
 constexpr int AT_STAGE = 4 * AT_TILE;
-constexpr int AT_STG = AT_KV + 2 * AT_STAGE;  // 4 x 8 KB output staging (hi, lo), one per warp pair
-constexpr int AT_XCH = AT_STG + 4 * 8192;      // 2 x 128 floats: per-row values exchanged within a pair
-constexpr int AT_BAR = AT_XCH + 2 * 128 * 4;
+constexpr int AT_STG = AT_KV + 2 * AT_STAGE;  // 8 x 4 KB output staging, one per softmax warp
+constexpr int AT_BAR = AT_STG + 8 * 4096;
 constexpr size_t AT_SMEM = 1024 + AT_BAR + 256;
 constexpr float AT_RESCALE = 8.0f;  // log2 headroom before a row's reference point m is raised
 static_assert(AT_SMEM <= 232448, "exceeds the 227 KB of dynamic shared memory per block");
@@ -207,18 +200,17 @@ __device__ __forceinline__ void split2(float p0, float p1, uint32_t &hi, uint32_
   lo = *reinterpret_cast<uint32_t *>(&l2);
 }
 
-// P = 2^(s*c - m) for this thread's 64 keys of a row (its half of a
-// 128-key tile) held in sr, written over the same S columns 32 keys at a
-// time (hi in a chunk's first 16 columns, lo in the last 16), for the first
-// nch chunks.  Returns the sum of the half's probabilities.  MASK: keys at
-// kvalid and beyond (counted within the half) get probability 0.
+// P = 2^(s*c - m) for this thread's row of a 128-key tile held in sr,
+// written over the row's S columns 32 keys at a time (hi in a chunk's first
+// 16 columns, lo in the last 16), for the first nch chunks.  Returns the row
+// sum.  MASK: keys at kvalid and beyond get probability 0.
 template <bool MASK>
-__device__ __forceinline__ float p_half(const uint32_t *sr, float c, float m, int kvalid, int nch, uint32_t tS) {
+__device__ __forceinline__ float p_row(const uint32_t *sr, float c, float m, int kvalid, int nch, uint32_t tS) {
   // even and odd keys summed in the two lanes of ps, in key order
   uint64_t ps = f2pack(0.0f, 0.0f);
   const uint64_t cc = f2pack(c, c), nm = f2pack(-m, -m);
 #pragma unroll
-  for (int ch = 0; ch < 2; ++ch) {
+  for (int ch = 0; ch < 4; ++ch) {
     if (ch >= nch) break;  // keys the PV MMAs of this tile do not read
     uint32_t hw[16], lw[16];
 #pragma unroll
@@ -247,22 +239,6 @@ __device__ __forceinline__ float p_half(const uint32_t *sr, float c, float m, in
   float s0, s1;
   f2unpack(ps, s0, s1);
   return s0 + s1;
-}
-
-// Named barrier of the two softmax warps that share a TMEM lane quarter
-// (64 threads), and the same barrier returning whether v held in all of them.
-__device__ __forceinline__ void pair_bar(int id) { asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory"); }
-__device__ __forceinline__ bool pair_all(int id, bool v) {
-  uint32_t out;
-  asm volatile(
-      "{\n\t.reg .pred q, p;\n\t"
-      "setp.ne.u32 q, %1, 0;\n\t"
-      "bar.red.and.pred p, %2, 64, q;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(out)
-      : "r"((uint32_t)v), "r"(id)
-      : "memory");
-  return out != 0;
 }
 
 struct AttnItem {
@@ -296,10 +272,10 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
   uint64_t *kv_full = bars + 2;   // [stage]
   uint64_t *kv_empty = bars + 4;  // [stage]
   uint64_t *s_full = bars + 6;    // [slot] S_x computed
-  uint64_t *p_full = bars + 8;    // [slot] P_x written and O_x rescaled (256 arrivals)
+  uint64_t *p_full = bars + 8;    // [slot] P_x written and O_x rescaled (128 arrivals)
   uint64_t *pv_done = bars + 10;  // [slot] PV_x complete: S_x may be overwritten
   uint64_t *o_done = bars + 12;   // [slot] the item's last PV_x complete
-  uint64_t *o_free = bars + 14;   // [slot] O_x read by the epilogue (256 arrivals)
+  uint64_t *o_free = bars + 14;   // [slot] O_x read by the epilogue (128 arrivals)
   uint32_t *tmem_slot = (uint32_t *)(bars + 16);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -310,10 +286,10 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
       mbar_init(&s_full[s], 1);
-      mbar_init(&p_full[s], 256);
+      mbar_init(&p_full[s], 128);
       mbar_init(&pv_done[s], 1);
       mbar_init(&o_done[s], 1);
-      mbar_init(&o_free[s], 256);
+      mbar_init(&o_free[s], 128);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -478,161 +454,142 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         }
       }
     }
-  } else {  // ── softmax: warps 4-7 take keys 0-63 of each row, warps 8-11 keys 64-127; slot a, then slot b ──
+  } else {  // ── softmax: warps 4-7 slot a, warps 8-11 slot b ──
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(AT_REG_SOFTMAX));
-    const int quarter = warp & 3, h = (warp - 4) >> 2;
+    const int quarter = warp & 3, x = (warp - 4) >> 2;
     const int r = quarter * 32 + lane;  // TMEM lane = query row of the tile
-    const int bar_id = 1 + quarter;     // named barrier of the warp pair sharing these rows
     const uint32_t lanes = (uint32_t)(quarter * 32) << 16;
-    float *xch = reinterpret_cast<float *>(sm + AT_XCH);  // [half][row]: a row's two partial values
-    const float c = a.scale * 1.4426950408889634f;       // hd^-0.5 * log2(e)
-    uint32_t s_seen[2] = {0, 0}, o_seen[2] = {0, 0};
-    bool ok = true;
-    for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x) {
+    const uint32_t tS = tmem + lanes + (uint32_t)(x * AT_BN), tO = tmem + lanes + 256u + (uint32_t)(x * 2 * AT_HD);
+    const float c = a.scale * 1.4426950408889634f;  // hd^-0.5 * log2(e)
+    uint32_t s_seen = 0, o_seen = 0;
+    for (int w = blockIdx.x; w < n_items; w += gridDim.x) {
       const AttnItem item = decode_item(items[w]);
-      const int nslot = item.two ? 2 : 1;
+      if (x == 1 && !item.two) continue;
       const int64_t off = seq_off[item.req];
       const int T = (int)(seq_off[item.req + 1] - off);
       const int nk = (T + AT_BN - 1) / AT_BN;
-      float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.0f, 0.0f};
-      for (int j = 0; j < nk && ok; ++j) {
-        const int kvalid = T - j * AT_BN;           // keys of this tile that belong to the request (>= 1)
-        const int kown = min(64, kvalid - 64 * h);  // of this thread's 64 keys (<= 0: none)
-        // this half's 32-key chunks that the PV MMAs read (warp-uniform)
-        const int nch = kvalid >= AT_BN ? 2 : max(0, min(2, ((kvalid + 31) >> 5) - 2 * h));
-        for (int x = 0; x < nslot; ++x) {
-          // both warps of the pair leave together on a timeout; the barrier
-          // also orders this exchange after the partner's last read of xch
-          if (!(ok = pair_all(bar_id, warp_wait(&s_full[x], s_seen[x] & 1, err)))) break;
-          ++s_seen[x];
-          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          const uint32_t tS = tmem + lanes + (uint32_t)(x * AT_BN + 64 * h);
-          // all 64 columns are loaded: those past the S MMA's columns hold
-          // stale values that the mask excludes
-          uint32_t sr[64];
-          tmem_ld32_raw(tS, sr);
-          tmem_ld32_raw(tS + 32, sr + 32);
-          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-          float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-          if (kown >= 64) {
+      float m = -INFINITY, l = 0.0f;
+      bool ok = true;
+      for (int j = 0; j < nk; ++j) {
+        if (!(ok = warp_wait(&s_full[x], s_seen & 1, err))) break;
+        ++s_seen;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const int kvalid = T - j * AT_BN;  // keys of this tile that belong to the request (>= 1)
+        // 32-key chunks the PV MMAs read (warp-uniform).  All 128 columns
+        // are loaded: those past the S MMA's columns hold stale values that
+        // the mask excludes.
+        const int nch = kvalid >= AT_BN ? 4 : (kvalid + 31) >> 5;
+        uint32_t sr[128];
 #pragma unroll
-            for (int e = 0; e < 64; e += 2)
-              mx[(e >> 1) & 3] = fmax3(mx[(e >> 1) & 3], __uint_as_float(sr[e]), __uint_as_float(sr[e + 1]));
-          } else {
+        for (int q = 0; q < 4; ++q) tmem_ld32_raw(tS + 32 * q, sr + 32 * q);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        if (kvalid >= AT_BN) {
 #pragma unroll
-            for (int e = 0; e < 64; ++e)
-              if (e < kown) mx[e & 3] = fmaxf(mx[e & 3], __uint_as_float(sr[e]));
-          }
-          const float mloc = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
-          xch[h * 128 + r] = mloc;
-          pair_bar(bar_id);
-          const float mt = fmaxf(mloc, xch[(h ^ 1) * 128 + r]) * c;  // the row's maximum, same in both halves
-          float corr = 1.0f;
-          const bool resc = j == 0 || mt > m[x] + AT_RESCALE;
-          if (resc) {
-            corr = ex2(m[x] - mt);  // 0 on the first tile (m = -inf)
-            m[x] = mt;
-          }
-          const float psum =
-              kown >= 64 ? p_half<false>(sr, c, m[x], 64, 2, tS) : p_half<true>(sr, c, m[x], kown, nch, tS);
-          l[x] = l[x] * corr + psum;
-          // O_x *= corr on this thread's 64 of the row's 128 O columns
-          // (PV_x(j-1) completed before S_x(j) was issued).  The tcgen05
-          // loads and stores are warp-collective, so the whole warp takes
-          // this branch when any of its rows moved m (corr = 1 elsewhere).
-          if (__any_sync(0xffffffffu, resc && j > 0)) {
-            const uint32_t tO = tmem + lanes + 256u + (uint32_t)(x * 2 * AT_HD + 64 * h);
-            uint32_t ov[64];
-            tmem_ld32_raw(tO, ov);
-            tmem_ld32_raw(tO + 32, ov + 32);
-            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-            const uint64_t cr2 = f2pack(corr, corr);
+          for (int e = 0; e < 128; e += 2)
+            mx[(e >> 1) & 3] = fmax3(mx[(e >> 1) & 3], __uint_as_float(sr[e]), __uint_as_float(sr[e + 1]));
+        } else {
 #pragma unroll
-            for (int e = 0; e < 64; e += 2) {
-              float a0, a1;
-              f2unpack(fmul2(f2pack(__uint_as_float(ov[e]), __uint_as_float(ov[e + 1])), cr2), a0, a1);
-              ov[e] = __float_as_uint(a0);
-              ov[e + 1] = __float_as_uint(a1);
-            }
-            tmem_st32(tO, ov);
-            tmem_st32(tO + 32, ov + 32);
-          }
-          asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-          asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-          mbar_arrive(&p_full[x]);
+          for (int e = 0; e < 128; ++e)
+            if (e < kvalid) mx[e & 3] = fmaxf(mx[e & 3], __uint_as_float(sr[e]));
         }
+        const float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * c;
+        float corr = 1.0f;
+        const bool resc = j == 0 || mt > m + AT_RESCALE;
+        if (resc) {
+          corr = ex2(m - mt);  // 0 on the first tile (m = -inf)
+          m = mt;
+        }
+        const float psum =
+            kvalid >= AT_BN ? p_row<false>(sr, c, m, kvalid, 4, tS) : p_row<true>(sr, c, m, kvalid, nch, tS);
+        l = l * corr + psum;
+        // O_x *= corr (PV_x(j-1) completed before S_x(j) was issued).  The
+        // tcgen05 loads and stores are warp-collective, so the whole warp
+        // takes this branch when any of its rows moved m (corr = 1 elsewhere).
+        if (__any_sync(0xffffffffu, resc && j > 0)) {
+          uint32_t ov[128];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) tmem_ld32_raw(tO + 32 * q, ov + 32 * q);
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+          const uint64_t cr2 = f2pack(corr, corr);
+#pragma unroll
+          for (int e = 0; e < 128; e += 2) {
+            float a0, a1;
+            f2unpack(fmul2(f2pack(__uint_as_float(ov[e]), __uint_as_float(ov[e + 1])), cr2), a0, a1);
+            ov[e] = __float_as_uint(a0);
+            ov[e + 1] = __float_as_uint(a1);
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) tmem_st32(tO + 32 * q, ov + 32 * q);
+        }
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        mbar_arrive(&p_full[x]);
       }
       if (!ok) break;
-      for (int x = 0; x < nslot; ++x) {
-        if (!(ok = pair_all(bar_id, warp_wait(&o_done[x], o_seen[x] & 1, err)))) break;  // the item's last PV_x
-        ++o_seen[x];
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        // output dims 32h..32h+31: O columns 32h.. (P V_hi + P_lo V_hi) and
-        // 64 + 32h.. (P_hi V_lo)
-        const uint32_t tO = tmem + lanes + 256u + (uint32_t)(x * 2 * AT_HD + 32 * h);
-        uint32_t ov[64];
-        tmem_ld32_raw(tO, ov);
-        tmem_ld32_raw(tO + 64, ov + 32);
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-        mbar_arrive(&o_free[x]);  // O_x may take the next item's PV
+      if (!warp_wait(&o_done[x], o_seen & 1, err)) break;  // the item's last PV_x
+      ++o_seen;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      uint32_t ov[128];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) + __uint_as_float(ov[32 + e]));
-        const int qt = x ? item.qt[1] : item.qt[0], head = x ? item.head[1] : item.head[0];
-        const int qr = qt * AT_BM + r;
-        const int row0 = qt * AT_BM + quarter * 32;  // the pair's first query row
-        // all 32 rows of the pair belong to the request: the hi and lo planes
-        // leave as two 32-row x 64-column TMA boxes, staged in the pair's
-        // 8 KB buffer with the 128-byte swizzle (16-byte chunk k of row r at
-        // r * 128 + ((k ^ (r & 7)) << 4)), each half writing its 4 chunks
-        const bool boxed = o_tma && row0 + 32 <= T;
-        uint8_t *stg = sm + AT_STG + quarter * 8192;
-        xch[h * 128 + r] = l[x];
-        if (boxed && h == 0 && lane == 0) bulk_wait_read_all();  // the pair's previous boxes have left stg
-        pair_bar(bar_id);
-        const float inv = 1.0f / (xch[r] + xch[128 + r]);  // the row sum, halves added in a fixed order
-        if (boxed) {
-          uint8_t *srow = stg + lane * 128;
+      for (int q = 0; q < 4; ++q) tmem_ld32_raw(tO + 32 * q, ov + 32 * q);
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      mbar_arrive(&o_free[x]);  // O_x may take the next item's PV
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
+      for (int e = 0; e < 64; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) + __uint_as_float(ov[64 + e]));
+      const int qt = x ? item.qt[1] : item.qt[0], head = x ? item.head[1] : item.head[0];
+      const int qr = qt * AT_BM + r;
+      const int row0 = qt * AT_BM + quarter * 32;  // the warp's first query row
+      if (o_tma && row0 + 32 <= T) {
+        // all 32 rows of the warp belong to the request: the hi and lo
+        // planes leave as two 32-row x 64-column TMA boxes, staged in the
+        // warp's 4 KB buffer with the 128-byte swizzle (16-byte chunk j of
+        // row r at r * 128 + ((j ^ (r & 7)) << 4))
+        const float inv = 1.0f / l;
+        uint8_t *stg = sm + AT_STG + (warp - 4) * 4096, *srow = stg + lane * 128;
+#pragma unroll
+        for (int part = 0; part < 2; ++part) {
+          if (lane == 0) bulk_wait_read_all();  // the warp's previous box has left stg
+          __syncwarp();
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
             uint32_t hw[4], lw[4];
 #pragma unroll
             for (int q = 0; q < 4; ++q)
               split2(__uint_as_float(ov[8 * e + 2 * q]) * inv, __uint_as_float(ov[8 * e + 2 * q + 1]) * inv, hw[q],
                      lw[q]);
-            const int k = ((4 * h + e) ^ (lane & 7)) << 4;
-            *reinterpret_cast<uint4 *>(srow + k) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-            *reinterpret_cast<uint4 *>(srow + 4096 + k) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+            *reinterpret_cast<uint4 *>(srow + ((e ^ (lane & 7)) << 4)) =
+                part ? make_uint4(lw[0], lw[1], lw[2], lw[3]) : make_uint4(hw[0], hw[1], hw[2], hw[3]);
           }
           fence_async_smem();
-          pair_bar(bar_id);
-          if (h == 0 && lane == 0) {
-            tma_store_2d(&tmOh, stg, head * AT_HD, (int)off + row0);
-            tma_store_2d(&tmOl, stg + 4096, head * AT_HD, (int)off + row0);
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(part ? &tmOl : &tmOh, stg, head * AT_HD, (int)off + row0);
             bulk_commit();
           }
-        } else if (qr < T) {
-          if (out_hi) {  // bf16 hi/lo planes of the O projection's input
-            const int64_t base = (off + qr) * (int64_t)ldp + head * AT_HD + 32 * h;
-            uint4 *dh = reinterpret_cast<uint4 *>(out_hi + base), *dl = reinterpret_cast<uint4 *>(out_lo + base);
+        }
+      } else if (qr < T) {
+        const float inv = 1.0f / l;
+        if (out_hi) {  // bf16 hi/lo planes of the O projection's input
+          const int64_t base = (off + qr) * (int64_t)ldp + head * AT_HD;
+          uint4 *dh = reinterpret_cast<uint4 *>(out_hi + base), *dl = reinterpret_cast<uint4 *>(out_lo + base);
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              uint32_t hw[4], lw[4];
+          for (int e = 0; e < 8; ++e) {
+            uint32_t hw[4], lw[4];
 #pragma unroll
-              for (int q = 0; q < 4; ++q)
-                split2(__uint_as_float(ov[8 * e + 2 * q]) * inv, __uint_as_float(ov[8 * e + 2 * q + 1]) * inv,
-                       hw[q], lw[q]);
-              dh[e] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-              dl[e] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-            }
-          } else {
-            float4 *dst =
-                reinterpret_cast<float4 *>(out + (off + qr) * (int64_t)(a.H * AT_HD) + head * AT_HD + 32 * h);
-#pragma unroll
-            for (int e = 0; e < 8; ++e)
-              dst[e] = make_float4(__uint_as_float(ov[4 * e]) * inv, __uint_as_float(ov[4 * e + 1]) * inv,
-                                   __uint_as_float(ov[4 * e + 2]) * inv, __uint_as_float(ov[4 * e + 3]) * inv);
+            for (int q = 0; q < 4; ++q)
+              split2(__uint_as_float(ov[8 * e + 2 * q]) * inv, __uint_as_float(ov[8 * e + 2 * q + 1]) * inv, hw[q],
+                     lw[q]);
+            dh[e] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            dl[e] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
           }
+        } else {
+          float4 *dst = reinterpret_cast<float4 *>(out + (off + qr) * (int64_t)(a.H * AT_HD) + head * AT_HD);
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            dst[e] = make_float4(__uint_as_float(ov[4 * e]) * inv, __uint_as_float(ov[4 * e + 1]) * inv,
+                                 __uint_as_float(ov[4 * e + 2]) * inv, __uint_as_float(ov[4 * e + 3]) * inv);
         }
       }
     }

@@ -1369,7 +1369,13 @@ cudaError_t tc_matmul(const TcPlanes &A, int M, const TcPlanes &B, int N, const 
   const auto *bh = reinterpret_cast<const CUtensorMap *>(B.hi), *bl = reinterpret_cast<const CUtensorMap *>(B.lo);
   const int tiles256 = num_m * ((N + 255) / 256);
   const int tiles_pair = ((M + 255) / 256) * ((N + 255) / 256);
-  if (tiles_pair >= sms && pair_regs == TC_REG_LAUNCH) {  // at least two 256 x 256 tiles per CTA pair
+  // Rounds of the grid: a CTA pair's 256 x 256 tile is twice the MMA work
+  // per CTA of a 128 x 128 tile at the same operand bytes per CTA and
+  // k-block, so a pair round takes about 1.5 single-CTA rounds.
+  const int rounds1 = (num_m * ((N + 127) / 128) + sms - 1) / sms;
+  const int rounds_pair = (tiles_pair + sms / 2 - 1) / (sms / 2);
+  const bool pair_wins = tiles_pair >= sms || 3 * rounds_pair < 2 * rounds1;
+  if (pair_wins && pair_regs == TC_REG_LAUNCH) {
     const int npairs = tiles_pair < sms / 2 ? tiles_pair : sms / 2;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * npairs);

@@ -367,13 +367,46 @@ __global__ void __launch_bounds__(256) gemv_kernel(const float *__restrict__ x, 
 // weights); x is read, and y written, after it.  Requires N % 16 == 0 and
 // 16-byte aligned weights and scales.
 // q * 2^s of the nibble (XORed with 8) at bit s of w, exactly: bias = 2^23 + 8 * 2^s.
-__device__ __forceinline__ float q4_at(uint32_t w, uint32_t mask, float bias) {
-  return __uint_as_float((w & mask) | 0x4B000000u) - bias;
+// Nibble under `mask` (bits 0-15) of w as an exact float.  The reference
+// packs two's-complement nibbles; XOR 8 makes them offset binary q + 8, and
+// OR 0x4B000000 places that in a float's mantissa: 2^23 + (q + 8) * 2^s for
+// the nibble at bit s.  The magic bits and the mask are disjoint, so both
+// steps are one XOR with g = (0x88888888 & mask) | 0x4B000000: a single
+// LOP3 when g sits in a register (a kernel argument, not an immediate,
+// since the mask already takes the instruction's one immediate).
+// Subtracting `bias` = 2^23 + 8 * 2^s leaves q * 2^s exactly.
+__device__ __forceinline__ float q4_at(uint32_t w, uint32_t mask, uint32_t g, float bias) {
+  return __uint_as_float((w & mask) ^ g) - bias;
+}
+
+// One 16-byte pair-row load of a thread (pair row p of its 16 columns) into
+// the per-group sums of one row of x: lo * x0 + hi * x1 per column, with x
+// pre-scaled per nibble position (x0, x0 / 256, x1 / 16, x1 / 4096), on
+// packed f32 pairs: in2[2 * wq + h] holds columns 4wq + 2h, 4wq + 2h + 1 of
+// 32-bit word wq.  Per lane the subtract and the two FMAs round as the
+// scalar form would.
+__device__ __forceinline__ void q4_row1x2(const uint4 cw, const float4 xv, uint64_t (&in2)[8], const uint4 gq) {
+  const uint64_t XL = f2pack(xv.x, xv.y), XH = f2pack(xv.z, xv.w);
+  const uint64_t BL = f2pack(8388616.0f, 8390656.0f), BH = f2pack(8388736.0f, 8421376.0f);
+  const uint32_t wds[4] = {cw.x, cw.y, cw.z, cw.w};
+#pragma unroll
+  for (int wq = 0; wq < 4; ++wq) {
+    const uint32_t wl = wds[wq], wu = wds[wq] >> 16;
+    const uint64_t lo01 = fsub2(f2pack(__uint_as_float((wl & 0xFu) ^ gq.x), __uint_as_float((wl & 0xF00u) ^ gq.z)), BL);
+    const uint64_t lo23 = fsub2(f2pack(__uint_as_float((wu & 0xFu) ^ gq.x), __uint_as_float((wu & 0xF00u) ^ gq.z)), BL);
+    const uint64_t hi01 =
+        fsub2(f2pack(__uint_as_float((wl & 0xF0u) ^ gq.y), __uint_as_float((wl & 0xF000u) ^ gq.w)), BH);
+    const uint64_t hi23 =
+        fsub2(f2pack(__uint_as_float((wu & 0xF0u) ^ gq.y), __uint_as_float((wu & 0xF000u) ^ gq.w)), BH);
+    in2[2 * wq] = ffma2(hi01, XH, ffma2(lo01, XL, in2[2 * wq]));
+    in2[2 * wq + 1] = ffma2(hi23, XH, ffma2(lo23, XL, in2[2 * wq + 1]));
+  }
 }
 
 template <int MR, int CX>
 __global__ void __launch_bounds__(256, MR <= 2 ? 2 : 1) gemv_q4_kernel(const float *__restrict__ x, int64_t ldx,
-                                                                        int M, int K, Int4Weight W, EpiCtx e) {
+                                                                        int M, int K, Int4Weight W, EpiCtx e,
+                                                                        uint4 gq) {
   constexpr int KS = 256 / CX;  // pair-row slices per CTA
   constexpr int NC = 16 * CX;   // columns per CTA
   constexpr int D = 8;          // pair rows in flight per thread (shared-memory ring)
@@ -456,8 +489,41 @@ __global__ void __launch_bounds__(256, MR <= 2 ? 2 : 1) gemv_q4_kernel(const flo
   };
 
   int slot = 0, gend = (g + 1) * gp;
+  bool fast = false;
+  if constexpr (kGroupSums) fast = gp == 16 && (p_beg & 15) == 0 && ((p_end - p_beg) & 15) == 0;
+  if constexpr (kGroupSums) {
+    // One row, whole 16-pair-row scale groups: a group per iteration, its
+    // rows unrolled, so ring slots and waits are constants and the scale
+    // switch falls on the iteration boundary.
+    const uint8_t *src = wcol + (int64_t)(p_beg + D - 1) * N;  // the next pair row to request
+    const int64_t stride = N;
+    for (int pg = p_beg; fast && pg < p_end; pg += 16) {
+      uint64_t in2[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) in2[j] = 0ull;
+#pragma unroll
+      for (int d = 0; d < 16; ++d) {
+        asm volatile("cp.async.wait_group %0;" ::"n"(D - 2) : "memory");  // row pg + d has landed
+        const uint4 cw = ring[(d & (D - 1)) * 256 + tid];
+        if (col_ok && pg + d + D - 1 < p_end)  // into the slot row pg + d - 1 left
+          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(ring0 + ((d + D - 1) & (D - 1)) * 4096u),
+                       "l"(src)
+                       : "memory");
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        src += stride;
+        q4_row1x2(cw, xq[pg + d], in2, gq);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) f2unpack(in2[j], inner[0][2 * j], inner[0][2 * j + 1]);
+      flush();
+      ++g;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) sc[j] = scn[j];
+      load_scales(g + 1, scn);
+    }
+  }
 #pragma unroll 2
-  for (int pi = p_beg; pi < p_end; ++pi) {
+  for (int pi = p_beg; !fast && pi < p_end; ++pi) {
     asm volatile("cp.async.wait_group %0;" ::"n"(D - 2) : "memory");  // row pi has landed
     const uint4 cw = ring[slot * 256 + tid];
     issue(pi + D - 1, slot == 0 ? D - 1 : slot - 1);  // into the slot row pi - 1 left
@@ -474,15 +540,15 @@ __global__ void __launch_bounds__(256, MR <= 2 ? 2 : 1) gemv_q4_kernel(const flo
       float4 xv[MR];
 #pragma unroll
       for (int m = 0; m < MR; ++m) xv[m] = xq[m * npairs + pi];
-      const uint32_t wd[4] = {cw.x ^ 0x88888888u, cw.y ^ 0x88888888u, cw.z ^ 0x88888888u, cw.w ^ 0x88888888u};
+      const uint32_t wd[4] = {cw.x, cw.y, cw.z, cw.w};
 #pragma unroll
       for (int wq = 0; wq < 4; ++wq) {
         const uint32_t wl = wd[wq], wu = wd[wq] >> 16;
         // columns 4wq .. 4wq+3: low nibbles at bits 0 / 8, high at 4 / 12 of each half-word
-        const float lo[4] = {q4_at(wl, 0xFu, 8388616.0f), q4_at(wl, 0xF00u, 8390656.0f), q4_at(wu, 0xFu, 8388616.0f),
-                             q4_at(wu, 0xF00u, 8390656.0f)};
-        const float hi[4] = {q4_at(wl, 0xF0u, 8388736.0f), q4_at(wl, 0xF000u, 8421376.0f),
-                             q4_at(wu, 0xF0u, 8388736.0f), q4_at(wu, 0xF000u, 8421376.0f)};
+        const float lo[4] = {q4_at(wl, 0xFu, gq.x, 8388616.0f), q4_at(wl, 0xF00u, gq.z, 8390656.0f),
+                             q4_at(wu, 0xFu, gq.x, 8388616.0f), q4_at(wu, 0xF00u, gq.z, 8390656.0f)};
+        const float hi[4] = {q4_at(wl, 0xF0u, gq.y, 8388736.0f), q4_at(wl, 0xF000u, gq.w, 8421376.0f),
+                             q4_at(wu, 0xF0u, gq.y, 8388736.0f), q4_at(wu, 0xF000u, gq.w, 8421376.0f)};
 #pragma unroll
         for (int m = 0; m < MR; ++m) {
           // x pre-scaled per nibble position: (x0, x0 / 256, x1 / 16, x1 / 4096)
@@ -565,7 +631,9 @@ cudaError_t launch_gemv_q4(const float *x, int64_t ldx, int M, const Int4Weight 
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, gemv_q4_kernel<MR, CX>, x, ldx, M, W.K, W, e);
+  // (0x88888888 & mask) | 0x4B000000 for the nibble masks 0xF, 0xF0, 0xF00, 0xF000
+  const uint4 gq = make_uint4(0x4B000008u, 0x4B000080u, 0x4B000800u, 0x4B008000u);
+  return cudaLaunchKernelEx(&cfg, gemv_q4_kernel<MR, CX>, x, ldx, M, W.K, W, e, gq);
 }
 
 // Column threads per CTA: 1024 columns a CTA for wide matrices (long runs of

@@ -799,6 +799,11 @@ inline double mm_flops(int M, const Lin &w) { return 2.0 * M * w.N * (double)w.K
 inline double mm_bytes(int M, const Lin &w) {
   return (double)w.G * w.gs / 2 * w.N + (double)w.G * w.N * 4 + 4.0 * M * w.K + 4.0 * M * w.N;
 }
+// The tensor-core path reads the weight's bf16 hi/lo planes (4 bytes per
+// element of [N][Kp]) and the activation's planes, not the INT4 codes.
+inline double mm_tc_bytes(int M, const Lin &w) {
+  return 4.0 * w.N * w.tc.Kp + 4.0 * M * w.tc.Kp + 4.0 * M * w.N;
+}
 }  // namespace
 
 bool Batch::mm(int cls, bool capture, const float *x, int64_t ldx, int M, const Lin &w, const MatmulOut &o,
@@ -840,7 +845,7 @@ bool Batch::mm_in(int cls, bool capture, const TcPlanes *planes, const float *x,
   MatmulOut os = o;
   os.splitk_ws = splitk_ws_;
   NDL_LK(tc_matmul(*planes, M, w.tc, w.N, os, m_->kerr, st_));
-  return tend(a, mm_flops(M, w), mm_bytes(M, w), err);
+  return tend(a, mm_flops(M, w), mm_tc_bytes(M, w), err);
 }
 
 bool Batch::prefill(std::string &err) {

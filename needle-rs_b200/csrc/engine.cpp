@@ -820,7 +820,7 @@ bool Batch::mm(int cls, bool capture, const float *x, int64_t ldx, int M, const 
     NDL_LK(tc_split_rows(x, ldx, M, w.K, ap->Kp, tc_hi_, tc_lo_, st_));
     NDL_LK(tc_matmul(*ap, M, w.tc, w.N, os, m_->kerr, st_));
   } else {
-    NDL_LK(int4_matmul(x, ldx, M, w.view(), o, st_));
+    NDL_LK(int4_matmul(x, ldx, M, w.view(), o, st_, pdl_on()));
   }
   return tend(a, mm_flops(M, w), mm_bytes(M, w), err);
 }
@@ -992,7 +992,6 @@ bool Batch::decode_step(std::string &err, bool capture, int att_rows) {
                               : nullptr;
     void *ahi = pal ? tc_hi_ : nullptr, *alo = pal ? tc_lo_ : nullptr;
     const int64_t aldp = pal ? pal->Kp : 0;
-    if (!norm(D.sa_norm, nullptr)) return false;
     const size_t coff = l * (size_t)B * cap_ * kvd;
     // tensor-core path: q/k norm, RoPE and the cache append run in the QKV
     // projection's epilogue
@@ -1013,7 +1012,13 @@ bool Batch::decode_step(std::string &err, bool capture, int att_rows) {
       o.vcache = self_v_ + coff;
       o.cache_cap = cap_;
     }
-    if (!mm_in(TIME_DECODE_MATMUL, capture, pd, xn_, d, B, D.sa_qkv, o, err)) return false;
+    // CUDA-core path: the matvec norms its input rows as it loads them
+    const bool sa_in = !pd && int4_matmul_norms_input(B, D.sa_qkv.view(), o);
+    if (sa_in)
+      o.in_norm = D.sa_norm;
+    else if (!norm(D.sa_norm, nullptr))
+      return false;
+    if (!mm_in(TIME_DECODE_MATMUL, capture, pd, sa_in ? x_ : xn_, d, B, D.sa_qkv, o, err)) return false;
     NDL_TK(TIME_SELF_ATTENTION, capture, decoder_self_attention(qkv_, pos_, D.sa_qn, D.sa_kn, m.rope_cos, m.rope_sin, self_k_ + coff,
                                   self_v_ + coff, cap_, B, att_, m.ad, st, ahi, alo, aldp, prep, att_rows));
     MatmulOut r;
@@ -1022,11 +1027,15 @@ bool Batch::decode_step(std::string &err, bool capture, int att_rows) {
     r.epi = EPI_RESID;
     r.gate = D.sa_gate;
     if (!mm_in(TIME_DECODE_MATMUL, capture, pal, att_, qd, B, D.sa_o, r, err)) return false;
-    if (!norm(D.ca_norm, nullptr)) return false;
     MatmulOut qo;
     qo.y = q_;
     qo.ldy = qd;
-    if (!mm_in(TIME_DECODE_MATMUL, capture, pd, xn_, d, B, D.ca_q, qo, err)) return false;
+    const bool ca_in = !pd && int4_matmul_norms_input(B, D.ca_q.view(), qo);
+    if (ca_in)
+      qo.in_norm = D.ca_norm;
+    else if (!norm(D.ca_norm, nullptr))
+      return false;
+    if (!mm_in(TIME_DECODE_MATMUL, capture, pd, ca_in ? x_ : xn_, d, B, D.ca_q, qo, err)) return false;
     const float *kp = kv_planes_ + (size_t)2 * l * ttot_ * kvd, *vp = kp + (size_t)ttot_ * kvd;
     cudaEvent_t ev;
     if (!tbegin(TIME_CROSS_ATTENTION, capture, ev, err)) return false;

@@ -452,12 +452,33 @@ __global__ void __launch_bounds__(256, MR <= 2 ? 2 : 1) gemv_q4_kernel(const flo
   load_scales(g + 1, scn);
 
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  // the rows' ZCRMSNorm folded into the load of x: warp m takes row m's sum
+  // of squares
+  __shared__ float rinv[8];
+  const float *nsc = e.o.in_norm;
+  if (nsc) {
+    const int warp = tid >> 5, lane = tid & 31;
+    if (warp < MR && warp < M) {
+      float ss = 0.0f;
+      for (int k = lane; k < K; k += 32) {
+        const float v = x[(int64_t)warp * ldx + k];
+        ss += v * v;
+      }
+      ss = warp_sum(ss);
+      if (lane == 0) rinv[warp] = 1.0f / sqrtf(ss / (float)K + 1e-6f);
+    }
+    __syncthreads();
+  }
   for (int i = tid; i < MR * npairs; i += 256) {
     const int m = i / npairs, p = i - m * npairs;
     float x0 = 0.0f, x1 = 0.0f;
     if (m < M) {
       if (2 * p < K) x0 = x[(int64_t)m * ldx + 2 * p];
       if (2 * p + 1 < K) x1 = x[(int64_t)m * ldx + 2 * p + 1];
+      if (nsc) {
+        if (2 * p < K) x0 = ((1.0f + __ldg(nsc + 2 * p)) * x0) * rinv[m];
+        if (2 * p + 1 < K) x1 = ((1.0f + __ldg(nsc + 2 * p + 1)) * x1) * rinv[m];
+      }
     }
     xq[i] = make_float4(x0, x0 * 0.00390625f, x1 * 0.0625f, x1 * 0.000244140625f);
   }
@@ -756,6 +777,7 @@ cudaError_t int4_matmul(const float *x, int64_t ldx, int M, const Int4Weight &W,
       (!o.col_block || (o.col_block % 64) || !o.vec || (o.kv_block && (o.kv_block % o.col_block))))
     return cudaErrorInvalidValue;
   if (o.epi == EPI_ACT && ((W.N & 1) || o.planes[0])) return cudaErrorInvalidValue;  // planes: tensor-core only
+  if (o.in_norm && !gemv_q4_fits(M, W, o)) return cudaErrorInvalidValue;  // input norm: the matvec only
   EpiCtx e{o, W.N};
   const int Kp = W.G * W.gs;
   if (gemv_q4_fits(M, W, o)) {
@@ -785,6 +807,8 @@ cudaError_t int4_matmul(const float *x, int64_t ldx, int M, const Int4Weight &W,
   tile_kernel<<<grid, 256, sm, stream>>>(x, ldx, M, W.K, W, e, xvec, yvec);
   return cudaGetLastError();
 }
+
+bool int4_matmul_norms_input(int M, const Int4Weight &W, const MatmulOut &o) { return gemv_q4_fits(M, W, o); }
 
 size_t int4_matmul_smem(int M, const Int4Weight &W, const MatmulOut &o) {
   if (M <= 0 || W.N <= 0 || W.G <= 0 || W.gs <= 0) return 0;

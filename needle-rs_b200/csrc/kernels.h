@@ -89,11 +89,18 @@ struct MatmulOut {
   // kernel's partial tiles, or NULL (no split).  Launches that share one
   // workspace must be ordered (one stream).
   float *splitk_ws = nullptr;
+  // CUDA-core matvec only (int4_matmul_norms_input): each row of x is first
+  // ZCRMSNorm'ed with this scale vector over its K columns (norm.rs:23-30:
+  // ((1 + s) * x) / sqrt(mean(x^2) + 1e-6)), as the kernel loads it.
+  const float *in_norm = nullptr;
 };
 
 // Y[M, N] (epilogue) X[M, K] @ W.  x row stride ldx (floats).
 cudaError_t int4_matmul(const float *x, int64_t ldx, int M, const Int4Weight &W, const MatmulOut &o,
                         cudaStream_t stream, bool pdl = false);
+// Whether int4_matmul takes MatmulOut::in_norm for these arguments (the
+// CUDA-core matvec, up to 8 rows); elsewhere it refuses it.
+bool int4_matmul_norms_input(int M, const Int4Weight &W, const MatmulOut &o);
 // Dynamic shared memory (bytes) int4_matmul requests for these arguments;
 // above kMaxDynSmem it refuses the call (cudaErrorInvalidValue).  Up to 8
 // rows it holds x: M * (K rounded up to the group) floats and more.
@@ -196,6 +203,8 @@ constexpr int kMaxDynSmem = 200 * 1024;
 // launch while on: each such kernel lets its successor's CTAs start during its
 // own tail and waits for its predecessor before touching global memory.
 void set_pdl(bool on);
+// Whether launches from this host thread use programmatic dependent launch.
+bool pdl_on();
 
 // Set per-device kernel attributes.  Call once per device, with it current.
 cudaError_t init_kernels();

@@ -1333,6 +1333,7 @@ cudaError_t tc_matmul(const TcPlanes &A, int M, const TcPlanes &B, int N, const 
     return cudaErrorInvalidValue;
   }
   if (o.epi == EPI_ACT && (N & 1)) return cudaErrorInvalidValue;
+  if (o.in_norm) return cudaErrorInvalidValue;  // input norm: CUDA-core matvec only
   TcEpi e{o, N};
   alignas(64) CUtensorMap ymap;
   std::memset(&ymap, 0, sizeof(ymap));

@@ -23,6 +23,8 @@ namespace {
 // ── ZCRMSNorm rows (norm.rs:23-30) ─────────────────────────────────────────
 __global__ void rms_norm_kernel(const float *__restrict__ x, int64_t ldx, float *out, int64_t ldo,
                                 const float *__restrict__ scale, int rows, int d) {
+  pdl_trigger();
+  pdl_wait();
   int row = (int)(((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
   if (row >= rows) return;
   const float *xr = x + (int64_t)row * ldx;
@@ -875,8 +877,8 @@ cudaError_t rms_norm_rows(const float *x, int64_t ldx, float *out, int64_t ldo, 
   if (rows <= 0) return cudaSuccess;
   if (d == 512 && ((ldx | ldo) & 3)) return cudaErrorInvalidValue;
   int64_t threads = (int64_t)rows * 32;
-  rms_norm_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(x, ldx, out, ldo, scale, rows, d);
-  return cudaGetLastError();
+  return launch(rms_norm_kernel, dim3((unsigned)((threads + 255) / 256)), dim3(256), 0, st, x, ldx, out, ldo, scale,
+                rows, d);
 }
 
 cudaError_t head_norm_rows(float *x, int rows, int64_t ld, int heads, int HD, const float *scale, cudaStream_t st) {

@@ -100,7 +100,10 @@ __global__ void __launch_bounds__(256) head_gemv_kernel(const float *__restrict_
 // the embedding is exactly a bf16 (as the shipped checkpoints store it):
 // the same products as over the f32 copy, from half the bytes.  One warp
 // per 4 vocabulary rows; each lane loads CPL 16-byte chunks (8 values) of
-// every row, all of the warp's loads issued before the first is used.
+// every row, all of the warp's loads issued before the first is used.  Under
+// programmatic dependent launch the embedding loads (weights, written by no
+// kernel of the step) go out before the wait for the previous kernel; h,
+// the masks and the positions are read after it.
 template <int CPL>
 __global__ void __launch_bounds__(256) head_gemv_bf16_kernel(const float *__restrict__ h, int B,
                                                              const uint16_t *__restrict__ emb, int64_t ld, int V,
@@ -109,6 +112,7 @@ __global__ void __launch_bounds__(256) head_gemv_bf16_kernel(const float *__rest
   __shared__ unsigned long long best_s[8][HB_MAX];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int v0 = (blockIdx.x * 8 + warp) * H_ROWS_PER_WARP;
+  pdl_trigger();
   uint4 ev[H_ROWS_PER_WARP][CPL];
 #pragma unroll
   for (int r = 0; r < H_ROWS_PER_WARP; ++r)
@@ -116,6 +120,7 @@ __global__ void __launch_bounds__(256) head_gemv_bf16_kernel(const float *__rest
     for (int j = 0; j < CPL; ++j)
       ev[r][j] = v0 + r < V ? __ldg(reinterpret_cast<const uint4 *>(emb + (int64_t)(v0 + r) * ld) + lane + 32 * j)
                             : make_uint4(0u, 0u, 0u, 0u);
+  pdl_wait();
   for (int i = tid; i < B * d; i += 256) hs[i] = h[i];
   __syncthreads();
   unsigned long long best[HB_MAX];
@@ -342,11 +347,11 @@ cudaError_t head_argmax(const float *h, int B, const float *emb, int V, int d, c
     if (emb_bf16 && d % 256 == 0 && cpl >= 1 && cpl <= 4 && ld_bf16 % 8 == 0 && ((uintptr_t)emb_bf16 % 16) == 0) {
       const uint16_t *e = (const uint16_t *)emb_bf16;
       const dim3 grid((V + rows_per_cta - 1) / rows_per_cta);
-      if (cpl == 1) head_gemv_bf16_kernel<1><<<grid, 256, sm, st>>>(h, B, e, ld_bf16, V, d, io, keys);
-      if (cpl == 2) head_gemv_bf16_kernel<2><<<grid, 256, sm, st>>>(h, B, e, ld_bf16, V, d, io, keys);
-      if (cpl == 3) head_gemv_bf16_kernel<3><<<grid, 256, sm, st>>>(h, B, e, ld_bf16, V, d, io, keys);
-      if (cpl == 4) head_gemv_bf16_kernel<4><<<grid, 256, sm, st>>>(h, B, e, ld_bf16, V, d, io, keys);
-      return cudaGetLastError();
+      auto k = cpl == 1   ? head_gemv_bf16_kernel<1>
+               : cpl == 2 ? head_gemv_bf16_kernel<2>
+               : cpl == 3 ? head_gemv_bf16_kernel<3>
+                          : head_gemv_bf16_kernel<4>;
+      return launch(k, grid, dim3(256), sm, st, h, B, e, ld_bf16, V, d, io, keys);
     }
     head_gemv_kernel<<<(V + rows_per_cta - 1) / rows_per_cta, 256, sm, st>>>(h, B, emb, V, d, io, keys);
     return cudaGetLastError();

@@ -452,35 +452,65 @@ __global__ void __launch_bounds__(256, MR <= 2 ? 2 : 1) gemv_q4_kernel(const flo
   load_scales(g + 1, scn);
 
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  // the rows' ZCRMSNorm folded into the load of x: warp m takes row m's sum
-  // of squares
-  __shared__ float rinv[8];
+  // Stage x: row m goes to the 8 / MR warps m * WPR .. m * WPR + WPR - 1,
+  // whose threads take 16-byte chunks 4q..4q+3 for q = r, r + 32 WPR, ...
+  // (r the thread's rank in the group; a thread's loads are in flight
+  // together), or single elements when the rows are not 16-byte aligned.
+  // The rows' ZCRMSNorm folds in: the same pass sums the squares, and once
+  // the group's sum is in each thread rescales the pairs it wrote.
   const float *nsc = e.o.in_norm;
-  if (nsc) {
-    const int warp = tid >> 5, lane = tid & 31;
-    if (warp < MR && warp < M) {
-      float ss = 0.0f;
-      for (int k = lane; k < K; k += 32) {
-        const float v = x[(int64_t)warp * ldx + k];
-        ss += v * v;
+  {
+    constexpr int WPR = 8 / MR, GT = 32 * WPR;  // warps and threads per row
+    __shared__ float ssq[8];
+    const int warp = tid >> 5, lane = tid & 31, m = warp / WPR, r = tid - m * GT;
+    const bool vec = ((ldx & 3) == 0) && (((uintptr_t)x & 15) == 0) && (K & 3) == 0;
+    float4 *xr = xq + m * npairs;
+    const float *xm = x + (int64_t)m * ldx;
+    auto put = [&](float4 *dst, float x0, float x1) {
+      *dst = nsc ? make_float4(x0, 0.0f, x1, 0.0f)  // rescaled below
+                 : make_float4(x0, x0 * 0.00390625f, x1 * 0.0625f, x1 * 0.000244140625f);
+    };
+    float ss = 0.0f;
+    if (vec) {
+#pragma unroll 4
+      for (int q = r; 2 * q < npairs; q += GT) {
+        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (m < M && 4 * q < K) v = *reinterpret_cast<const float4 *>(xm + 4 * q);
+        ss += v.x * v.x;
+        ss += v.y * v.y;
+        ss += v.z * v.z;
+        ss += v.w * v.w;
+        put(xr + 2 * q, v.x, v.y);
+        put(xr + 2 * q + 1, v.z, v.w);
       }
+    } else {
+#pragma unroll 4
+      for (int p = r; p < npairs; p += GT) {
+        const float x0 = m < M && 2 * p < K ? xm[2 * p] : 0.0f, x1 = m < M && 2 * p + 1 < K ? xm[2 * p + 1] : 0.0f;
+        ss += x0 * x0;
+        ss += x1 * x1;
+        put(xr + p, x0, x1);
+      }
+    }
+    if (nsc) {
       ss = warp_sum(ss);
-      if (lane == 0) rinv[warp] = 1.0f / sqrtf(ss / (float)K + 1e-6f);
+      if (lane == 0) ssq[warp] = ss;
+      __syncthreads();
+      float tot = 0.0f;
+#pragma unroll
+      for (int w = 0; w < WPR; ++w) tot += ssq[m * WPR + w];
+      const float ri = 1.0f / sqrtf(tot / (float)K + 1e-6f);
+      // the pairs this thread wrote: 2q, 2q + 1 (chunks) or p (elements)
+      const int step = vec ? 2 * GT : GT, first = vec ? 2 * r : r, span = vec ? 2 : 1;
+      for (int p0 = first; p0 < npairs; p0 += step)
+        for (int p = p0; p < p0 + span; ++p) {
+          const float4 v = xr[p];
+          float x0 = 0.0f, x1 = 0.0f;
+          if (2 * p < K) x0 = ((1.0f + __ldg(nsc + 2 * p)) * v.x) * ri;
+          if (2 * p + 1 < K) x1 = ((1.0f + __ldg(nsc + 2 * p + 1)) * v.z) * ri;
+          xr[p] = make_float4(x0, x0 * 0.00390625f, x1 * 0.0625f, x1 * 0.000244140625f);
+        }
     }
-    __syncthreads();
-  }
-  for (int i = tid; i < MR * npairs; i += 256) {
-    const int m = i / npairs, p = i - m * npairs;
-    float x0 = 0.0f, x1 = 0.0f;
-    if (m < M) {
-      if (2 * p < K) x0 = x[(int64_t)m * ldx + 2 * p];
-      if (2 * p + 1 < K) x1 = x[(int64_t)m * ldx + 2 * p + 1];
-      if (nsc) {
-        if (2 * p < K) x0 = ((1.0f + __ldg(nsc + 2 * p)) * x0) * rinv[m];
-        if (2 * p + 1 < K) x1 = ((1.0f + __ldg(nsc + 2 * p + 1)) * x1) * rinv[m];
-      }
-    }
-    xq[i] = make_float4(x0, x0 * 0.00390625f, x1 * 0.0625f, x1 * 0.000244140625f);
   }
   __syncthreads();
 
@@ -593,23 +623,46 @@ __global__ void __launch_bounds__(256, MR <= 2 ? 2 : 1) gemv_q4_kernel(const flo
   // 32) by shuffles, then the R partial rows in shared memory in a fixed order.
   constexpr int R = CX >= 32 ? KS : 8;
   const int warp = tid >> 5, lane = tid & 31;
-  float (&a)[MR][16] = acc;
   if constexpr (CX < 32) {
+    // Transposed butterfly, row by row: at each level a lane keeps the half
+    // of a row's 16 values that its offset bit selects and adds its
+    // partner's copies of them.  The pairs and their order are the plain
+    // butterfly's, so the sums are the same bits, with 16 - 16 / 2^L
+    // shuffles a row instead of 16 L.
+    constexpr int L = CX == 2 ? 4 : CX == 4 ? 3 : CX == 8 ? 2 : 1, LEN = 16 >> L;
+    int base = 0;  // the lane ends with the sums of columns 16 tx + base .. + LEN - 1
 #pragma unroll
-    for (int off = CX; off < 32; off <<= 1)
+    for (int l = 0; l < L; ++l) {
+      const int off = CX << l, h = 8 >> l;
+      const bool up = lane & off;
 #pragma unroll
       for (int m = 0; m < MR; ++m)
 #pragma unroll
-        for (int j = 0; j < 16; ++j) a[m][j] += __shfl_xor_sync(0xffffffffu, a[m][j], off);
-  }
-  const int rslot = CX >= 32 ? ks : warp;
-  if (CX >= 32 || lane < CX) {
+        for (int i = 0; i < h; ++i) {
+          const float send = up ? acc[m][i] : acc[m][i + h], keep = up ? acc[m][i + h] : acc[m][i];
+          acc[m][i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        }
+      if (up) base += h;
+    }
+#pragma unroll
+    for (int m = 0; m < MR; ++m) {
+      float *dst = red + (warp * MR + m) * NC + 16 * tx + base;
+      if constexpr (LEN >= 4) {
+#pragma unroll
+        for (int i = 0; i < LEN; i += 4)
+          *reinterpret_cast<float4 *>(dst + i) = make_float4(acc[m][i], acc[m][i + 1], acc[m][i + 2], acc[m][i + 3]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < LEN; ++i) dst[i] = acc[m][i];
+      }
+    }
+  } else {
 #pragma unroll
     for (int m = 0; m < MR; ++m)
 #pragma unroll
       for (int j = 0; j < 16; j += 4)
-        *reinterpret_cast<float4 *>(red + (rslot * MR + m) * NC + 16 * tx + j) =
-            make_float4(a[m][j], a[m][j + 1], a[m][j + 2], a[m][j + 3]);
+        *reinterpret_cast<float4 *>(red + (ks * MR + m) * NC + 16 * tx + j) =
+            make_float4(acc[m][j], acc[m][j + 1], acc[m][j + 2], acc[m][j + 3]);
   }
   __syncthreads();
   for (int i = tid; i < M * (NC / 4); i += 256) {

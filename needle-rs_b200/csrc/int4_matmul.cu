@@ -519,6 +519,11 @@ __global__ void __launch_bounds__(256, MR <= 2 ? 2 : 1) gemv_q4_kernel(const flo
   // per pair row (fewer registers)
   constexpr bool kGroupSums = MR == 1;
   float acc[MR][16], inner[kGroupSums ? MR : 1][16];
+  uint64_t acc2[kGroupSums ? 1 : MR][8];  // more rows: packed column pairs
+#pragma unroll
+  for (int m = 0; m < (kGroupSums ? 1 : MR); ++m)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc2[m][j] = 0ull;
 #pragma unroll
   for (int m = 0; m < MR; ++m)
 #pragma unroll
@@ -573,7 +578,7 @@ __global__ void __launch_bounds__(256, MR <= 2 ? 2 : 1) gemv_q4_kernel(const flo
       load_scales(g + 1, scn);
     }
   }
-#pragma unroll 2
+#pragma unroll(kGroupSums ? 2 : 1)
   for (int pi = p_beg; !fast && pi < p_end; ++pi) {
     asm volatile("cp.async.wait_group %0;" ::"n"(D - 2) : "memory");  // row pi has landed
     const uint4 cw = ring[slot * 256 + tid];
@@ -596,25 +601,44 @@ __global__ void __launch_bounds__(256, MR <= 2 ? 2 : 1) gemv_q4_kernel(const flo
       for (int wq = 0; wq < 4; ++wq) {
         const uint32_t wl = wd[wq], wu = wd[wq] >> 16;
         // columns 4wq .. 4wq+3: low nibbles at bits 0 / 8, high at 4 / 12 of each half-word
-        const float lo[4] = {q4_at(wl, 0xFu, gq.x, 8388616.0f), q4_at(wl, 0xF00u, gq.z, 8390656.0f),
-                             q4_at(wu, 0xFu, gq.x, 8388616.0f), q4_at(wu, 0xF00u, gq.z, 8390656.0f)};
-        const float hi[4] = {q4_at(wl, 0xF0u, gq.y, 8388736.0f), q4_at(wl, 0xF000u, gq.w, 8421376.0f),
-                             q4_at(wu, 0xF0u, gq.y, 8388736.0f), q4_at(wu, 0xF000u, gq.w, 8421376.0f)};
-#pragma unroll
-        for (int m = 0; m < MR; ++m) {
+        if constexpr (kGroupSums) {
+          const float lo[4] = {q4_at(wl, 0xFu, gq.x, 8388616.0f), q4_at(wl, 0xF00u, gq.z, 8390656.0f),
+                               q4_at(wu, 0xFu, gq.x, 8388616.0f), q4_at(wu, 0xF00u, gq.z, 8390656.0f)};
+          const float hi[4] = {q4_at(wl, 0xF0u, gq.y, 8388736.0f), q4_at(wl, 0xF000u, gq.w, 8421376.0f),
+                               q4_at(wu, 0xF0u, gq.y, 8388736.0f), q4_at(wu, 0xF000u, gq.w, 8421376.0f)};
           // x pre-scaled per nibble position: (x0, x0 / 256, x1 / 16, x1 / 4096)
-          const float xl[4] = {xv[m].x, xv[m].y, xv[m].x, xv[m].y}, xh[4] = {xv[m].z, xv[m].w, xv[m].z, xv[m].w};
+          const float xl[4] = {xv[0].x, xv[0].y, xv[0].x, xv[0].y}, xh[4] = {xv[0].z, xv[0].w, xv[0].z, xv[0].w};
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            if constexpr (kGroupSums) {
-              inner[m][4 * wq + c] = fmaf(hi[c], xh[c], fmaf(lo[c], xl[c], inner[m][4 * wq + c]));
-            } else {  // (lo * x0 + hi * x1) * scale, as matvec_avx2 orders it
-              acc[m][4 * wq + c] = fmaf(fmaf(hi[c], xh[c], lo[c] * xl[c]), sc[4 * wq + c], acc[m][4 * wq + c]);
-            }
+          for (int c = 0; c < 4; ++c)
+            inner[0][4 * wq + c] = fmaf(hi[c], xh[c], fmaf(lo[c], xl[c], inner[0][4 * wq + c]));
+        } else {
+          // (lo * x0 + hi * x1) * scale per column, as matvec_avx2 orders it,
+          // on packed column pairs (each lane rounds as the scalar form)
+          const uint64_t BL = f2pack(8388616.0f, 8390656.0f), BH = f2pack(8388736.0f, 8421376.0f);
+          const uint64_t lo01 =
+              fsub2(f2pack(__uint_as_float((wl & 0xFu) ^ gq.x), __uint_as_float((wl & 0xF00u) ^ gq.z)), BL);
+          const uint64_t lo23 =
+              fsub2(f2pack(__uint_as_float((wu & 0xFu) ^ gq.x), __uint_as_float((wu & 0xF00u) ^ gq.z)), BL);
+          const uint64_t hi01 =
+              fsub2(f2pack(__uint_as_float((wl & 0xF0u) ^ gq.y), __uint_as_float((wl & 0xF000u) ^ gq.w)), BH);
+          const uint64_t hi23 =
+              fsub2(f2pack(__uint_as_float((wu & 0xF0u) ^ gq.y), __uint_as_float((wu & 0xF000u) ^ gq.w)), BH);
+          const uint64_t s01 = f2pack(sc[4 * wq], sc[4 * wq + 1]), s23 = f2pack(sc[4 * wq + 2], sc[4 * wq + 3]);
+#pragma unroll
+          for (int m = 0; m < MR; ++m) {
+            const uint64_t XL = f2pack(xv[m].x, xv[m].y), XH = f2pack(xv[m].z, xv[m].w);
+            acc2[m][2 * wq] = ffma2(ffma2(hi01, XH, fmul2(lo01, XL)), s01, acc2[m][2 * wq]);
+            acc2[m][2 * wq + 1] = ffma2(ffma2(hi23, XH, fmul2(lo23, XL)), s23, acc2[m][2 * wq + 1]);
           }
         }
       }
     }
+  }
+  if constexpr (!kGroupSums) {
+#pragma unroll
+    for (int m = 0; m < MR; ++m)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) f2unpack(acc2[m][j], acc[m][2 * j], acc[m][2 * j + 1]);
   }
   flush();
   asm volatile("cp.async.wait_group 0;" ::: "memory");
